@@ -1,0 +1,198 @@
+// Elementwise glue of the forward: GELU, residual add, Q scale, varlen RoPE,
+// the q|k|v split for the FP32 path, token positions and the embedding
+// gather with the per-sequence token-dropout rescale.
+#include "common.cuh"
+#include "epilogue.cuh"
+#include "kernels.cuh"
+
+namespace esmb200 {
+namespace {
+
+inline int grid_for(long work, int block) {
+  long g = (work + block - 1) / block;
+  if (g > 148L * 32) g = 148L * 32;
+  return static_cast<int>(g < 1 ? 1 : g);
+}
+
+__global__ void gelu_kernel(const float* __restrict__ x, float* __restrict__ out, long n) {
+  for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long>(gridDim.x) * blockDim.x)
+    out[i] = gelu_erf(x[i]);
+}
+
+__global__ void residual_kernel(float* __restrict__ y, const float* __restrict__ x, long n) {
+  for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long>(gridDim.x) * blockDim.x)
+    y[i] = __fadd_rn(y[i], x[i]);
+}
+
+__global__ void scale_kernel(float* __restrict__ x, long n, float s) {
+  for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long>(gridDim.x) * blockDim.x)
+    x[i] = __fmul_rn(x[i], s);
+}
+
+// Sequence index of token t: the last b with cu[b] <= t (cu has B+1 entries).
+__device__ __forceinline__ int seq_of(const int* cu, int B, int t) {
+  int lo = 0, hi = B;  // invariant: cu[lo] <= t < cu[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (__ldg(cu + mid) <= t) lo = mid;
+    else hi = mid;
+  }
+  return lo;
+}
+
+// rope.cpp:90-152 (AVX-512 form): in place on [T, H, dh]; one thread per
+// (token, head, i < dh/2).
+__global__ void rope_varlen_kernel(float* __restrict__ x, const float* __restrict__ cos_t,
+                                   const float* __restrict__ sin_t, const int* __restrict__ cu,
+                                   int B, int H, int dh) {
+  const int half = dh / 2;
+  const int T = __ldg(cu + B);
+  const long total = static_cast<long>(T) * H * half;
+  for (long w = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; w < total;
+       w += static_cast<long>(gridDim.x) * blockDim.x) {
+    const int i = static_cast<int>(w % half);
+    const long th = w / half;
+    const int t = static_cast<int>(th / H);
+    const int p = t - __ldg(cu + seq_of(cu, B, t));
+    float* xr = x + th * dh;
+    const float c = __ldg(cos_t + static_cast<long>(p) * dh + i);
+    const float s = __ldg(sin_t + static_cast<long>(p) * dh + i);
+    const float lo = xr[i], hi = xr[i + half];
+    xr[i] = __fmaf_rn(-hi, s, __fmul_rn(lo, c));
+    xr[i + half] = __fmaf_rn(hi, c, __fmul_rn(lo, s));
+  }
+}
+
+// qkv [T, 3d] -> q, k, v [T, d] with q *= q_scale then RoPE on q, k.
+__global__ void split_qkv_rope_kernel(const float* __restrict__ qkv, float* __restrict__ q,
+                                      float* __restrict__ k, float* __restrict__ v, int T, int d,
+                                      int H, int dh, const int* __restrict__ pos,
+                                      const float* __restrict__ cos_t,
+                                      const float* __restrict__ sin_t, float q_scale) {
+  const int half = dh / 2;
+  const long total = static_cast<long>(T) * H * half;
+  for (long w = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; w < total;
+       w += static_cast<long>(gridDim.x) * blockDim.x) {
+    const int i = static_cast<int>(w % half);
+    const long th = w / half;
+    const long t = th / H;
+    const int h = static_cast<int>(th - t * H);
+    const float* src = qkv + t * 3L * d + static_cast<long>(h) * dh;
+    const long o = t * d + static_cast<long>(h) * dh;
+    const int p = __ldg(pos + t);
+    const float c = __ldg(cos_t + static_cast<long>(p) * dh + i);
+    const float s = __ldg(sin_t + static_cast<long>(p) * dh + i);
+    // q: scale before RoPE (model.cpp:976-988)
+    float lo = __fmul_rn(src[i], q_scale), hi = __fmul_rn(src[i + half], q_scale);
+    q[o + i] = __fmaf_rn(-hi, s, __fmul_rn(lo, c));
+    q[o + i + half] = __fmaf_rn(hi, c, __fmul_rn(lo, s));
+    lo = src[d + i];
+    hi = src[d + i + half];
+    k[o + i] = __fmaf_rn(-hi, s, __fmul_rn(lo, c));
+    k[o + i + half] = __fmaf_rn(hi, c, __fmul_rn(lo, s));
+    v[o + i] = src[2 * d + i];
+    v[o + i + half] = src[2 * d + i + half];
+  }
+}
+
+__global__ void positions_kernel(const int* __restrict__ cu, int B, int* __restrict__ pos) {
+  const int b = blockIdx.x;
+  if (b >= B) return;
+  const int s0 = cu[b], s1 = cu[b + 1];
+  for (int t = s0 + threadIdx.x; t < s1; t += blockDim.x) pos[t] = t - s0;
+}
+
+// model.cpp:737-778 Embed: one block per sequence.  scale =
+// (1 - 0.15f*0.8f) / max(1 - masks_seen/real_tokens, 1e-12); mask-token and
+// pad rows are zero.
+__global__ void embed_kernel(const float* __restrict__ embed_w, int d, const int* __restrict__ ids,
+                             const int* __restrict__ masks, const int* __restrict__ cu, int B,
+                             int mask_id, float* __restrict__ out) {
+  __shared__ int s_counts[2];
+  const int b = blockIdx.x;
+  if (b >= B) return;
+  const int s0 = cu[b], s1 = cu[b + 1];
+  if (threadIdx.x == 0) {
+    s_counts[0] = 0;
+    s_counts[1] = 0;
+  }
+  __syncthreads();
+  int src = 0, obs = 0;
+  for (int t = s0 + threadIdx.x; t < s1; t += blockDim.x) {
+    if (masks == nullptr || masks[t] != 0) ++src;
+    if (ids[t] == mask_id) ++obs;
+  }
+  atomicAdd(&s_counts[0], src);
+  atomicAdd(&s_counts[1], obs);
+  __syncthreads();
+  const int src_len = s_counts[0], observed = s_counts[1];
+  const float ratio_train = __fmul_rn(0.15f, 0.8f);
+  const float obs_ratio =
+      src_len > 0 ? __fdiv_rn(static_cast<float>(observed), static_cast<float>(src_len)) : 0.0f;
+  const float denom = fmaxf(__fsub_rn(1.0f, obs_ratio), 1e-12f);
+  const float scale = __fdiv_rn(__fsub_rn(1.0f, ratio_train), denom);
+  const long n = static_cast<long>(s1 - s0) * d;
+  for (long w = threadIdx.x; w < n; w += blockDim.x) {
+    const int t = s0 + static_cast<int>(w / d);
+    const int c = static_cast<int>(w % d);
+    const int id = ids[t];
+    const bool zero = (id == mask_id) || (masks != nullptr && masks[t] == 0);
+    out[static_cast<long>(t) * d + c] = zero ? 0.0f : __fmul_rn(__ldg(embed_w + static_cast<long>(id) * d + c), scale);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_gelu(const float* x, float* out, long n, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  gelu_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, out, n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_residual_add(float* y, const float* x, long n, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  residual_kernel<<<grid_for(n, 256), 256, 0, s>>>(y, x, n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_scale(float* x, long n, float sc, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  scale_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, n, sc);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rope_varlen(float* x, const float* cos_t, const float* sin_t, const int* cu,
+                               int B, int H, int dh, cudaStream_t s) {
+  if (B <= 0) return cudaSuccess;
+  // T is read on the device from cu[B]; size the grid for a generous bound.
+  rope_varlen_kernel<<<148 * 8, 256, 0, s>>>(x, cos_t, sin_t, cu, B, H, dh);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_split_qkv_rope(const float* qkv, float* q, float* k, float* v, int T, int d,
+                                  int H, int dh, const int* pos, const float* cos_t,
+                                  const float* sin_t, float q_scale, cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  const long work = static_cast<long>(T) * H * (dh / 2);
+  split_qkv_rope_kernel<<<grid_for(work, 256), 256, 0, s>>>(qkv, q, k, v, T, d, H, dh, pos,
+                                                            cos_t, sin_t, q_scale);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_positions(const int* cu, int B, int* pos, cudaStream_t s) {
+  if (B <= 0) return cudaSuccess;
+  positions_kernel<<<B, 128, 0, s>>>(cu, B, pos);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_embed(const float* embed_w, int d, const int* ids, const int* masks,
+                         const int* cu, int B, int mask_id, float* out, cudaStream_t s) {
+  if (B <= 0) return cudaSuccess;
+  embed_kernel<<<B, 256, 0, s>>>(embed_w, d, ids, masks, cu, B, mask_id, out);
+  return cudaGetLastError();
+}
+
+}  // namespace esmb200

@@ -1,0 +1,90 @@
+// Row-run epilogue shared by the INT8 and FP32 GEMMs: takes NV finished fp32
+// values of one output row and applies store / residual add / GELU, with an
+// optional running absmax of what was stored.
+#pragma once
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace esmb200 {
+
+// gelu.cpp:30-35: x * 0.5 * (1 + erf(x / sqrt(2))), each step rounded.
+__device__ __forceinline__ float gelu_erf(float x) {
+  const float kInvSqrt2 = 0.70710678118654752440f;
+  return __fmul_rn(__fmul_rn(x, 0.5f), __fadd_rn(1.0f, erff(__fmul_rn(x, kInvSqrt2))));
+}
+
+// Applies kEpiStore / kEpiResidual / kEpiGelu to y[0..NV) = columns
+// [c0, c0+NV) of row m (columns >= N are skipped).  Returns max|stored|.
+template <int NV>
+__device__ __forceinline__ float epi_row_run(const EpiParams& e, long m, int c0, int N,
+                                             float (&y)[NV]) {
+  float mx = 0.0f;
+  float* row = e.C + m * e.ldc + c0;
+  const bool vec = (c0 + NV <= N) && ((e.ldc & 3) == 0) && ((c0 & 3) == 0) &&
+                   ((reinterpret_cast<uintptr_t>(e.C) & 15) == 0);
+  if (vec) {
+#pragma unroll
+    for (int j = 0; j < NV; j += 4) {
+      float4 o = make_float4(y[j], y[j + 1], y[j + 2], y[j + 3]);
+      if (e.kind == kEpiResidual) {
+        const float4 h = *reinterpret_cast<const float4*>(row + j);
+        o.x = __fadd_rn(h.x, o.x);
+        o.y = __fadd_rn(h.y, o.y);
+        o.z = __fadd_rn(h.z, o.z);
+        o.w = __fadd_rn(h.w, o.w);
+      } else if (e.kind == kEpiGelu) {
+        o.x = gelu_erf(o.x);
+        o.y = gelu_erf(o.y);
+        o.z = gelu_erf(o.z);
+        o.w = gelu_erf(o.w);
+      }
+      *reinterpret_cast<float4*>(row + j) = o;
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(o.x), fabsf(o.y)), fmaxf(fabsf(o.z), fabsf(o.w))));
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      if (c0 + j < N) {
+        float o = y[j];
+        if (e.kind == kEpiResidual) o = __fadd_rn(row[j], o);
+        else if (e.kind == kEpiGelu) o = gelu_erf(o);
+        row[j] = o;
+        mx = fmaxf(mx, fabsf(o));
+      }
+    }
+  }
+  return mx;
+}
+
+// kEpiQkvRope for one 64-wide head chunk of row m starting at output column
+// n_base (a multiple of 64): q|k|v split by n_base / d, Q scaled before RoPE
+// (model.cpp:976-988), rotate-half RoPE in the AVX-512 form of rope.cpp:109-113
+// (lo' = fma(-hi, s, lo*c), hi' = fma(hi, c, lo*s)).
+__device__ __forceinline__ void epi_qkv_rope_head(const EpiParams& e, long m, int n_base,
+                                                  float (&y)[64]) {
+  const int which = n_base / e.d;
+  const int col = n_base - which * e.d;
+  float* dst = (which == 0 ? e.q : (which == 1 ? e.k : e.v)) + m * e.d + col;
+  if (which == 0) {
+#pragma unroll
+    for (int j = 0; j < 64; ++j) y[j] = __fmul_rn(y[j], e.q_scale);
+  }
+  if (which <= 1) {
+    const int p = e.pos[m];
+    const float* c = e.cos_t + static_cast<long>(p) * 64;
+    const float* s = e.sin_t + static_cast<long>(p) * 64;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float lo = y[i], hi = y[i + 32];
+      const float ci = __ldg(c + i), si = __ldg(s + i);
+      y[i] = __fmaf_rn(-hi, si, __fmul_rn(lo, ci));
+      y[i + 32] = __fmaf_rn(hi, ci, __fmul_rn(lo, si));
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 64; j += 4)
+    *reinterpret_cast<float4*>(dst + j) = make_float4(y[j], y[j + 1], y[j + 2], y[j + 3]);
+}
+
+}  // namespace esmb200

@@ -1,0 +1,47 @@
+// Host-side context and error plumbing behind the C ABI (include/esm_b200.h).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+
+#include "esm_b200.h"
+
+struct esmcu_context {
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t stream = nullptr;
+  cudaStream_t own_stream = nullptr;
+  uint32_t* d_status = nullptr;  // device-side status word (timeouts)
+  // Scratch for the kernel-facade entry points (quantised activations,
+  // absmax, scales, padded weights).  Grows between calls, never shrinks.
+  void* scratch = nullptr;
+  size_t scratch_bytes = 0;
+};
+
+namespace esmb200 {
+
+// Thread-local last error message (esmcu_last_error).
+void set_error(const std::string& msg);
+int fail(int code, const std::string& msg);
+int cuda_fail(cudaError_t e, const char* what);
+
+// Makes ctx->device current on this thread.
+int use_device(esmcu_context* ctx);
+// Ensures the context scratch holds at least `bytes`; synchronises the
+// stream before re-allocating.
+int ensure_scratch(esmcu_context* ctx, size_t bytes);
+// Reads (and clears) the device status word after a stream synchronise.
+int check_device_status(esmcu_context* ctx);
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+}  // namespace esmb200
+
+#define ESMCU_CUDA(call)                                          \
+  do {                                                            \
+    cudaError_t e_ = (call);                                      \
+    if (e_ != cudaSuccess) return ::esmb200::cuda_fail(e_, #call); \
+  } while (0)

@@ -1,0 +1,831 @@
+// Device-resident ESM-2 model: one weight replica per device, the packed
+// varlen forward, the scheduled forward and the multi-device dispatcher.
+//
+// Mirrors the reference's model.cpp:
+//   ForwardPackedInto (model.cpp:1093-1255): embed -> N x TransformerBlock ->
+//     final LN -> LM head (dense, GELU, LN, tied decoder) -> packed logits.
+//   TransformerBlock (model.cpp:932-1066): pre-LN attention block and FFN
+//     block, INT8 Linears when the model is quantised, FP32 otherwise.
+//   ForwardScheduled (model.cpp:1298-1421): PlanBatches, pack each group,
+//     ForwardPacked, scatter outputs back to caller order.
+//
+// The W8A8 layer on the device (per-tensor activation scales):
+//   LN1(+absmax) -> quantise -> QKV GEMM (dequant, Q scale, RoPE fused in the
+//   epilogue) -> attention(+absmax) -> quantise -> out GEMM (+residual fused)
+//   -> LN2(+absmax) -> quantise -> fc1 GEMM (+GELU, +absmax fused) ->
+//   quantise -> fc2 GEMM (+residual fused).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../kernels.cuh"
+#include "context.h"
+#include "esm_b200.h"
+#include "scheduler.h"
+
+using namespace esmb200;
+
+namespace {
+
+struct DevLayer {
+  float *ln1_w = nullptr, *ln1_b = nullptr, *ln2_w = nullptr, *ln2_b = nullptr;
+  int8_t *wqkv = nullptr, *wo = nullptr, *w1 = nullptr, *w2 = nullptr;
+  float *sqkv = nullptr, *so = nullptr, *s1 = nullptr, *s2 = nullptr;
+  float *fqkv = nullptr, *fo = nullptr, *f1 = nullptr, *f2 = nullptr;
+  float *bqkv = nullptr, *bo = nullptr, *b1 = nullptr, *b2 = nullptr;
+  bool set = false;
+};
+
+// Byte offsets of the per-forward buffers inside the arena.
+struct Arena {
+  size_t ids, masks, cu, pos, hidden, ln, q8, ascale, q, k, v, attn, inter, qkv, logits, amax;
+  size_t total;
+};
+
+}  // namespace
+
+struct esmcu_model {
+  esmcu_context* ctx = nullptr;
+  esmcu_config cfg{};
+  long ldk_d = 0, ldk_ffn = 0;  // int8 row strides (multiples of 16)
+  std::vector<DevLayer> layers;
+  float *embed = nullptr, *final_ln_w = nullptr, *final_ln_b = nullptr;
+  float *lm_w = nullptr, *lm_b = nullptr, *lm_ln_w = nullptr, *lm_ln_b = nullptr,
+        *lm_bias = nullptr;
+  bool embed_set = false, head_set = false;
+  float *cos_t = nullptr, *sin_t = nullptr;
+  int rope_len = 0;
+  std::vector<void*> owned;
+  char* arena = nullptr;
+  size_t arena_bytes = 0;
+  // profiling
+  bool profiling = false;
+  using EventPair = std::pair<std::string, std::pair<cudaEvent_t, cudaEvent_t>>;
+  std::vector<EventPair> pending;  // recorded, not yet read
+  std::vector<std::pair<std::string, float>> prof;
+  int launches = 0;
+};
+
+namespace {
+
+#define TRY(x)                     \
+  do {                             \
+    int rc_ = (x);                 \
+    if (rc_ != ESMCU_OK) return rc_; \
+  } while (0)
+
+// Launch wrapper: checks the launch and counts it.
+#define LAUNCH(m, call)                                   \
+  do {                                                    \
+    cudaError_t e_ = (call);                              \
+    if (e_ != cudaSuccess) return cuda_fail(e_, #call);   \
+    ++(m)->launches;                                      \
+  } while (0)
+
+int upload(esmcu_model* m, void** dst, const void* src, size_t bytes) {
+  void* p = nullptr;
+  ESMCU_CUDA(cudaMalloc(&p, bytes == 0 ? 16 : bytes));
+  m->owned.push_back(p);
+  if (bytes) ESMCU_CUDA(cudaMemcpy(p, src, bytes, cudaMemcpyHostToDevice));
+  *dst = p;
+  return ESMCU_OK;
+}
+
+template <class T>
+int upload_vec(esmcu_model* m, T** dst, const T* src, size_t count, const char* name) {
+  if (src == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, std::string(name) + " is null");
+  return upload(m, reinterpret_cast<void**>(dst), src, count * sizeof(T));
+}
+
+// Upload int8 [rows, K] (densely packed) into rows of stride ldk, zero-padded.
+int upload_i8_padded(esmcu_model* m, int8_t** dst, const int8_t* const* parts, const int* part_rows,
+                     int nparts, int K, long ldk) {
+  long rows = 0;
+  for (int i = 0; i < nparts; ++i) rows += part_rows[i];
+  std::vector<int8_t> host(static_cast<size_t>(rows * ldk), 0);
+  long r0 = 0;
+  for (int i = 0; i < nparts; ++i) {
+    if (parts[i] == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "int8 weight is null");
+    for (long r = 0; r < part_rows[i]; ++r)
+      std::memcpy(&host[static_cast<size_t>((r0 + r) * ldk)], parts[i] + r * K, static_cast<size_t>(K));
+    r0 += part_rows[i];
+  }
+  return upload(m, reinterpret_cast<void**>(dst), host.data(), host.size());
+}
+
+int upload_concat_f32(esmcu_model* m, float** dst, const float* const* parts, const size_t* counts,
+                      int nparts, const char* name) {
+  size_t total = 0;
+  for (int i = 0; i < nparts; ++i) total += counts[i];
+  std::vector<float> host(total);
+  size_t off = 0;
+  for (int i = 0; i < nparts; ++i) {
+    if (parts[i] == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, std::string(name) + " is null");
+    std::memcpy(host.data() + off, parts[i], counts[i] * sizeof(float));
+    off += counts[i];
+  }
+  return upload(m, reinterpret_cast<void**>(dst), host.data(), total * sizeof(float));
+}
+
+Arena plan_arena(const esmcu_model* m, int T, int B) {
+  const auto& c = m->cfg;
+  Arena a{};
+  size_t cur = 0;
+  auto take = [&](size_t bytes) {
+    const size_t off = cur;
+    cur = align_up(cur + std::max<size_t>(bytes, 16), 256);
+    return off;
+  };
+  const size_t Tz = static_cast<size_t>(T), d = static_cast<size_t>(c.hidden_size),
+               ffn = static_cast<size_t>(c.intermediate_size);
+  a.ids = take(Tz * 4);
+  a.masks = take(Tz * 4);
+  a.cu = take((static_cast<size_t>(B) + 1) * 4);
+  a.pos = take(Tz * 4);
+  a.hidden = take(Tz * d * 4);
+  a.ln = take(Tz * d * 4);
+  a.q8 = take(Tz * static_cast<size_t>(std::max(m->ldk_d, m->ldk_ffn)));
+  a.ascale = take(std::max<size_t>(Tz, 1) * 4);
+  a.q = take(Tz * d * 4);
+  a.k = take(Tz * d * 4);
+  a.v = take(Tz * d * 4);
+  a.attn = take(Tz * d * 4);
+  a.inter = take(Tz * ffn * 4);
+  a.qkv = take(Tz * 3 * d * 4);
+  a.logits = take(Tz * static_cast<size_t>(c.vocab_size) * 4);
+  a.amax = take(static_cast<size_t>(4 * c.num_layers + 8) * 4);
+  a.total = cur;
+  return a;
+}
+
+int ensure_arena(esmcu_model* m, size_t bytes) {
+  if (bytes <= m->arena_bytes) return ESMCU_OK;
+  ESMCU_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  if (m->arena) ESMCU_CUDA(cudaFree(m->arena));
+  m->arena = nullptr;
+  m->arena_bytes = 0;
+  const size_t want = align_up(bytes + bytes / 8, 1 << 21);
+  ESMCU_CUDA(cudaMalloc(&m->arena, want));
+  m->arena_bytes = want;
+  return ESMCU_OK;
+}
+
+int ensure_rope(esmcu_model* m, int max_len) {
+  if (max_len <= m->rope_len) return ESMCU_OK;
+  const int len = std::max(max_len, 1024);
+  const int dh = m->cfg.head_dim;
+  std::vector<float> c(static_cast<size_t>(len) * dh), s(static_cast<size_t>(len) * dh);
+  RopeBuildTables(len, dh, c.data(), s.data());
+  ESMCU_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  if (m->cos_t) ESMCU_CUDA(cudaFree(m->cos_t));
+  if (m->sin_t) ESMCU_CUDA(cudaFree(m->sin_t));
+  m->cos_t = m->sin_t = nullptr;
+  ESMCU_CUDA(cudaMalloc(&m->cos_t, c.size() * 4));
+  ESMCU_CUDA(cudaMalloc(&m->sin_t, s.size() * 4));
+  ESMCU_CUDA(cudaMemcpy(m->cos_t, c.data(), c.size() * 4, cudaMemcpyHostToDevice));
+  ESMCU_CUDA(cudaMemcpy(m->sin_t, s.data(), s.size() * 4, cudaMemcpyHostToDevice));
+  m->rope_len = len;
+  return ESMCU_OK;
+}
+
+// CUDA-event section timer, active only when profiling (names follow the
+// reference's ESM_PROFILE sections, model.cpp:948-1064).
+struct Sections {
+  esmcu_model* m;
+  std::vector<std::pair<std::string, std::pair<cudaEvent_t, cudaEvent_t>>> ev;
+  explicit Sections(esmcu_model* mm) : m(mm) {}
+  void begin(const char* name) {
+    if (!m->profiling) return;
+    cudaEvent_t a, b;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    cudaEventRecord(a, m->ctx->stream);
+    ev.push_back({name, {a, b}});
+  }
+  void end() {
+    if (!m->profiling || ev.empty()) return;
+    cudaEventRecord(ev.back().second.second, m->ctx->stream);
+  }
+};
+
+// Reads the section events of the forwards issued since the last read and
+// accumulates them per section name into m->prof (after a stream sync).
+void collect_profile(esmcu_model* m, bool reset) {
+  if (reset) m->prof.clear();
+  if (m->pending.empty()) return;
+  cudaStreamSynchronize(m->ctx->stream);
+  for (auto& e : m->pending) {
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, e.second.first, e.second.second);
+    auto it = std::find_if(m->prof.begin(), m->prof.end(),
+                           [&](const auto& p) { return p.first == e.first; });
+    if (it == m->prof.end()) m->prof.push_back({e.first, ms});
+    else it->second += ms;
+    cudaEventDestroy(e.second.first);
+    cudaEventDestroy(e.second.second);
+  }
+  m->pending.clear();
+}
+
+// Percentile of |x| exactly as ActivationObserver::Percentile indexes a
+// sorted sample (observer.cpp:33-51), over every value instead of a
+// 65536-entry reservoir.
+float host_percentile(const float* dev, size_t n, float pctile, cudaStream_t s) {
+  if (n == 0) return 0.0f;
+  std::vector<float> h(n);
+  cudaMemcpyAsync(h.data(), dev, n * 4, cudaMemcpyDeviceToHost, s);
+  cudaStreamSynchronize(s);
+  for (auto& v : h) v = std::fabs(v);
+  const float frac = std::clamp(pctile / 100.0f, 0.0f, 1.0f);
+  size_t idx = static_cast<size_t>(std::floor(frac * static_cast<float>(n - 1)));
+  if (idx >= n) idx = n - 1;
+  std::nth_element(h.begin(), h.begin() + static_cast<long>(idx), h.end());
+  return h[idx];
+}
+
+// The packed forward on device buffers already in the arena.  When stats
+// is non-null (calibration), writes the four per-layer site percentiles.
+int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk, float* logits,
+                   int T, int B, int max_len, float pctile, float* stats) {
+  const auto& c = m->cfg;
+  esmcu_context* ctx = m->ctx;
+  cudaStream_t s = ctx->stream;
+  char* base = m->arena;
+  auto F = [&](size_t off) { return reinterpret_cast<float*>(base + off); };
+  const int* cu = reinterpret_cast<const int*>(base + a.cu);
+  int* pos = reinterpret_cast<int*>(base + a.pos);
+  float* hidden = F(a.hidden);
+  float* ln = F(a.ln);
+  int8_t* q8 = reinterpret_cast<int8_t*>(base + a.q8);
+  float* ascale = F(a.ascale);
+  float *q = F(a.q), *k = F(a.k), *v = F(a.v), *attn = F(a.attn), *inter = F(a.inter);
+  float* qkv = F(a.qkv);
+  uint32_t* amax = reinterpret_cast<uint32_t*>(base + a.amax);
+  const int d = c.hidden_size, ffn = c.intermediate_size, H = c.num_heads, dh = c.head_dim;
+  const bool quant = c.weights_quantized != 0;
+  const bool per_token = c.act_quant == ESMCU_ACT_PER_TOKEN;
+  const float q_scale = 1.0f / std::sqrt(static_cast<float>(dh));  // model.cpp:978
+  const bool fused_rope = quant && dh == 64 && (d % 64) == 0;
+
+  Sections sec(m);
+
+  ESMCU_CUDA(cudaMemsetAsync(amax, 0, static_cast<size_t>(4 * c.num_layers + 8) * 4, s));
+  LAUNCH(m, launch_positions(cu, B, pos, s));
+  sec.begin("embed");
+  LAUNCH(m, launch_embed(m->embed, d, ids, mk, cu, B, c.mask_token_id, hidden, s));
+  sec.end();
+
+  // INT8 GEMM helper: A = quantised activations in q8 (row stride lda).
+  auto gemm_i8 = [&](const int8_t* W, long ldk, int N, const float* ws, const float* bias,
+                     EpiParams epi) -> int {
+    GemmI8Args g;
+    g.A = q8;
+    g.lda = ldk;
+    g.W = W;
+    g.ldw = ldk;
+    g.M = T;
+    g.N = N;
+    g.K = static_cast<int>(ldk);
+    g.w_scale = ws;
+    g.a_scale = ascale;
+    g.per_token = per_token ? 1 : 0;
+    g.bias = bias;
+    g.epi = epi;
+    g.status = ctx->d_status;
+    g.num_sms = ctx->num_sms;
+    LAUNCH(m, launch_gemm_i8(g, s));
+    return ESMCU_OK;
+  };
+  auto gemm_f32 = [&](const float* A, int K, const float* W, int N, const float* bias,
+                      EpiParams epi) -> int {
+    GemmF32Args g;
+    g.A = A;
+    g.lda = K;
+    g.W = W;
+    g.ldw = K;
+    g.M = T;
+    g.N = N;
+    g.K = K;
+    g.bias = bias;
+    g.epi = epi;
+    LAUNCH(m, launch_gemm_f32(g, s));
+    return ESMCU_OK;
+  };
+  // Quantise an fp32 activation [T, K] into q8 with row stride ldk.
+  auto quantize = [&](const float* x, int K, long ldk, uint32_t* am) -> int {
+    if (per_token) LAUNCH(m, launch_quantize_per_token(x, K, T, K, q8, ldk, ascale, s));
+    else LAUNCH(m, launch_quantize_per_tensor(x, K, T, K, am, q8, ldk, ascale, s));
+    return ESMCU_OK;
+  };
+  auto observe = [&](int layer, int site, const float* x, size_t n) {
+    if (stats) stats[layer * 4 + site] = host_percentile(x, n, pctile, s);
+  };
+  const size_t Td = static_cast<size_t>(T) * d;
+
+  for (int li = 0; li < c.num_layers; ++li) {
+    const DevLayer& L = m->layers[static_cast<size_t>(li)];
+    uint32_t* am = amax + 4 * li;
+    // ---- attention block
+    sec.begin("attn_ln");
+    if (quant && per_token) {
+      LAUNCH(m, launch_layernorm(hidden, L.ln1_w, L.ln1_b, c.layer_norm_eps, nullptr, T, d, nullptr,
+                                 q8, m->ldk_d, ascale, s));
+    } else {
+      LAUNCH(m, launch_layernorm(hidden, L.ln1_w, L.ln1_b, c.layer_norm_eps, ln, T, d,
+                                 quant ? am + 0 : nullptr, nullptr, 0, nullptr, s));
+    }
+    sec.end();
+    observe(li, 0, ln, Td);
+    if (quant && !per_token) {
+      sec.begin("quantize");
+      TRY(quantize(ln, d, m->ldk_d, am + 0));
+      sec.end();
+    }
+    sec.begin("qkv_proj");
+    if (quant) {
+      EpiParams e;
+      if (fused_rope) {
+        e.kind = kEpiQkvRope;
+        e.q = q;
+        e.k = k;
+        e.v = v;
+        e.d = d;
+        e.pos = pos;
+        e.cos_t = m->cos_t;
+        e.sin_t = m->sin_t;
+        e.q_scale = q_scale;
+      } else {
+        e.kind = kEpiStore;
+        e.C = qkv;
+        e.ldc = 3L * d;
+      }
+      TRY(gemm_i8(L.wqkv, m->ldk_d, 3 * d, L.sqkv, L.bqkv, e));
+    } else {
+      EpiParams e;
+      e.kind = kEpiStore;
+      e.C = qkv;
+      e.ldc = 3L * d;
+      TRY(gemm_f32(ln, d, L.fqkv, 3 * d, L.bqkv, e));
+    }
+    sec.end();
+    if (!fused_rope) {
+      sec.begin("q_scale_rope");
+      LAUNCH(m, launch_split_qkv_rope(qkv, q, k, v, T, d, H, dh, pos, m->cos_t, m->sin_t, q_scale, s));
+      sec.end();
+    }
+    sec.begin("attention");
+    LAUNCH(m, launch_attention_varlen(q, k, v, cu, B, H, dh, max_len, attn,
+                                      (quant && !per_token) ? am + 1 : nullptr, s));
+    sec.end();
+    observe(li, 1, attn, Td);
+    if (quant) {
+      sec.begin("quantize");
+      TRY(quantize(attn, d, m->ldk_d, am + 1));
+      sec.end();
+    }
+    sec.begin("attn_out_proj");
+    {
+      EpiParams e;
+      e.kind = kEpiResidual;  // hidden += out_proj(attn)  (model.cpp:1002-1015)
+      e.C = hidden;
+      e.ldc = d;
+      if (quant) {
+        TRY(gemm_i8(L.wo, m->ldk_d, d, L.so, L.bo, e));
+      } else {
+        TRY(gemm_f32(attn, d, L.fo, d, L.bo, e));
+      }
+    }
+    sec.end();
+    // ---- FFN block
+    sec.begin("ffn_ln");
+    if (quant && per_token) {
+      LAUNCH(m, launch_layernorm(hidden, L.ln2_w, L.ln2_b, c.layer_norm_eps, nullptr, T, d, nullptr,
+                                 q8, m->ldk_d, ascale, s));
+    } else {
+      LAUNCH(m, launch_layernorm(hidden, L.ln2_w, L.ln2_b, c.layer_norm_eps, ln, T, d,
+                                 quant ? am + 2 : nullptr, nullptr, 0, nullptr, s));
+    }
+    sec.end();
+    observe(li, 2, ln, Td);
+    if (quant && !per_token) {
+      sec.begin("quantize");
+      TRY(quantize(ln, d, m->ldk_d, am + 2));
+      sec.end();
+    }
+    sec.begin("fc1");
+    {
+      EpiParams e;
+      e.kind = kEpiGelu;  // fc1 -> GELU (model.cpp:1036-1046)
+      e.C = inter;
+      e.ldc = ffn;
+      if (quant) {
+        e.amax = per_token ? nullptr : am + 3;
+        TRY(gemm_i8(L.w1, m->ldk_d, ffn, L.s1, L.b1, e));
+      } else {
+        TRY(gemm_f32(ln, d, L.f1, ffn, L.b1, e));
+      }
+    }
+    sec.end();
+    observe(li, 3, inter, static_cast<size_t>(T) * ffn);
+    if (quant) {
+      sec.begin("quantize");
+      TRY(quantize(inter, ffn, m->ldk_ffn, am + 3));
+      sec.end();
+    }
+    sec.begin("fc2");
+    {
+      EpiParams e;
+      e.kind = kEpiResidual;  // hidden += fc2(inter_gelu) (model.cpp:1052-1065)
+      e.C = hidden;
+      e.ldc = d;
+      if (quant) {
+        TRY(gemm_i8(L.w2, m->ldk_ffn, d, L.s2, L.b2, e));
+      } else {
+        TRY(gemm_f32(inter, ffn, L.f2, d, L.b2, e));
+      }
+    }
+    sec.end();
+  }
+
+  // ---- final LN + LM head (model.cpp:1181-1239), FP32
+  sec.begin("final_ln");
+  LAUNCH(m, launch_layernorm(hidden, m->final_ln_w, m->final_ln_b, c.layer_norm_eps, ln, T, d,
+                             nullptr, nullptr, 0, nullptr, s));
+  sec.end();
+  sec.begin("lm_dense");
+  {
+    EpiParams e;
+    e.kind = kEpiGelu;  // dense -> GELU (model.cpp:1192-1223)
+    e.C = attn;
+    e.ldc = d;
+    TRY(gemm_f32(ln, d, m->lm_w, d, m->lm_b, e));
+  }
+  sec.end();
+  sec.begin("lm_ln");
+  LAUNCH(m, launch_layernorm(attn, m->lm_ln_w, m->lm_ln_b, c.layer_norm_eps, q, T, d, nullptr,
+                             nullptr, 0, nullptr, s));
+  sec.end();
+  sec.begin("lm_decoder");
+  {
+    EpiParams e;
+    e.kind = kEpiStore;  // tied decoder: lm_ln . embed^T + bias (model.cpp:1234-1239)
+    e.C = logits;
+    e.ldc = c.vocab_size;
+    TRY(gemm_f32(q, d, m->embed, c.vocab_size, m->lm_bias, e));
+  }
+  sec.end();
+  for (auto& e : sec.ev) m->pending.push_back(std::move(e));
+  return ESMCU_OK;
+}
+
+bool model_ready(esmcu_model* m) {
+  if (!m->embed_set || !m->head_set) return false;
+  for (auto& l : m->layers)
+    if (!l.set) return false;
+  return true;
+}
+
+// Validates a packed batch (host cu_seqlens) and prepares rope tables and the
+// arena; returns max_len through *max_len_out.
+int prepare(esmcu_model* m, int T, bool has_masks, const int32_t* cu, int B, Arena* a,
+            int* max_len_out) {
+  if (m == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "null model");
+  TRY(use_device(m->ctx));
+  if (!model_ready(m)) return fail(ESMCU_ERR_INVALID_ARGUMENT, "model weights are not fully set");
+  if (cu == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "cu_seqlens is null");
+  std::string msg = ValidateBatchView(T, has_masks ? T : 0, cu, B + 1, B);
+  if (!msg.empty()) return fail(ESMCU_ERR_INVALID_ARGUMENT, msg);
+  int max_len = 0;
+  for (int b = 0; b < B; ++b) max_len = std::max(max_len, cu[b + 1] - cu[b]);
+  TRY(ensure_rope(m, max_len));
+  *a = plan_arena(m, T, B);
+  TRY(ensure_arena(m, a->total));
+  *max_len_out = max_len;
+  return ESMCU_OK;
+}
+
+// Packed forward from host buffers; logits (host) [T, V].
+int forward_packed_host(esmcu_model* m, const int32_t* ids, const int32_t* masks, int T,
+                        const int32_t* cu, int B, float* logits, float pctile, float* stats) {
+  Arena a;
+  int max_len = 0;
+  TRY(prepare(m, T, masks != nullptr, cu, B, &a, &max_len));
+  if (T == 0) return ESMCU_OK;  // model.cpp:1105-1108
+  if (ids == nullptr || (logits == nullptr && stats == nullptr))
+    return fail(ESMCU_ERR_INVALID_ARGUMENT, "ids/logits is null");
+  for (int t = 0; t < T; ++t)
+    if (ids[t] < 0 || ids[t] >= m->cfg.vocab_size)
+      return fail(ESMCU_ERR_OUT_OF_RANGE, "token id " + std::to_string(ids[t]) + " out of range");
+  m->launches = 0;
+  cudaStream_t s = m->ctx->stream;
+  char* base = m->arena;
+  ESMCU_CUDA(cudaMemcpyAsync(base + a.ids, ids, static_cast<size_t>(T) * 4, cudaMemcpyHostToDevice, s));
+  if (masks)
+    ESMCU_CUDA(cudaMemcpyAsync(base + a.masks, masks, static_cast<size_t>(T) * 4, cudaMemcpyHostToDevice, s));
+  ESMCU_CUDA(cudaMemcpyAsync(base + a.cu, cu, static_cast<size_t>(B + 1) * 4, cudaMemcpyHostToDevice, s));
+  float* d_logits = reinterpret_cast<float*>(base + a.logits);
+  TRY(forward_device(m, a, reinterpret_cast<const int*>(base + a.ids),
+                     masks ? reinterpret_cast<const int*>(base + a.masks) : nullptr, d_logits, T, B,
+                     max_len, pctile, stats));
+  if (logits) {
+    ESMCU_CUDA(cudaMemcpyAsync(logits, d_logits, static_cast<size_t>(T) * m->cfg.vocab_size * 4,
+                               cudaMemcpyDeviceToHost, s));
+  }
+  ESMCU_CUDA(cudaStreamSynchronize(s));
+  if (m->profiling) collect_profile(m, true);
+  return check_device_status(m->ctx);
+}
+
+// One scheduled group: pack, forward, scatter into caller order.
+int run_group(esmcu_model* m, const std::vector<int>& group, const int32_t* ids_concat,
+              const std::vector<long>& offsets, const int32_t* lens, const int32_t* masks_concat,
+              float* logits) {
+  const int V = m->cfg.vocab_size;
+  std::vector<int32_t> ids, masks, cu(group.size() + 1, 0);
+  for (size_t gi = 0; gi < group.size(); ++gi) {
+    const int idx = group[gi];
+    ids.insert(ids.end(), ids_concat + offsets[static_cast<size_t>(idx)],
+               ids_concat + offsets[static_cast<size_t>(idx)] + lens[idx]);
+    if (masks_concat)
+      masks.insert(masks.end(), masks_concat + offsets[static_cast<size_t>(idx)],
+                   masks_concat + offsets[static_cast<size_t>(idx)] + lens[idx]);
+    cu[gi + 1] = cu[gi] + lens[idx];
+  }
+  const int T = cu.back();
+  std::vector<float> out(static_cast<size_t>(T) * V);
+  TRY(forward_packed_host(m, ids.data(), masks_concat ? masks.data() : nullptr, T, cu.data(),
+                          static_cast<int>(group.size()), out.data(), 0.0f, nullptr));
+  for (size_t gi = 0; gi < group.size(); ++gi) {
+    const int idx = group[gi];
+    std::memcpy(logits + offsets[static_cast<size_t>(idx)] * V, out.data() + static_cast<size_t>(cu[gi]) * V,
+                static_cast<size_t>(lens[idx]) * V * sizeof(float));
+  }
+  return ESMCU_OK;
+}
+
+int check_sched_args(const int32_t* ids_concat, const int32_t* lens, int n, float* logits) {
+  if (n < 0) return fail(ESMCU_ERR_INVALID_ARGUMENT, "n < 0");
+  if (n > 0 && (lens == nullptr || ids_concat == nullptr || logits == nullptr))
+    return fail(ESMCU_ERR_INVALID_ARGUMENT, "null ids/lens/logits");
+  for (int i = 0; i < n; ++i)
+    if (lens[i] < 0) return fail(ESMCU_ERR_INVALID_ARGUMENT, "negative sequence length");
+  return ESMCU_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int esmcu_model_create(esmcu_context* ctx, const esmcu_config* cfg, esmcu_model** out) {
+  if (out == nullptr || cfg == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "null argument");
+  *out = nullptr;
+  TRY(use_device(ctx));
+  const auto& c = *cfg;
+  if (c.num_layers <= 0 || c.hidden_size <= 0 || c.num_heads <= 0 || c.head_dim <= 0 ||
+      c.intermediate_size <= 0 || c.vocab_size <= 0)
+    return fail(ESMCU_ERR_INVALID_ARGUMENT, "config dimensions must be positive");
+  if (c.num_heads * c.head_dim != c.hidden_size)
+    return fail(ESMCU_ERR_SHAPE_MISMATCH, "num_heads * head_dim != hidden_size");
+  if (c.head_dim % 4 != 0 || c.head_dim > 128)
+    return fail(ESMCU_ERR_INVALID_ARGUMENT, "head_dim must be a multiple of 4 and <= 128");
+  if (c.act_quant != ESMCU_ACT_PER_TENSOR && c.act_quant != ESMCU_ACT_PER_TOKEN)
+    return fail(ESMCU_ERR_INVALID_ARGUMENT, "bad act_quant");
+  auto* m = new esmcu_model();
+  m->ctx = ctx;
+  m->cfg = c;
+  m->ldk_d = static_cast<long>(align_up(static_cast<size_t>(c.hidden_size), 16));
+  m->ldk_ffn = static_cast<long>(align_up(static_cast<size_t>(c.intermediate_size), 16));
+  m->layers.resize(static_cast<size_t>(c.num_layers));
+  const char* prof = std::getenv("ESM_PROFILE");
+  m->profiling = prof && *prof && std::string(prof) != "0";
+  *out = m;
+  return ESMCU_OK;
+}
+
+int esmcu_model_destroy(esmcu_model* m) {
+  if (m == nullptr) return ESMCU_OK;
+  cudaSetDevice(m->ctx->device);
+  cudaStreamSynchronize(m->ctx->stream);
+  for (void* p : m->owned) cudaFree(p);
+  if (m->arena) cudaFree(m->arena);
+  if (m->cos_t) cudaFree(m->cos_t);
+  if (m->sin_t) cudaFree(m->sin_t);
+  delete m;
+  return ESMCU_OK;
+}
+
+int esmcu_model_config(const esmcu_model* m, esmcu_config* out) {
+  if (m == nullptr || out == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "null argument");
+  *out = m->cfg;
+  return ESMCU_OK;
+}
+
+int esmcu_model_set_embeddings(esmcu_model* m, const float* embed) {
+  if (m == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "null model");
+  TRY(use_device(m->ctx));
+  TRY(upload_vec(m, &m->embed, embed,
+                 static_cast<size_t>(m->cfg.vocab_size) * m->cfg.hidden_size, "embed"));
+  m->embed_set = true;
+  return ESMCU_OK;
+}
+
+int esmcu_model_set_head(esmcu_model* m, const float* final_ln_w, const float* final_ln_b,
+                         const float* lm_dense_w, const float* lm_dense_b, const float* lm_ln_w,
+                         const float* lm_ln_b, const float* lm_decoder_bias) {
+  if (m == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "null model");
+  TRY(use_device(m->ctx));
+  const size_t d = static_cast<size_t>(m->cfg.hidden_size);
+  TRY(upload_vec(m, &m->final_ln_w, final_ln_w, d, "final_ln_w"));
+  TRY(upload_vec(m, &m->final_ln_b, final_ln_b, d, "final_ln_b"));
+  TRY(upload_vec(m, &m->lm_w, lm_dense_w, d * d, "lm_dense_w"));
+  TRY(upload_vec(m, &m->lm_b, lm_dense_b, d, "lm_dense_b"));
+  TRY(upload_vec(m, &m->lm_ln_w, lm_ln_w, d, "lm_ln_w"));
+  TRY(upload_vec(m, &m->lm_ln_b, lm_ln_b, d, "lm_ln_b"));
+  TRY(upload_vec(m, &m->lm_bias, lm_decoder_bias, static_cast<size_t>(m->cfg.vocab_size), "lm_bias"));
+  m->head_set = true;
+  return ESMCU_OK;
+}
+
+int esmcu_model_set_layer(esmcu_model* m, int layer, const esmcu_layer_weights* w) {
+  if (m == nullptr || w == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "null argument");
+  if (layer < 0 || layer >= m->cfg.num_layers)
+    return fail(ESMCU_ERR_OUT_OF_RANGE, "layer index out of range");
+  TRY(use_device(m->ctx));
+  DevLayer& L = m->layers[static_cast<size_t>(layer)];
+  const int d = m->cfg.hidden_size, ffn = m->cfg.intermediate_size;
+  const size_t dz = static_cast<size_t>(d), fz = static_cast<size_t>(ffn);
+  TRY(upload_vec(m, &L.ln1_w, w->attn_ln_w, dz, "attn_ln_w"));
+  TRY(upload_vec(m, &L.ln1_b, w->attn_ln_b, dz, "attn_ln_b"));
+  TRY(upload_vec(m, &L.ln2_w, w->ffn_ln_w, dz, "ffn_ln_w"));
+  TRY(upload_vec(m, &L.ln2_b, w->ffn_ln_b, dz, "ffn_ln_b"));
+  {
+    const float* parts[3] = {w->q_b, w->k_b, w->v_b};
+    const size_t counts[3] = {dz, dz, dz};
+    TRY(upload_concat_f32(m, &L.bqkv, parts, counts, 3, "q/k/v bias"));
+  }
+  TRY(upload_vec(m, &L.bo, w->out_b, dz, "out_b"));
+  TRY(upload_vec(m, &L.b1, w->fc1_b, fz, "fc1_b"));
+  TRY(upload_vec(m, &L.b2, w->fc2_b, dz, "fc2_b"));
+  if (m->cfg.weights_quantized) {
+    {
+      const int8_t* parts[3] = {w->q_wq, w->k_wq, w->v_wq};
+      const int rows[3] = {d, d, d};
+      TRY(upload_i8_padded(m, &L.wqkv, parts, rows, 3, d, m->ldk_d));
+      const float* sp[3] = {w->q_ws, w->k_ws, w->v_ws};
+      const size_t sc[3] = {dz, dz, dz};
+      TRY(upload_concat_f32(m, &L.sqkv, sp, sc, 3, "q/k/v scales"));
+    }
+    {
+      const int8_t* p[1] = {w->out_wq};
+      const int r[1] = {d};
+      TRY(upload_i8_padded(m, &L.wo, p, r, 1, d, m->ldk_d));
+      TRY(upload_vec(m, &L.so, w->out_ws, dz, "out scales"));
+    }
+    {
+      const int8_t* p[1] = {w->fc1_wq};
+      const int r[1] = {ffn};
+      TRY(upload_i8_padded(m, &L.w1, p, r, 1, d, m->ldk_d));
+      TRY(upload_vec(m, &L.s1, w->fc1_ws, fz, "fc1 scales"));
+    }
+    {
+      const int8_t* p[1] = {w->fc2_wq};
+      const int r[1] = {d};
+      TRY(upload_i8_padded(m, &L.w2, p, r, 1, ffn, m->ldk_ffn));
+      TRY(upload_vec(m, &L.s2, w->fc2_ws, dz, "fc2 scales"));
+    }
+  } else {
+    const float* parts[3] = {w->q_w, w->k_w, w->v_w};
+    const size_t counts[3] = {dz * dz, dz * dz, dz * dz};
+    TRY(upload_concat_f32(m, &L.fqkv, parts, counts, 3, "q/k/v weight"));
+    TRY(upload_vec(m, &L.fo, w->out_w, dz * dz, "out_w"));
+    TRY(upload_vec(m, &L.f1, w->fc1_w, fz * dz, "fc1_w"));
+    TRY(upload_vec(m, &L.f2, w->fc2_w, dz * fz, "fc2_w"));
+  }
+  L.set = true;
+  return ESMCU_OK;
+}
+
+int esmcu_model_forward_packed(esmcu_model* m, const int32_t* ids, const int32_t* masks, int T,
+                               const int32_t* cu, int B, float* logits) {
+  return forward_packed_host(m, ids, masks, T, cu, B, logits, 0.0f, nullptr);
+}
+
+int esmcu_model_forward_packed_device(esmcu_model* m, const int32_t* d_ids,
+                                      const int32_t* d_masks, int T, const int32_t* cu, int B,
+                                      float* d_logits) {
+  Arena a;
+  int max_len = 0;
+  TRY(prepare(m, T, d_masks != nullptr, cu, B, &a, &max_len));
+  if (T == 0) return ESMCU_OK;
+  if (d_ids == nullptr || d_logits == nullptr)
+    return fail(ESMCU_ERR_INVALID_ARGUMENT, "ids/logits is null");
+  m->launches = 0;
+  ESMCU_CUDA(cudaMemcpyAsync(m->arena + a.cu, cu, static_cast<size_t>(B + 1) * 4,
+                             cudaMemcpyHostToDevice, m->ctx->stream));
+  return forward_device(m, a, d_ids, d_masks, d_logits, T, B, max_len, 0.0f, nullptr);
+}
+
+int esmcu_model_observe_packed(esmcu_model* m, const int32_t* ids, int T, const int32_t* cu,
+                               int B, float pctile, float* stats_out) {
+  if (m == nullptr || stats_out == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "null argument");
+  if (m->cfg.weights_quantized)
+    return fail(ESMCU_ERR_INVALID_ARGUMENT, "calibration runs on the unquantised model");
+  return forward_packed_host(m, ids, nullptr, T, cu, B, nullptr, pctile, stats_out);
+}
+
+int esmcu_model_forward_scheduled(esmcu_model* m, const int32_t* ids_concat, const int32_t* lens,
+                                  const int32_t* masks_concat, int n, float threshold,
+                                  int max_batch, float* logits) {
+  if (m == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "null model");
+  TRY(check_sched_args(ids_concat, lens, n, logits));
+  if (n == 0) return ESMCU_OK;
+  std::vector<int> lengths(lens, lens + n);
+  std::vector<long> offsets(static_cast<size_t>(n) + 1, 0);
+  for (int i = 0; i < n; ++i) offsets[static_cast<size_t>(i) + 1] = offsets[static_cast<size_t>(i)] + lens[i];
+  auto plan = PlanBatches(lengths, threshold, max_batch);
+  for (const auto& g : plan) {
+    if (g.empty()) continue;
+    TRY(run_group(m, g, ids_concat, offsets, lens, masks_concat, logits));
+  }
+  return ESMCU_OK;
+}
+
+int esmcu_forward_scheduled_multi(esmcu_model** models, int n_models, const int32_t* ids_concat,
+                                  const int32_t* lens, const int32_t* masks_concat, int n,
+                                  float threshold, int max_batch, float* logits) {
+  if (models == nullptr || n_models <= 0) return fail(ESMCU_ERR_INVALID_ARGUMENT, "no models");
+  TRY(check_sched_args(ids_concat, lens, n, logits));
+  if (n == 0) return ESMCU_OK;
+  std::vector<int> lengths(lens, lens + n);
+  std::vector<long> offsets(static_cast<size_t>(n) + 1, 0);
+  for (int i = 0; i < n; ++i) offsets[static_cast<size_t>(i) + 1] = offsets[static_cast<size_t>(i)] + lens[i];
+  auto plan = PlanBatches(lengths, threshold, max_batch);
+  // Longest-processing-time assignment on sum_b(24 d^2 L_b + 4 d L_b^2).
+  const double d = models[0]->cfg.hidden_size;
+  std::vector<std::pair<double, int>> cost;
+  for (size_t g = 0; g < plan.size(); ++g) {
+    double c = 0.0;
+    for (int idx : plan[g]) {
+      const double L = lens[idx];
+      c += 24.0 * d * d * L + 4.0 * d * L * L;
+    }
+    cost.push_back({c, static_cast<int>(g)});
+  }
+  std::sort(cost.begin(), cost.end(), [](auto& a, auto& b) { return a.first > b.first; });
+  std::vector<double> load(static_cast<size_t>(n_models), 0.0);
+  std::vector<std::vector<int>> assign(static_cast<size_t>(n_models));
+  for (auto& cg : cost) {
+    const size_t best = static_cast<size_t>(std::min_element(load.begin(), load.end()) - load.begin());
+    load[best] += cg.first;
+    assign[best].push_back(cg.second);
+  }
+  std::vector<int> rc(static_cast<size_t>(n_models), ESMCU_OK);
+  std::vector<std::string> err(static_cast<size_t>(n_models));
+  std::vector<std::thread> threads;
+  for (int w = 0; w < n_models; ++w) {
+    threads.emplace_back([&, w]() {
+      for (int g : assign[static_cast<size_t>(w)]) {
+        int r = run_group(models[w], plan[static_cast<size_t>(g)], ids_concat, offsets, lens,
+                          masks_concat, logits);
+        if (r != ESMCU_OK) {
+          rc[static_cast<size_t>(w)] = r;
+          err[static_cast<size_t>(w)] = esmcu_last_error();
+          return;
+        }
+      }
+    });
+  }
+  for (auto& t : threads) t.join();
+  for (int w = 0; w < n_models; ++w)
+    if (rc[static_cast<size_t>(w)] != ESMCU_OK)
+      return fail(rc[static_cast<size_t>(w)], "device worker " + std::to_string(w) + ": " + err[static_cast<size_t>(w)]);
+  return ESMCU_OK;
+}
+
+int esmcu_model_set_profiling(esmcu_model* m, int enabled) {
+  if (m == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "null model");
+  collect_profile(m, true);
+  m->profiling = enabled != 0;
+  return ESMCU_OK;
+}
+
+int esmcu_model_profile(esmcu_model* m, const char** names, float* ms, int n) {
+  if (m == nullptr) return -1;
+  collect_profile(m, false);
+  int i = 0;
+  for (; i < n && i < static_cast<int>(m->prof.size()); ++i) {
+    names[i] = m->prof[static_cast<size_t>(i)].first.c_str();
+    ms[i] = m->prof[static_cast<size_t>(i)].second;
+  }
+  return i;
+}
+
+int esmcu_model_last_launch_count(const esmcu_model* m) { return m ? m->launches : 0; }
+
+}  // extern "C"

@@ -1,0 +1,118 @@
+// Internal launcher API of the sm_100a kernels.  The C-ABI layer (capi.cu)
+// and nothing else calls these; every pointer is a device pointer.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace esmb200 {
+
+// Epilogue applied to a finished fp32 output tile (after dequant for the
+// INT8 GEMM, after bias for the FP32 GEMM).
+enum EpiKind : int {
+  kEpiStore = 0,    // C[m,n] = y
+  kEpiResidual = 1, // C[m,n] = C[m,n] + y           (hidden += proj)
+  kEpiGelu = 2,     // C[m,n] = gelu(y)
+  kEpiQkvRope = 3,  // y -> q|k|v split, q *= q_scale, RoPE(q,k) at pos[m]
+};
+
+struct EpiParams {
+  int kind = kEpiStore;
+  float* C = nullptr;
+  long ldc = 0;
+  // When non-null, max|stored value| over the tensor is folded into *amax
+  // (float bits, atomicMax).  Feeds the next GEMM's per-tensor scale.
+  uint32_t* amax = nullptr;
+  // kEpiQkvRope: the output columns [0,d) | [d,2d) | [2d,3d) go to q | k | v,
+  // each [M, d] with row stride d; head_dim must be 64.
+  float* q = nullptr;
+  float* k = nullptr;
+  float* v = nullptr;
+  int d = 0;
+  const int* pos = nullptr;      // [M] position of each token in its sequence
+  const float* cos_t = nullptr;  // [max_len, 64]
+  const float* sin_t = nullptr;
+  float q_scale = 1.0f;
+};
+
+// ---------------------------------------------------------------- INT8 GEMM
+// C = epilogue( fma(float(A_q8 . W_q8^T), w_scale[n] * a_scale, bias[n]) )
+// A: [M, K] int8 row stride lda (bytes); W: [N, K] int8 row stride ldw.
+// K, lda, ldw must be multiples of 16 and the pointers 16-byte aligned.
+// a_scale: one float (per_token == 0) or M floats (per_token == 1).
+struct GemmI8Args {
+  const int8_t* A = nullptr;
+  long lda = 0;
+  const int8_t* W = nullptr;
+  long ldw = 0;
+  int M = 0, N = 0, K = 0;
+  const float* w_scale = nullptr;
+  const float* a_scale = nullptr;
+  int per_token = 0;
+  const float* bias = nullptr;
+  EpiParams epi;
+  uint32_t* status = nullptr;
+  int num_sms = 148;
+  // Debug/test: write the raw int32 accumulators [M, N] here instead of
+  // running the epilogue.
+  int32_t* acc_out = nullptr;
+};
+cudaError_t launch_gemm_i8(const GemmI8Args& a, cudaStream_t s);
+
+// ---------------------------------------------------------------- FP32 GEMM
+// C = epilogue( A[M,K] . W[N,K]^T + bias ), FP32 SIMT.
+struct GemmF32Args {
+  const float* A = nullptr;
+  long lda = 0;
+  const float* W = nullptr;
+  long ldw = 0;
+  int M = 0, N = 0, K = 0;
+  const float* bias = nullptr;
+  EpiParams epi;
+};
+cudaError_t launch_gemm_f32(const GemmF32Args& a, cudaStream_t s);
+
+// ------------------------------------------------------------ quantisation
+// Per-tensor: scale = amax>0 ? amax/127 : 1 (amax read from *amax_bits);
+// q = clamp(rne(x * (1/scale)), +-127); writes *scale_out; pads columns
+// [K, ldq) of each row with zeros.
+cudaError_t launch_quantize_per_tensor(const float* x, long ldx, int M, int K,
+                                       const uint32_t* amax_bits, int8_t* q, long ldq,
+                                       float* scale_out, cudaStream_t s);
+// Per-token: one scale per row computed from that row's absmax.
+cudaError_t launch_quantize_per_token(const float* x, long ldx, int M, int K, int8_t* q,
+                                      long ldq, float* row_scales, cudaStream_t s);
+cudaError_t launch_absmax(const float* x, long n, uint32_t* amax_bits, cudaStream_t s);
+
+// --------------------------------------------------------------- LayerNorm
+// out = LN(x) with the reference's rounding (double sums, float normalise).
+// Optional absmax of out into *amax.  When q != nullptr the row is also (or
+// only, if out == nullptr) quantised per token into q / row_scales.
+cudaError_t launch_layernorm(const float* x, const float* g, const float* b, float eps,
+                             float* out, int rows, int d, uint32_t* amax, int8_t* q,
+                             long ldq, float* row_scales, cudaStream_t s);
+
+// --------------------------------------------------------------- attention
+// Packed-varlen attention, q pre-scaled and RoPE'd; q,k,v,out [T, H, dh].
+// Optional absmax of out into *amax.
+cudaError_t launch_attention_varlen(const float* q, const float* k, const float* v,
+                                    const int* cu, int B, int H, int dh, int max_len,
+                                    float* out, uint32_t* amax, cudaStream_t s);
+
+// ------------------------------------------------------------- elementwise
+cudaError_t launch_gelu(const float* x, float* out, long n, cudaStream_t s);
+cudaError_t launch_residual_add(float* y, const float* x, long n, cudaStream_t s);
+cudaError_t launch_scale(float* x, long n, float scale, cudaStream_t s);
+cudaError_t launch_rope_varlen(float* x, const float* cos_t, const float* sin_t,
+                               const int* cu, int B, int H, int dh, cudaStream_t s);
+// qkv [T, 3d] -> q, k, v [T, d]; q *= q_scale; RoPE on q and k.
+cudaError_t launch_split_qkv_rope(const float* qkv, float* q, float* k, float* v, int T,
+                                  int d, int H, int dh, const int* pos, const float* cos_t,
+                                  const float* sin_t, float q_scale, cudaStream_t s);
+// Token -> position inside its sequence, from cu_seqlens.
+cudaError_t launch_positions(const int* cu, int B, int* pos, cudaStream_t s);
+// model.cpp:737-778 Embed.
+cudaError_t launch_embed(const float* embed_w, int d, const int* ids, const int* masks,
+                         const int* cu, int B, int mask_id, float* out, cudaStream_t s);
+
+}  // namespace esmb200

@@ -1,0 +1,127 @@
+// Activation quantisation for the W8A8 GEMMs.
+//
+// Per-tensor (the reference's semantics, gemm_int8.cpp:391-508): the scale
+// is max|A|/127 over the whole [M,K] operand (1 when the tensor is all
+// zero) and q = clamp(round_half_even(x * (1/scale)), -127, 127).  The
+// absmax is folded into *amax_bits by the kernel that produced A (LayerNorm,
+// attention, the fc1 GELU epilogue); this kernel only applies it.
+//
+// Per-token: the same formula with one scale per row (the reference's
+// QuantizeActivationSymmetricRef, pack.cpp:134-147, applied row by row).
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace esmb200 {
+namespace {
+
+__device__ __forceinline__ float act_scale_from_amax(float amax) {
+  return amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+}
+
+__device__ __forceinline__ int quant1(float x, float inv) {
+  int q = __float2int_rn(__fmul_rn(x, inv));
+  return max(-127, min(127, q));
+}
+
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+  return (static_cast<uint32_t>(a) & 0xffu) | ((static_cast<uint32_t>(b) & 0xffu) << 8) |
+         ((static_cast<uint32_t>(c) & 0xffu) << 16) | ((static_cast<uint32_t>(d) & 0xffu) << 24);
+}
+
+// Each thread writes 16 output bytes (one uint4) of one row.
+__global__ void quantize_per_tensor_kernel(const float* __restrict__ x, long ldx, int M, int K,
+                                           const uint32_t* __restrict__ amax_bits,
+                                           int8_t* __restrict__ q, long ldq,
+                                           float* __restrict__ scale_out) {
+  const float s = act_scale_from_amax(__uint_as_float(__ldg(amax_bits)));
+  const float inv = __fdiv_rn(1.0f, s);
+  if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = s;
+  const long groups_per_row = ldq / 16;
+  const long total = static_cast<long>(M) * groups_per_row;
+  const bool vec = ((ldx & 3) == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+  for (long g = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; g < total;
+       g += static_cast<long>(gridDim.x) * blockDim.x) {
+    const long m = g / groups_per_row;
+    const int c0 = static_cast<int>(g - m * groups_per_row) * 16;
+    const float* xr = x + m * ldx;
+    uint32_t w[4];
+    if (vec && c0 + 16 <= K) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(xr + c0 + 4 * i));
+        w[i] = pack4(quant1(v.x, inv), quant1(v.y, inv), quant1(v.z, inv), quant1(v.w, inv));
+      }
+    } else {
+      int qq[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) qq[i] = (c0 + i < K) ? quant1(xr[c0 + i], inv) : 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) w[i] = pack4(qq[4 * i], qq[4 * i + 1], qq[4 * i + 2], qq[4 * i + 3]);
+    }
+    *reinterpret_cast<uint4*>(q + m * ldq + c0) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+// One warp per row: absmax, scale, quantise.
+__global__ void quantize_per_token_kernel(const float* __restrict__ x, long ldx, int M, int K,
+                                          int8_t* __restrict__ q, long ldq,
+                                          float* __restrict__ row_scales) {
+  const int lane = threadIdx.x & 31;
+  const long m = (blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x) >> 5;
+  if (m >= M) return;
+  const float* xr = x + m * ldx;
+  float mx = 0.0f;
+  for (int c = lane; c < K; c += 32) mx = fmaxf(mx, fabsf(xr[c]));
+  mx = warp_max(mx);
+  const float s = act_scale_from_amax(mx);
+  const float inv = __fdiv_rn(1.0f, s);
+  if (lane == 0) row_scales[m] = s;
+  int8_t* qr = q + m * ldq;
+  for (int c = lane; c < ldq; c += 32) qr[c] = static_cast<int8_t>(c < K ? quant1(xr[c], inv) : 0);
+}
+
+__global__ void absmax_kernel(const float* __restrict__ x, long n, uint32_t* amax_bits) {
+  float mx = 0.0f;
+  for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long>(gridDim.x) * blockDim.x)
+    mx = fmaxf(mx, fabsf(x[i]));
+  mx = warp_max(mx);
+  if ((threadIdx.x & 31) == 0) atomicMax(amax_bits, __float_as_uint(mx));
+}
+
+int grid_for(long work, int block) {
+  long g = (work + block - 1) / block;
+  if (g > 148L * 16) g = 148L * 16;
+  return static_cast<int>(g < 1 ? 1 : g);
+}
+
+}  // namespace
+
+cudaError_t launch_quantize_per_tensor(const float* x, long ldx, int M, int K,
+                                       const uint32_t* amax_bits, int8_t* q, long ldq,
+                                       float* scale_out, cudaStream_t s) {
+  if (M <= 0) return cudaSuccess;
+  if ((ldq & 15) || ldq < K || (reinterpret_cast<uintptr_t>(q) & 15)) return cudaErrorInvalidValue;
+  const long work = static_cast<long>(M) * (ldq / 16);
+  quantize_per_tensor_kernel<<<grid_for(work, 256), 256, 0, s>>>(x, ldx, M, K, amax_bits, q,
+                                                                  ldq, scale_out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_per_token(const float* x, long ldx, int M, int K, int8_t* q,
+                                      long ldq, float* row_scales, cudaStream_t s) {
+  if (M <= 0) return cudaSuccess;
+  if (ldq < K) return cudaErrorInvalidValue;
+  const long threads = static_cast<long>(M) * 32;
+  quantize_per_token_kernel<<<static_cast<int>((threads + 255) / 256), 256, 0, s>>>(
+      x, ldx, M, K, q, ldq, row_scales);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_absmax(const float* x, long n, uint32_t* amax_bits, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  absmax_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, n, amax_bits);
+  return cudaGetLastError();
+}
+
+}  // namespace esmb200

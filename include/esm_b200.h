@@ -1,0 +1,222 @@
+/* esm_b200: B200-native (sm_100a) packed-varlen ESM-2 encoder forward,
+ * W8A8 SmoothQuant INT8 -- the C-ABI drop-in boundary.
+ *
+ * Two layers of entry points, both plain C (no C++ or torch types):
+ *
+ *  1. Kernel facade (device pointers, enqueued on the context's stream).
+ *     One function per function of the reference's kernel facade
+ *     include/esm_cpp/kernels.h, same argument order and meaning, plus a
+ *     context and an int status.  The reference's versions take host
+ *     pointers; these take device pointers, because the device-resident
+ *     forward never round-trips activations through the host.
+ *
+ *  2. Model (host buffers in, host buffers out).  Mirrors esm::Model's
+ *     ForwardPacked / ForwardScheduled (include/esm_cpp/model.h:136-159)
+ *     on a per-device weight replica; the host side keeps the reference's
+ *     BatchView validation and PlanBatches packing.
+ *
+ * Every function returns an esmcu_status; esmcu_last_error() gives the
+ * message of the calling thread's last failure.  No C++ exception crosses
+ * this boundary.  A context serves one host thread at a time, like
+ * esm::Model (model.h:179-181: one forward in flight per instance).
+ */
+#ifndef ESM_B200_H
+#define ESM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* The first seven values mirror esm::StatusCode (include/esm_cpp/status.h:9-17). */
+typedef enum {
+  ESMCU_OK = 0,
+  ESMCU_ERR_INVALID_ARGUMENT = 1,
+  ESMCU_ERR_OUT_OF_RANGE = 2,
+  ESMCU_ERR_NOT_FOUND = 3,
+  ESMCU_ERR_IO = 4,
+  ESMCU_ERR_SHAPE_MISMATCH = 5,
+  ESMCU_ERR_INTERNAL = 6,
+  ESMCU_ERR_CUDA = 7,    /* a CUDA runtime call failed */
+  ESMCU_ERR_TIMEOUT = 8, /* a device-side bounded wait ran out */
+  ESMCU_ERR_NO_DEVICE = 9
+} esmcu_status;
+
+/* Activation quantisation of the W8A8 GEMMs. */
+typedef enum {
+  /* Reference semantics: one dynamic scale max|A|/127 over the whole packed
+   * operand (gemm_int8.cpp:391-508).  Bit-exact int8/int32 parity mode. */
+  ESMCU_ACT_PER_TENSOR = 0,
+  /* One scale per token row (QuantizeActivationSymmetricRef per row,
+   * pack.cpp:134-147). */
+  ESMCU_ACT_PER_TOKEN = 1
+} esmcu_act_quant;
+
+typedef struct esmcu_context esmcu_context;
+typedef struct esmcu_model esmcu_model;
+
+const char* esmcu_last_error(void);
+const char* esmcu_version(void);
+int esmcu_device_count(int* count);
+
+/* ---- context ----------------------------------------------------------- */
+int esmcu_open(int device, esmcu_context** out);
+int esmcu_close(esmcu_context* ctx);
+/* Use an existing cudaStream_t (passed as void*); NULL = the context's own. */
+int esmcu_set_stream(esmcu_context* ctx, void* cuda_stream);
+void* esmcu_get_stream(esmcu_context* ctx);
+/* Waits for the stream and reports device-side failures (timeouts). */
+int esmcu_synchronize(esmcu_context* ctx);
+/* Device memory helpers for C callers without another allocator. */
+int esmcu_malloc(esmcu_context* ctx, size_t bytes, void** dptr);
+int esmcu_free(esmcu_context* ctx, void* dptr);
+int esmcu_memcpy_h2d(esmcu_context* ctx, void* dst, const void* src, size_t bytes);
+int esmcu_memcpy_d2h(esmcu_context* ctx, void* dst, const void* src, size_t bytes);
+
+/* ---- kernel facade (device pointers) ------------------------------------
+ * Each replaces the esm::kernels function named in its comment. */
+
+/* kernels.h:19-20 Linear: C[M,N] = A[M,K] . W[N,K]^T + bias (bias nullable). */
+int esmcu_linear(esmcu_context* ctx, const float* A, const float* W, const float* bias,
+                 float* C, int M, int N, int K);
+
+/* kernels.h:56-57 LinearInt8 (W8A8): W is QuantizedTensor::packed [N,K]
+ * int8 with per_channel_scales w_scales [N] (quant.h:17-23).  Activations are
+ * quantised on the device per esmcu_act_quant, accumulated in int32 and
+ * dequantised as fma(float(acc), w_scales[n]*a_scale, bias[n])
+ * (gemm_int8.cpp:109-126). */
+int esmcu_linear_int8(esmcu_context* ctx, const float* A, const int8_t* W,
+                      const float* w_scales, const float* bias, float* C, int M, int N, int K,
+                      int act_quant);
+
+/* The two halves of LinearInt8, exposed for the bit-exact parity gates.
+ * esmcu_quantize_activations: QuantizeActPrefixAvx512 (gemm_int8.cpp:391-508)
+ * in its symmetric s8 form q = clamp(rne(A*(1/s)), +-127), q_out [M, ldq]
+ * (ldq >= K, a multiple of 16; columns [K, ldq) are zeroed); scales_out gets
+ * 1 (per tensor) or M (per token) floats.
+ * esmcu_gemm_int8_s32: acc[M,N] = sum_k q[m,k]*W[n,k] in int32 on the
+ * tensor cores (K, ldq, ldw multiples of 16). */
+int esmcu_quantize_activations(esmcu_context* ctx, const float* A, int M, int K, int8_t* q_out,
+                               int ldq, float* scales_out, int act_quant);
+int esmcu_gemm_int8_s32(esmcu_context* ctx, const int8_t* q, int ldq, const int8_t* W, int ldw,
+                        int32_t* acc, int M, int N, int K);
+
+/* kernels.h:32-33 LayerNorm over rows of width d. */
+int esmcu_layernorm(esmcu_context* ctx, const float* x, const float* gamma, const float* beta,
+                    float eps, float* out, int num_rows, int d);
+/* kernels.h:35 Gelu (exact erf form). */
+int esmcu_gelu(esmcu_context* ctx, const float* x, float* out, size_t n);
+/* kernels.h:24 ResidualAddInplace: y += x. */
+int esmcu_residual_add_inplace(esmcu_context* ctx, float* y, const float* x, size_t n);
+/* kernels.h:29 ScaleInplace: x *= scale. */
+int esmcu_scale_inplace(esmcu_context* ctx, float* x, size_t n, float scale);
+/* kernels.h:73 RopeBuildTables: pure host function, host buffers
+ * cos/sin [seq_len, head_dim] (rope_tables.cpp:14-29). */
+int esmcu_rope_build_tables(int seq_len, int head_dim, float* cos_out, float* sin_out);
+/* kernels.h:90-92 RopeApplyVarlen: x [T, H, dh] in place, positions restart
+ * at every cu_seqlens boundary. */
+int esmcu_rope_apply_varlen(esmcu_context* ctx, float* x, const float* cos_t,
+                            const float* sin_t, const int* cu_seqlens, int batch_size,
+                            int num_heads, int head_dim);
+/* kernels.h:119-121 AttentionVarlen: q (pre-scaled, RoPE'd), k, v, out
+ * [T, H, dh]; per-sequence softmax attention over cu_seqlens. */
+int esmcu_attention_varlen(esmcu_context* ctx, const float* q, const float* k, const float* v,
+                           const int* cu_seqlens, int batch_size, int num_heads, int head_dim,
+                           float* out);
+
+/* ---- host-side packing (scheduler.h:29-30, batch.h:28-31) ---------------- */
+/* PlanBatches: writes every caller index once, group after group, into
+ * order_out[n] and each group's size into group_sizes_out; returns the
+ * group count (>= 0) or -1. */
+int esmcu_plan_batches(const int* lengths, int n, float imbalance_threshold,
+                       int max_batch_size, int* order_out, int* group_sizes_out);
+/* BatchView validation: ESMCU_OK or ESMCU_ERR_INVALID_ARGUMENT with the
+ * reference's message. n_masks is 0 (all tokens real) or T. */
+int esmcu_batch_view_check(int T, int n_masks, const int* cu_seqlens, int n_cu,
+                           int batch_size);
+
+/* ---- model --------------------------------------------------------------- */
+typedef struct {
+  int num_layers;
+  int hidden_size;
+  int num_heads;
+  int head_dim;
+  int intermediate_size;
+  int vocab_size;
+  float layer_norm_eps;
+  int mask_token_id;
+  int weights_quantized; /* 1: W8A8 Linears (Q8_ESM weights); 0: FP32 */
+  int act_quant;         /* esmcu_act_quant */
+} esmcu_config;
+
+/* Host pointers to one encoder layer (LayerWeights, model.h:50-85).  FP32
+ * Linear weights [out, in] for an unquantised model; int8 [out, in] plus
+ * per-output-channel scales for a quantised one.  Biases and LN are FP32. */
+typedef struct {
+  const float *attn_ln_w, *attn_ln_b;
+  const float *q_w, *k_w, *v_w, *out_w, *fc1_w, *fc2_w;
+  const int8_t *q_wq, *k_wq, *v_wq, *out_wq, *fc1_wq, *fc2_wq;
+  const float *q_ws, *k_ws, *v_ws, *out_ws, *fc1_ws, *fc2_ws;
+  const float *q_b, *k_b, *v_b, *out_b, *fc1_b, *fc2_b;
+  const float *ffn_ln_w, *ffn_ln_b;
+} esmcu_layer_weights;
+
+/* Allocates the per-device replica on ctx's device. */
+int esmcu_model_create(esmcu_context* ctx, const esmcu_config* cfg, esmcu_model** out);
+int esmcu_model_destroy(esmcu_model* m);
+int esmcu_model_config(const esmcu_model* m, esmcu_config* out);
+/* Uploads (copies) weights; the host buffers may be freed afterwards. */
+int esmcu_model_set_embeddings(esmcu_model* m, const float* embed /* [V, d] */);
+int esmcu_model_set_layer(esmcu_model* m, int layer, const esmcu_layer_weights* w);
+int esmcu_model_set_head(esmcu_model* m, const float* final_ln_w, const float* final_ln_b,
+                         const float* lm_dense_w, const float* lm_dense_b,
+                         const float* lm_ln_w, const float* lm_ln_b,
+                         const float* lm_decoder_bias);
+/* Model::ForwardPacked (model.cpp:1093-1255): host ids [T], masks [T] or
+ * NULL, cu_seqlens [B+1] -> host logits [T, V] in packed order.  T == 0
+ * writes nothing. */
+int esmcu_model_forward_packed(esmcu_model* m, const int32_t* ids, const int32_t* masks, int T,
+                               const int32_t* cu_seqlens, int batch_size, float* logits);
+/* Model::ForwardScheduled (model.cpp:1298-1421): n sequences concatenated in
+ * ids_concat with lengths lens[n] (masks_concat NULL = all real) -> logits
+ * concatenated in caller order [sum(lens), V]. */
+int esmcu_model_forward_scheduled(esmcu_model* m, const int32_t* ids_concat,
+                                  const int32_t* lens, const int32_t* masks_concat, int n,
+                                  float imbalance_threshold, int max_batch_size, float* logits);
+/* The same forward on device buffers, asynchronous on the context stream:
+ * d_ids [T] (and d_masks [T] or NULL) already on the device, host cu_seqlens
+ * [B+1] (validated on the host), d_logits [T, V] on the device.  Call
+ * esmcu_synchronize to wait and collect device-side failures. */
+int esmcu_model_forward_packed_device(esmcu_model* m, const int32_t* d_ids,
+                                      const int32_t* d_masks, int T, const int32_t* cu_seqlens,
+                                      int batch_size, float* d_logits);
+/* ForwardScheduled over several per-device replicas (one host thread each):
+ * groups from PlanBatches go to devices by longest-processing-time on the
+ * cost sum(24*d^2*L + 4*d*L^2); logits come back in caller order. */
+int esmcu_forward_scheduled_multi(esmcu_model** models, int n_models, const int32_t* ids_concat,
+                                  const int32_t* lens, const int32_t* masks_concat, int n,
+                                  float imbalance_threshold, int max_batch_size, float* logits);
+/* Calibration observer for SmoothQuant (Model::ForwardWithObserver,
+ * model.cpp:952-1050): runs the packed forward of an unquantised model and
+ * returns, per layer, the pctile-th percentile of |X| at the four Linear
+ * inputs (attn_ln_output, attn_out, ffn_ln_output, inter_gelu) in
+ * stats_out[num_layers * 4]. */
+int esmcu_model_observe_packed(esmcu_model* m, const int32_t* ids, int T,
+                               const int32_t* cu_seqlens, int batch_size, float pctile,
+                               float* stats_out);
+/* Section times (ms, CUDA events on the model's stream, names as the
+ * reference's ESM_PROFILE sections) when profiling is on (ESM_PROFILE=1 or
+ * esmcu_model_set_profiling).  esmcu_model_profile sums every forward since
+ * profiling was (re)enabled, or since the last host-buffer forward, and
+ * writes up to n {name, ms} entries; returns the count. */
+int esmcu_model_set_profiling(esmcu_model* m, int enabled);
+int esmcu_model_profile(esmcu_model* m, const char** names, float* ms, int n);
+/* Kernel launches issued by the last forward (the product's own kernels). */
+int esmcu_model_last_launch_count(const esmcu_model* m);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ESM_B200_H */
