@@ -187,8 +187,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_ok = m < p.M;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
-      float as = 1.0f;
-      if (row_ok) as = p.per_token ? __ldg(p.a_scale + m) : __ldg(p.a_scale);
+      float as = 1.0f;  // the raw-accumulator mode carries no activation scale
+      if (row_ok && p.acc_out == nullptr) as = p.per_token ? __ldg(p.a_scale + m) : __ldg(p.a_scale);
 
       if (EPI == kEpiQkvRope) {
 #pragma unroll 1
@@ -331,6 +331,8 @@ cudaError_t launch_gemm_i8(const GemmI8Args& a, cudaStream_t s) {
       (reinterpret_cast<uintptr_t>(a.A) & 15) || (reinterpret_cast<uintptr_t>(a.W) & 15) ||
       a.status == nullptr)
     return cudaErrorInvalidValue;
+  if (a.acc_out == nullptr && (a.a_scale == nullptr || a.w_scale == nullptr))
+    return cudaErrorInvalidValue;  // dequant needs both scales
   const int epi = a.acc_out ? kEpiStore : a.epi.kind;
   if (epi == kEpiQkvRope) {
     // One tile never straddles q|k|v and holds whole 64-wide heads.

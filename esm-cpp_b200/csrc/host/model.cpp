@@ -64,6 +64,10 @@ struct esmcu_model {
   std::vector<void*> owned;
   char* arena = nullptr;
   size_t arena_bytes = 0;
+  // Pinned host staging for the host-buffer entry points: inputs are copied
+  // here and sent with one async H2D each; logits come back the same way.
+  char* pinned = nullptr;
+  size_t pinned_bytes = 0;
   // profiling
   bool profiling = false;
   using EventPair = std::pair<std::string, std::pair<cudaEvent_t, cudaEvent_t>>;
@@ -173,6 +177,18 @@ int ensure_arena(esmcu_model* m, size_t bytes) {
   const size_t want = align_up(bytes + bytes / 8, 1 << 21);
   ESMCU_CUDA(cudaMalloc(&m->arena, want));
   m->arena_bytes = want;
+  return ESMCU_OK;
+}
+
+int ensure_pinned(esmcu_model* m, size_t bytes) {
+  if (bytes <= m->pinned_bytes) return ESMCU_OK;
+  ESMCU_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  if (m->pinned) ESMCU_CUDA(cudaFreeHost(m->pinned));
+  m->pinned = nullptr;
+  m->pinned_bytes = 0;
+  const size_t want = align_up(bytes + bytes / 8, 1 << 20);
+  ESMCU_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&m->pinned), want, cudaHostAllocDefault));
+  m->pinned_bytes = want;
   return ESMCU_OK;
 }
 
@@ -525,19 +541,26 @@ int forward_packed_host(esmcu_model* m, const int32_t* ids, const int32_t* masks
   m->launches = 0;
   cudaStream_t s = m->ctx->stream;
   char* base = m->arena;
-  ESMCU_CUDA(cudaMemcpyAsync(base + a.ids, ids, static_cast<size_t>(T) * 4, cudaMemcpyHostToDevice, s));
-  if (masks)
-    ESMCU_CUDA(cudaMemcpyAsync(base + a.masks, masks, static_cast<size_t>(T) * 4, cudaMemcpyHostToDevice, s));
-  ESMCU_CUDA(cudaMemcpyAsync(base + a.cu, cu, static_cast<size_t>(B + 1) * 4, cudaMemcpyHostToDevice, s));
+  const size_t V = static_cast<size_t>(m->cfg.vocab_size);
+  const size_t n_ids = static_cast<size_t>(T) * 4, n_cu = static_cast<size_t>(B + 1) * 4;
+  const size_t n_logits = logits ? static_cast<size_t>(T) * V * 4 : 0;
+  const size_t off_masks = align_up(n_ids, 256), off_cu = off_masks + align_up(masks ? n_ids : 0, 256);
+  const size_t off_logits = off_cu + align_up(n_cu, 256);
+  TRY(ensure_pinned(m, off_logits + n_logits));
+  char* pin = m->pinned;
+  std::memcpy(pin, ids, n_ids);
+  if (masks) std::memcpy(pin + off_masks, masks, n_ids);
+  std::memcpy(pin + off_cu, cu, n_cu);
+  ESMCU_CUDA(cudaMemcpyAsync(base + a.ids, pin, n_ids, cudaMemcpyHostToDevice, s));
+  if (masks) ESMCU_CUDA(cudaMemcpyAsync(base + a.masks, pin + off_masks, n_ids, cudaMemcpyHostToDevice, s));
+  ESMCU_CUDA(cudaMemcpyAsync(base + a.cu, pin + off_cu, n_cu, cudaMemcpyHostToDevice, s));
   float* d_logits = reinterpret_cast<float*>(base + a.logits);
   TRY(forward_device(m, a, reinterpret_cast<const int*>(base + a.ids),
                      masks ? reinterpret_cast<const int*>(base + a.masks) : nullptr, d_logits, T, B,
                      max_len, pctile, stats));
-  if (logits) {
-    ESMCU_CUDA(cudaMemcpyAsync(logits, d_logits, static_cast<size_t>(T) * m->cfg.vocab_size * 4,
-                               cudaMemcpyDeviceToHost, s));
-  }
+  if (logits) ESMCU_CUDA(cudaMemcpyAsync(pin + off_logits, d_logits, n_logits, cudaMemcpyDeviceToHost, s));
   ESMCU_CUDA(cudaStreamSynchronize(s));
+  if (logits) std::memcpy(logits, pin + off_logits, n_logits);
   if (m->profiling) collect_profile(m, true);
   return check_device_status(m->ctx);
 }
@@ -614,6 +637,7 @@ int esmcu_model_destroy(esmcu_model* m) {
   cudaStreamSynchronize(m->ctx->stream);
   for (void* p : m->owned) cudaFree(p);
   if (m->arena) cudaFree(m->arena);
+  if (m->pinned) cudaFreeHost(m->pinned);
   if (m->cos_t) cudaFree(m->cos_t);
   if (m->sin_t) cudaFree(m->sin_t);
   delete m;

@@ -1,0 +1,124 @@
+"""W8A8 INT8 GEMM on the tcgen05 tensor cores vs the oracle, through the C ABI.
+
+Gates: int8 quantised activations and int32
+accumulators bit-exact; dequantised outputs within rtol 1e-3 / atol 1 (they
+are in fact bit-exact: the epilogue performs the reference's
+FinalizeStore16 arithmetic, gemm_int8.cpp:109-126).  Shapes follow the
+reference's Int8Shapes sweep (tests/cpp/test_gemm_shapes.cpp:147-217): row
+tails, small M, N not a multiple of the tile, and the 650M shapes.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [  # (M, N, K)
+    (1, 16, 16), (7, 64, 48), (37, 96, 320), (128, 256, 128), (129, 200, 1280),
+    (300, 3840, 1280), (513, 1280, 1280), (260, 5120, 1280), (257, 1280, 5120),
+]
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def _weights(rng, N, K, O):
+    return O.quantize_weights((rng.standard_normal((N, K)) * 0.02).astype(np.float32))
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_quantize_and_int32_bitexact(cuda, O, M, N, K):
+    from esm_b200 import ops
+
+    torch = _torch()
+    rng = np.random.default_rng(M * 7 + N + K)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    Wq, _ = _weights(rng, N, K, O)
+    q, s = ops.quantize_activations(torch.from_numpy(A).to(cuda))
+    acc = ops.gemm_int8_s32(q, torch.from_numpy(Wq).to(cuda))
+    ops.synchronize()
+    q_ref, s_ref = O.quantize_act_per_tensor(A)
+    assert s.cpu().numpy()[0] == s_ref[0]
+    assert np.array_equal(q.cpu().numpy()[:, :K], q_ref)
+    assert np.array_equal(acc.cpu().numpy(), O.gemm_i8_s32(q_ref, Wq))
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES[:6])
+def test_per_token_quantize_bitexact(cuda, O, M, N, K):
+    from esm_b200 import ACT_PER_TOKEN, ops
+
+    torch = _torch()
+    rng = np.random.default_rng(M + 3 * N + K)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    A[:, rng.integers(0, K, max(1, K // 100))] *= 20.0  # outlier channels
+    q, s = ops.quantize_activations(torch.from_numpy(A).to(cuda), ACT_PER_TOKEN)
+    ops.synchronize()
+    q_ref, s_ref = O.quantize_act_per_token(A)
+    assert np.array_equal(s.cpu().numpy(), s_ref)
+    assert np.array_equal(q.cpu().numpy()[:, :K], q_ref)
+
+
+@pytest.mark.parametrize("per_token", [False, True])
+@pytest.mark.parametrize("M,N,K", SHAPES + [(33, 48, 40), (5, 17, 23)])
+def test_linear_int8_matches_oracle(cuda, O, M, N, K, per_token):
+    from esm_b200 import ACT_PER_TENSOR, ACT_PER_TOKEN, ops
+
+    torch = _torch()
+    rng = np.random.default_rng(M * 13 + N * 5 + K)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    Wq, ws = _weights(rng, N, K, O)
+    bias = (rng.standard_normal(N) * 0.1).astype(np.float32)
+    C = ops.linear_int8(torch.from_numpy(A).to(cuda), torch.from_numpy(Wq).to(cuda),
+                        torch.from_numpy(ws).to(cuda), torch.from_numpy(bias).to(cuda),
+                        ACT_PER_TOKEN if per_token else ACT_PER_TENSOR)
+    ops.synchronize()
+    want = O.linear_int8(A, Wq, ws, bias, per_token=per_token)
+    got = C.cpu().numpy()
+    np.testing.assert_allclose(got, want, rtol=1e-3, atol=1.0)
+    assert np.array_equal(got, want), "epilogue should reproduce FinalizeStore16 exactly"
+
+
+def test_linear_int8_matches_reference_vnni(cuda, O, R):
+    """Against the reference's own LinearVnni (one activation scale over M)."""
+    from esm_b200 import ops
+
+    torch = _torch()
+    rng = np.random.default_rng(11)
+    M, N, K = 96, 1280, 1280
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    Wq, ws = _weights(rng, N, K, O)
+    bias = (rng.standard_normal(N) * 0.1).astype(np.float32)
+    want = np.zeros((M, N), np.float32)
+    O.ref_check(R.ref_linear_int8_vnni(A.ctypes.data, Wq.ctypes.data, ws.ctypes.data,
+                                       bias.ctypes.data, want.ctypes.data, M, N, K))
+    C = ops.linear_int8(torch.from_numpy(A).to(cuda), torch.from_numpy(Wq).to(cuda),
+                        torch.from_numpy(ws).to(cuda), torch.from_numpy(bias).to(cuda))
+    ops.synchronize()
+    assert np.array_equal(C.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("N,K", [(3840, 1280), (1280, 1280), (5120, 1280), (1280, 5120)])
+def test_config2_full_size_sampled_rows(cuda, O, N, K):
+    """Config 2 at M = 32768 with 1% x20 outlier channels; int32 accumulators
+    of 64 sampled rows bit-exact, and every row's int8 quantisation exact."""
+    from esm_b200 import ops
+
+    torch = _torch()
+    M = 32768
+    g = torch.Generator(device=cuda).manual_seed(N + K)
+    A = torch.randn((M, K), device=cuda, generator=g)
+    cols = torch.randperm(K, device=cuda, generator=g)[: K // 100]
+    A[:, cols] *= 20.0
+    rng = np.random.default_rng(N * K)
+    Wq, _ = _weights(rng, N, K, O)
+    q, s = ops.quantize_activations(A)
+    acc = ops.gemm_int8_s32(q, torch.from_numpy(Wq).to(cuda))
+    ops.synchronize()
+    A_h = A.cpu().numpy()
+    q_ref, s_ref = O.quantize_act_per_tensor(A_h)
+    assert s.cpu().numpy()[0] == s_ref[0]
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+    rows = np.sort(rng.choice(M, 64, replace=False))
+    assert np.array_equal(acc.cpu().numpy()[rows], O.gemm_i8_s32(q_ref[rows], Wq))

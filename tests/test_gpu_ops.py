@@ -1,0 +1,183 @@
+"""Kernel-facade ops on the GPU vs the oracle (and the compiled reference),
+through the C ABI: LayerNorm, GELU, residual, scale, RoPE, varlen attention,
+FP32 Linear.  Tolerances are the reference's own precision classes
+(tests/cpp/test_gemm_shapes.cpp:250-256, test_attention_varlen.cpp:374-375):
+FP32 1e-4 * (1 + |ref|)."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _t(x, dev):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+
+
+def _close(got, want, tol=1e-4):
+    err = np.abs(got - want) / (1.0 + np.abs(want))
+    assert err.max() <= tol, f"max rel err {err.max():.3e}"
+
+
+@pytest.mark.parametrize("rows,d", [(1, 320), (37, 1280), (1000, 1280), (64, 2560), (5, 100)])
+def test_layernorm_matches_ref_twin(cuda, O, rows, d):
+    from esm_b200 import ops
+
+    rng = np.random.default_rng(rows + d)
+    x = (rng.standard_normal((rows, d)) * 3 + 0.5).astype(np.float32)
+    g = rng.standard_normal(d).astype(np.float32)
+    b = rng.standard_normal(d).astype(np.float32)
+    y = ops.layernorm(_t(x, cuda), _t(g, cuda), _t(b, cuda))
+    ops.synchronize()
+    got, want = y.cpu().numpy(), O.layernorm(x, g, b)
+    # Double-precision sums make the float result the reference's (LayerNormRef)
+    # except when a sum rounds across a float boundary: allow rare 1-ulp cases.
+    mism = np.mean(got != want)
+    assert mism < 1e-3, f"{mism:.2e} of outputs differ from LayerNormRef"
+    _close(got, want, 1e-6)
+
+
+def test_layernorm_known_answer(cuda):
+    """tests/cpp/test_kernels.cpp:113-139: x = [1,2,3,4], gamma 1, beta 0."""
+    from esm_b200 import ops
+
+    x = np.array([[1, 2, 3, 4]], np.float32)
+    y = ops.layernorm(_t(x, cuda), _t(np.ones(4, np.float32), cuda), _t(np.zeros(4, np.float32), cuda))
+    ops.synchronize()
+    mean, var = 2.5, 1.25
+    want = (x - mean) / np.sqrt(var + 1e-5)
+    np.testing.assert_allclose(y.cpu().numpy(), want, atol=1e-5)
+
+
+def test_gelu_known_answers_and_oracle(cuda, O):
+    from esm_b200 import ops
+
+    x = np.array([1.0, -1.0, 2.0], np.float32)
+    y = ops.gelu(_t(x, cuda))
+    ops.synchronize()
+    np.testing.assert_allclose(y.cpu().numpy(), [0.8413447, -0.1586553, 1.9544997], atol=1e-6)
+    xs = (np.random.default_rng(1).standard_normal(100000) * 4).astype(np.float32)
+    y = ops.gelu(_t(xs, cuda))
+    ops.synchronize()
+    _close(y.cpu().numpy(), O.gelu(xs), 1e-6)
+
+
+def test_residual_and_scale_exact(cuda):
+    from esm_b200 import ops
+
+    rng = np.random.default_rng(2)
+    a = rng.standard_normal(10001).astype(np.float32)
+    b = rng.standard_normal(10001).astype(np.float32)
+    ta = _t(a, cuda)
+    ops.residual_add_inplace(ta, _t(b, cuda))
+    ops.scale_inplace(ta, 0.125)
+    ops.synchronize()
+    assert np.array_equal(ta.cpu().numpy(), ((a + b) * np.float32(0.125)).astype(np.float32))
+
+
+def test_rope_tables_bitexact(O):
+    from esm_b200 import ops
+
+    for L, dh in [(300, 64), (1024, 16), (5, 32)]:
+        c, s = ops.rope_build_tables(L, dh)
+        co, so = O.rope_build_tables(L, dh)
+        assert np.array_equal(c, co) and np.array_equal(s, so)
+
+
+def test_rope_varlen_positions_restart(cuda, O):
+    """rope.cpp AVX-512 form, bit-exact; positions restart per sequence
+    (tests/cpp/test_attention_varlen.cpp:144-183)."""
+    from esm_b200 import ops
+
+    rng = np.random.default_rng(3)
+    cu = np.array([0, 5, 5, 30, 31, 100], np.int32)
+    H, dh = 3, 64
+    x = rng.standard_normal((100, H, dh)).astype(np.float32)
+    c, s = ops.rope_build_tables(128, dh)
+    tx = _t(x, cuda)
+    ops.rope_apply_varlen(tx, _t(c, cuda), _t(s, cuda), _t(cu, cuda), H, dh)
+    ops.synchronize()
+    want = O.rope_apply_varlen(x, c, s, cu, H, dh, fused=True)
+    assert np.array_equal(tx.cpu().numpy(), want)
+    # position 0 of every sequence is the identity rotation
+    for b in range(len(cu) - 1):
+        if cu[b + 1] > cu[b]:
+            assert np.array_equal(tx.cpu().numpy()[cu[b]], x[cu[b]])
+
+
+@pytest.mark.parametrize("lens,H,dh", [([1], 1, 16), ([7, 13, 1], 2, 16), ([33, 250, 90], 20, 64),
+                                       ([129, 300], 4, 64), ([1024], 2, 64), ([17, 5], 3, 32)])
+def test_attention_varlen_matches_oracle(cuda, O, lens, H, dh):
+    from esm_b200 import ops
+
+    rng = np.random.default_rng(sum(lens) + H)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    T = int(cu[-1])
+    q, k, v = (rng.standard_normal((3, T, H, dh)).astype(np.float32))
+    q *= np.float32(1.0 / np.sqrt(dh))
+    out = ops.attention_varlen(_t(q, cuda), _t(k, cuda), _t(v, cuda), _t(cu, cuda), H, dh)
+    ops.synchronize()
+    _close(out.cpu().numpy(), O.attention_varlen(q, k, v, cu, H, dh))
+
+
+def test_attention_matches_reference_avx512(cuda, O, R):
+    from esm_b200 import ops
+
+    rng = np.random.default_rng(9)
+    lens = [122, 90, 250, 17]
+    H, dh = 20, 64
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    T = int(cu[-1])
+    q, k, v = (rng.standard_normal((3, T, H, dh)).astype(np.float32))
+    want = np.zeros_like(q)
+    O.ref_check(R.ref_attention_varlen(q.ctypes.data, k.ctypes.data, v.ctypes.data, cu.ctypes.data,
+                                       len(lens), H, dh, want.ctypes.data))
+    out = ops.attention_varlen(_t(q, cuda), _t(k, cuda), _t(v, cuda), _t(cu, cuda), H, dh)
+    ops.synchronize()
+    _close(out.cpu().numpy(), want)
+
+
+def test_attention_isolation_poisoned_kv(cuda):
+    """tests/cpp/test_attention_varlen.cpp:185-225: poisoning sequence 2's
+    K/V must not change sequence 1's output."""
+    from esm_b200 import ops
+
+    rng = np.random.default_rng(5)
+    cu = np.array([0, 40, 100], np.int32)
+    H, dh = 4, 64
+    q, k, v = (rng.standard_normal((3, 100, H, dh)).astype(np.float32))
+    a = ops.attention_varlen(_t(q, cuda), _t(k, cuda), _t(v, cuda), _t(cu, cuda), H, dh)
+    k2, v2 = k.copy(), v.copy()
+    k2[40:] = 1e4
+    v2[40:] = -1e4
+    b = ops.attention_varlen(_t(q, cuda), _t(k2, cuda), _t(v2, cuda), _t(cu, cuda), H, dh)
+    ops.synchronize()
+    assert np.array_equal(a.cpu().numpy()[:40], b.cpu().numpy()[:40])
+
+
+def test_attention_large_scores_finite(cuda):
+    from esm_b200 import ops
+
+    cu = np.array([0, 64], np.int32)
+    q = np.full((64, 1, 64), 30.0, np.float32)
+    k = np.full((64, 1, 64), 30.0, np.float32)
+    v = np.random.default_rng(0).standard_normal((64, 1, 64)).astype(np.float32)
+    out = ops.attention_varlen(_t(q, cuda), _t(k, cuda), _t(v, cuda), _t(cu, cuda), 1, 64)
+    ops.synchronize()
+    o = out.cpu().numpy()
+    assert np.isfinite(o).all()
+    np.testing.assert_allclose(o[0, 0], v.mean(axis=0)[0], rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 33, 320), (130, 1280, 1280), (77, 33, 1280), (9, 11, 40)])
+def test_linear_f32_matches_oracle(cuda, O, M, N, K):
+    from esm_b200 import ops
+
+    rng = np.random.default_rng(M + N + K)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    W = (rng.standard_normal((N, K)) * 0.05).astype(np.float32)
+    b = rng.standard_normal(N).astype(np.float32)
+    C = ops.linear(_t(A, cuda), _t(W, cuda), _t(b, cuda))
+    ops.synchronize()
+    _close(C.cpu().numpy(), O.linear_f32(A, W, b))
