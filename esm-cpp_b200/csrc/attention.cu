@@ -3,7 +3,9 @@
 // 770-811).  Q arrives pre-scaled by 1/sqrt(dh) and RoPE'd; each query of
 // sequence b attends to the keys of sequence b only (cu_seqlens isolation).
 //
-// FP32 throughout.  One CTA per (sequence, head); each thread owns one query
+// This FP32 SIMT kernel serves head dims other than 64 and sequences longer
+// than 256 tokens; attention_tc.cu covers the rest on the tensor cores.
+// One CTA per (sequence, head); each thread owns one query
 // row (q and the output accumulator live in registers) and streams the
 // sequence's keys/values through shared memory in 32-row tiles with an
 // online (running-max) softmax, so any length up to the tokenizer's 1024
@@ -24,14 +26,14 @@ template <int DH>
 __global__ void __launch_bounds__(QT)
     attention_varlen_kernel(const float* __restrict__ q, const float* __restrict__ k,
                             const float* __restrict__ v, const int* __restrict__ cu, int H,
-                            int dh, float* __restrict__ out, uint32_t* amax) {
+                            int dh, float* __restrict__ out, uint32_t* amax, int min_len) {
   __shared__ __align__(16) float sK[KT][DH];
   __shared__ __align__(16) float sV[KT][DH];
   const int h = blockIdx.x;
   const int b = blockIdx.y;
   const int s0 = __ldg(cu + b);
   const int L = __ldg(cu + b + 1) - s0;
-  if (L <= 0) return;
+  if (L <= 0 || L <= min_len) return;  // shorter sequences run on the tensor-core kernel
   const long row_stride = static_cast<long>(H) * dh;
   float mx_out = 0.0f;
 
@@ -120,27 +122,33 @@ __global__ void __launch_bounds__(QT)
       }
     }
   }
-  if (amax != nullptr) {
-    mx_out = warp_max(mx_out);
-    if ((threadIdx.x & 31) == 0) atomicMax(amax, __float_as_uint(mx_out));
-  }
+  if (amax != nullptr) amax_publish(amax, mx_out);
 }
 
 }  // namespace
 
+cudaError_t launch_attention_tc(const float* q, const float* k, const float* v, const int* cu,
+                                int B, int H, int max_len, float* out, uint32_t* amax,
+                                uint32_t* status, cudaStream_t s);
+
 cudaError_t launch_attention_varlen(const float* q, const float* k, const float* v,
                                     const int* cu, int B, int H, int dh, int max_len,
-                                    float* out, uint32_t* amax, cudaStream_t s) {
-  (void)max_len;
-  if (B <= 0 || H <= 0) return cudaSuccess;
-  if (dh <= 0 || dh > 128 || (dh & 1)) return cudaErrorInvalidValue;
+                                    float* out, uint32_t* amax, uint32_t* status, cudaStream_t s) {
+  if (B <= 0 || H <= 0 || max_len <= 0) return cudaSuccess;
+  if (dh <= 0 || dh > 128 || (dh & 3)) return cudaErrorInvalidValue;
+  // head_dim 64, length <= 256: tensor cores (3xTF32); the rest: FP32 SIMT.
+  int min_len = 0;
+  if (dh == 64 && status != nullptr) {
+    cudaError_t e = launch_attention_tc(q, k, v, cu, B, H, max_len, out, amax, status, s);
+    if (e != cudaSuccess) return e;
+    if (max_len <= 256) return cudaSuccess;
+    min_len = 256;
+  }
   dim3 grid(H, B);
-  // The float4 paths need row bases 16-byte aligned: dh % 4 == 0.
-  if ((dh & 3) != 0) return cudaErrorInvalidValue;
-  if (dh <= 16) attention_varlen_kernel<16><<<grid, QT, 0, s>>>(q, k, v, cu, H, dh, out, amax);
-  else if (dh <= 32) attention_varlen_kernel<32><<<grid, QT, 0, s>>>(q, k, v, cu, H, dh, out, amax);
-  else if (dh <= 64) attention_varlen_kernel<64><<<grid, QT, 0, s>>>(q, k, v, cu, H, dh, out, amax);
-  else attention_varlen_kernel<128><<<grid, QT, 0, s>>>(q, k, v, cu, H, dh, out, amax);
+  if (dh <= 16) attention_varlen_kernel<16><<<grid, QT, 0, s>>>(q, k, v, cu, H, dh, out, amax, min_len);
+  else if (dh <= 32) attention_varlen_kernel<32><<<grid, QT, 0, s>>>(q, k, v, cu, H, dh, out, amax, min_len);
+  else if (dh <= 64) attention_varlen_kernel<64><<<grid, QT, 0, s>>>(q, k, v, cu, H, dh, out, amax, min_len);
+  else attention_varlen_kernel<128><<<grid, QT, 0, s>>>(q, k, v, cu, H, dh, out, amax, min_len);
   return cudaGetLastError();
 }
 

@@ -14,9 +14,15 @@ namespace esmb200 {
 // of spinning forever; the host turns the bit into ESMCU_ERR_TIMEOUT.
 constexpr uint32_t kStatusTimeout = 1u;
 
-// ~2^26 polls with a short sleep between late polls is seconds of wall time,
+// Bound of every barrier wait: 2 s of device wall time (%globaltimer, ns),
 // far above any legitimate wait in these kernels (microseconds).
-constexpr uint32_t kWaitPolls = 1u << 26;
+constexpr uint64_t kWaitNs = 2000000000ull;
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -61,9 +67,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Bounded wait for the phase with the given parity.  Returns false (and sets
 // the timeout bit in *status) when the bound is reached.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status) {
-  for (uint32_t i = 0; i < kWaitPolls; ++i) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (i > 1024) __nanosleep(64);
+    if ((i & 255u) == 0 && global_timer_ns() - t0 > kWaitNs) break;
+    if (i > 64) __nanosleep(32);
   }
   atomicOr(status, kStatusTimeout);
   return false;
@@ -113,6 +122,24 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_
       "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, tf32 x tf32 -> fp32 (operands are fp32
+// words; the tensor core reads their tf32 part), issued by one thread.
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Makes this thread's generic-proxy shared-memory writes visible to the
+// async proxy (tensor core / TMA reads) after the following barrier.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // Arrive on an mbarrier once every tcgen05 op issued so far by this thread
@@ -166,6 +193,23 @@ __host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
          (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// Instruction descriptor for kind::tf32: D f32, A/B tf32, both K-major.
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
+         (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// Byte offset of element (row, col) of a K-major tile stored with 128-byte
+// swizzle for 4-byte elements: 32 elements per 128-byte row segment,
+// segments ("column blocks") of `rows` rows stored one after the other; the
+// 16-byte chunk index inside a row segment is XORed with (row % 8).
+__device__ __forceinline__ uint32_t sw128_off4(int row, int col, int rows) {
+  const int blk = col >> 5;
+  const int byte = (col & 31) * 4;
+  const int chunk = (byte >> 4) ^ (row & 7);
+  return static_cast<uint32_t>(blk * rows * 128 + row * 128 + chunk * 16 + (byte & 15));
+}
+
 // ------------------------------------------------------------ misc device
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
@@ -186,8 +230,30 @@ __device__ __forceinline__ double warp_sum_d(double v) {
 // Non-negative float bit patterns order like the floats, so the absmax of a
 // tensor reduces with an integer atomicMax on the bits (the reference's CAS
 // on float bits, gemm_int8.cpp:464-470, relies on the same fact).
-__device__ __forceinline__ void atomic_absmax(uint32_t* bits, float v) {
-  atomicMax(bits, __float_as_uint(fabsf(v)));
+// amax_publish: block-wide max (all threads call it) -> one atomic into the
+// block's slot.  v >= 0.
+__device__ __forceinline__ void amax_publish(uint32_t* slots, float v) {
+  __shared__ float s_wmax[32];
+  v = warp_max(v);
+  const int w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  if ((threadIdx.x & 31) == 0) s_wmax[w] = v;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float m = 0.0f;
+    for (int i = 0; i < nw; ++i) m = fmaxf(m, s_wmax[i]);
+    atomicMax(slots + (blockIdx.x % 64), __float_as_uint(m));
+  }
+}
+// Warp-level variant for kernels whose warps cannot meet at a block barrier.
+__device__ __forceinline__ void amax_publish_warp(uint32_t* slots, float v) {
+  v = warp_max(v);
+  if ((threadIdx.x & 31) == 0) atomicMax(slots + (blockIdx.x % 64), __float_as_uint(v));
+}
+__device__ __forceinline__ float amax_read(const uint32_t* slots) {
+  uint32_t m = 0;
+#pragma unroll 8
+  for (int i = 0; i < 64; ++i) m = max(m, __ldg(slots + i));
+  return __uint_as_float(m);
 }
 
 }  // namespace esmb200

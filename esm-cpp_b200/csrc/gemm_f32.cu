@@ -108,10 +108,7 @@ __global__ void __launch_bounds__(256)
       mx = fmaxf(mx, epi_row_run<4>(e, m, c0, N, y));
     }
   }
-  if (e.amax != nullptr) {
-    mx = warp_max(mx);
-    if ((threadIdx.x & 31) == 0) atomicMax(e.amax, __float_as_uint(mx));
-  }
+  if (e.amax != nullptr) amax_publish(e.amax, mx);
 }
 
 }  // namespace

@@ -244,10 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
-    if (p.epi.amax != nullptr) {
-      amax = warp_max(amax);
-      if (lane == 0) atomic_absmax(p.epi.amax, amax);
-    }
+    if (p.epi.amax != nullptr) amax_publish_warp(p.epi.amax, amax);
   }
 
   tc_fence_before();

@@ -3,8 +3,10 @@
 // reference named in include/esm_b200.h and enqueues on the context stream.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstring>
 #include <string>
+#include <vector>
 
 #include "../kernels.cuh"
 #include "context.h"
@@ -216,9 +218,9 @@ int esmcu_quantize_activations(esmcu_context* ctx, const float* A, int M, int K,
     return ESMCU_OK;
   }
   if (act_quant != ESMCU_ACT_PER_TENSOR) return fail(ESMCU_ERR_INVALID_ARGUMENT, "bad act_quant");
-  ESMCU_TRY(ensure_scratch(ctx, 256));
+  ESMCU_TRY(ensure_scratch(ctx, kAmaxSlots * sizeof(uint32_t)));
   uint32_t* amax = static_cast<uint32_t*>(ctx->scratch);
-  ESMCU_CUDA(cudaMemsetAsync(amax, 0, sizeof(uint32_t), ctx->stream));
+  ESMCU_CUDA(cudaMemsetAsync(amax, 0, kAmaxSlots * sizeof(uint32_t), ctx->stream));
   ESMCU_CUDA(launch_absmax(A, static_cast<long>(M) * K, amax, ctx->stream));
   ESMCU_CUDA(launch_quantize_per_tensor(A, K, M, K, amax, q_out, ldq, scales_out, ctx->stream));
   return ESMCU_OK;
@@ -265,8 +267,8 @@ int esmcu_linear_int8(esmcu_context* ctx, const float* A, const int8_t* W, const
   }
   const long ldq = static_cast<long>(align_up(static_cast<size_t>(K), 16));
   const bool pad_w = (ldq != K) || (reinterpret_cast<uintptr_t>(W) & 15);
-  // Scratch layout: [amax 256B][scales M*4 -> 256-aligned][q M*ldq][padded W N*ldq]
-  const size_t off_scales = 256;
+  // Scratch layout: [amax slots 256B][scales M*4 -> 256-aligned][q M*ldq][padded W N*ldq]
+  const size_t off_scales = kAmaxSlots * sizeof(uint32_t);
   const size_t off_q = align_up(off_scales + sizeof(float) * static_cast<size_t>(M), 256);
   const size_t off_w = align_up(off_q + static_cast<size_t>(M) * ldq, 256);
   const size_t total = off_w + (pad_w ? static_cast<size_t>(N) * ldq : 0);
@@ -285,7 +287,7 @@ int esmcu_linear_int8(esmcu_context* ctx, const float* A, const int8_t* W, const
   if (act_quant == ESMCU_ACT_PER_TOKEN) {
     ESMCU_CUDA(launch_quantize_per_token(A, K, M, K, q, ldq, scales, ctx->stream));
   } else {
-    ESMCU_CUDA(cudaMemsetAsync(amax, 0, sizeof(uint32_t), ctx->stream));
+    ESMCU_CUDA(cudaMemsetAsync(amax, 0, kAmaxSlots * sizeof(uint32_t), ctx->stream));
     ESMCU_CUDA(launch_absmax(A, static_cast<long>(M) * K, amax, ctx->stream));
     ESMCU_CUDA(launch_quantize_per_tensor(A, K, M, K, amax, q, ldq, scales, ctx->stream));
   }
@@ -373,7 +375,16 @@ int esmcu_attention_varlen(esmcu_context* ctx, const float* q, const float* k, c
   ESMCU_TRY(check_ptr(v, "v"));
   ESMCU_TRY(check_ptr(cu, "cu_seqlens"));
   ESMCU_TRY(check_ptr(out, "out"));
-  ESMCU_CUDA(launch_attention_varlen(q, k, v, cu, B, H, dh, 0, out, nullptr, ctx->stream));
+  // The sequence lengths decide the kernel (tensor cores up to 256 tokens),
+  // so read cu_seqlens back once.
+  std::vector<int> cu_h(static_cast<size_t>(B) + 1);
+  ESMCU_CUDA(cudaMemcpyAsync(cu_h.data(), cu, cu_h.size() * sizeof(int), cudaMemcpyDeviceToHost,
+                             ctx->stream));
+  ESMCU_CUDA(cudaStreamSynchronize(ctx->stream));
+  int max_len = 0;
+  for (int b = 0; b < B; ++b) max_len = std::max(max_len, cu_h[b + 1] - cu_h[b]);
+  ESMCU_CUDA(launch_attention_varlen(q, k, v, cu, B, H, dh, max_len, out, nullptr, ctx->d_status,
+                                     ctx->stream));
   return ESMCU_OK;
 }
 

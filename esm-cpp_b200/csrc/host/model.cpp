@@ -72,6 +72,7 @@ struct esmcu_model {
   bool profiling = false;
   using EventPair = std::pair<std::string, std::pair<cudaEvent_t, cudaEvent_t>>;
   std::vector<EventPair> pending;  // recorded, not yet read
+  std::vector<cudaEvent_t> event_pool;  // reused so timing adds no event creation
   std::vector<std::pair<std::string, float>> prof;
   int launches = 0;
 };
@@ -163,7 +164,7 @@ Arena plan_arena(const esmcu_model* m, int T, int B) {
   a.inter = take(Tz * ffn * 4);
   a.qkv = take(Tz * 3 * d * 4);
   a.logits = take(Tz * static_cast<size_t>(c.vocab_size) * 4);
-  a.amax = take(static_cast<size_t>(4 * c.num_layers + 8) * 4);
+  a.amax = take(static_cast<size_t>(4 * c.num_layers + 8) * kAmaxSlots * 4);
   a.total = cur;
   return a;
 }
@@ -216,11 +217,19 @@ struct Sections {
   esmcu_model* m;
   std::vector<std::pair<std::string, std::pair<cudaEvent_t, cudaEvent_t>>> ev;
   explicit Sections(esmcu_model* mm) : m(mm) {}
+  cudaEvent_t take() {
+    cudaEvent_t e;
+    if (m->event_pool.empty()) {
+      cudaEventCreate(&e);
+    } else {
+      e = m->event_pool.back();
+      m->event_pool.pop_back();
+    }
+    return e;
+  }
   void begin(const char* name) {
     if (!m->profiling) return;
-    cudaEvent_t a, b;
-    cudaEventCreate(&a);
-    cudaEventCreate(&b);
+    cudaEvent_t a = take(), b = take();
     cudaEventRecord(a, m->ctx->stream);
     ev.push_back({name, {a, b}});
   }
@@ -243,8 +252,8 @@ void collect_profile(esmcu_model* m, bool reset) {
                            [&](const auto& p) { return p.first == e.first; });
     if (it == m->prof.end()) m->prof.push_back({e.first, ms});
     else it->second += ms;
-    cudaEventDestroy(e.second.first);
-    cudaEventDestroy(e.second.second);
+    m->event_pool.push_back(e.second.first);
+    m->event_pool.push_back(e.second.second);
   }
   m->pending.clear();
 }
@@ -291,7 +300,7 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
 
   Sections sec(m);
 
-  ESMCU_CUDA(cudaMemsetAsync(amax, 0, static_cast<size_t>(4 * c.num_layers + 8) * 4, s));
+  ESMCU_CUDA(cudaMemsetAsync(amax, 0, static_cast<size_t>(4 * c.num_layers + 8) * kAmaxSlots * 4, s));
   LAUNCH(m, launch_positions(cu, B, pos, s));
   sec.begin("embed");
   LAUNCH(m, launch_embed(m->embed, d, ids, mk, cu, B, c.mask_token_id, hidden, s));
@@ -346,7 +355,7 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
 
   for (int li = 0; li < c.num_layers; ++li) {
     const DevLayer& L = m->layers[static_cast<size_t>(li)];
-    uint32_t* am = amax + 4 * li;
+    uint32_t* am = amax + 4 * li * kAmaxSlots;  // 4 tensors x kAmaxSlots slots
     // ---- attention block
     sec.begin("attn_ln");
     if (quant && per_token) {
@@ -354,13 +363,13 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
                                  q8, m->ldk_d, ascale, s));
     } else {
       LAUNCH(m, launch_layernorm(hidden, L.ln1_w, L.ln1_b, c.layer_norm_eps, ln, T, d,
-                                 quant ? am + 0 : nullptr, nullptr, 0, nullptr, s));
+                                 quant ? am : nullptr, nullptr, 0, nullptr, s));
     }
     sec.end();
     observe(li, 0, ln, Td);
     if (quant && !per_token) {
       sec.begin("quantize");
-      TRY(quantize(ln, d, m->ldk_d, am + 0));
+      TRY(quantize(ln, d, m->ldk_d, am));
       sec.end();
     }
     sec.begin("qkv_proj");
@@ -397,12 +406,12 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
     }
     sec.begin("attention");
     LAUNCH(m, launch_attention_varlen(q, k, v, cu, B, H, dh, max_len, attn,
-                                      (quant && !per_token) ? am + 1 : nullptr, s));
+                                      (quant && !per_token) ? am + 1 * kAmaxSlots : nullptr, ctx->d_status, s));
     sec.end();
     observe(li, 1, attn, Td);
     if (quant) {
       sec.begin("quantize");
-      TRY(quantize(attn, d, m->ldk_d, am + 1));
+      TRY(quantize(attn, d, m->ldk_d, am + 1 * kAmaxSlots));
       sec.end();
     }
     sec.begin("attn_out_proj");
@@ -425,13 +434,13 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
                                  q8, m->ldk_d, ascale, s));
     } else {
       LAUNCH(m, launch_layernorm(hidden, L.ln2_w, L.ln2_b, c.layer_norm_eps, ln, T, d,
-                                 quant ? am + 2 : nullptr, nullptr, 0, nullptr, s));
+                                 quant ? am + 2 * kAmaxSlots : nullptr, nullptr, 0, nullptr, s));
     }
     sec.end();
     observe(li, 2, ln, Td);
     if (quant && !per_token) {
       sec.begin("quantize");
-      TRY(quantize(ln, d, m->ldk_d, am + 2));
+      TRY(quantize(ln, d, m->ldk_d, am + 2 * kAmaxSlots));
       sec.end();
     }
     sec.begin("fc1");
@@ -441,7 +450,7 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
       e.C = inter;
       e.ldc = ffn;
       if (quant) {
-        e.amax = per_token ? nullptr : am + 3;
+        e.amax = per_token ? nullptr : am + 3 * kAmaxSlots;
         TRY(gemm_i8(L.w1, m->ldk_d, ffn, L.s1, L.b1, e));
       } else {
         TRY(gemm_f32(ln, d, L.f1, ffn, L.b1, e));
@@ -451,7 +460,7 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
     observe(li, 3, inter, static_cast<size_t>(T) * ffn);
     if (quant) {
       sec.begin("quantize");
-      TRY(quantize(inter, ffn, m->ldk_ffn, am + 3));
+      TRY(quantize(inter, ffn, m->ldk_ffn, am + 3 * kAmaxSlots));
       sec.end();
     }
     sec.begin("fc2");
@@ -638,6 +647,11 @@ int esmcu_model_destroy(esmcu_model* m) {
   for (void* p : m->owned) cudaFree(p);
   if (m->arena) cudaFree(m->arena);
   if (m->pinned) cudaFreeHost(m->pinned);
+  for (auto& e : m->pending) {
+    cudaEventDestroy(e.second.first);
+    cudaEventDestroy(e.second.second);
+  }
+  for (auto e : m->event_pool) cudaEventDestroy(e);
   if (m->cos_t) cudaFree(m->cos_t);
   if (m->sin_t) cudaFree(m->sin_t);
   delete m;

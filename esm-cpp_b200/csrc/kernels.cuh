@@ -7,6 +7,12 @@
 
 namespace esmb200 {
 
+// A per-tensor absmax lives in kAmaxSlots uint32 slots (float bits): each
+// producer block folds its maximum into slot (blockIdx.x % kAmaxSlots) and the
+// consumer takes the max over the slots.  Spreading the atomics over 64
+// addresses keeps thousands of blocks from serialising on one L2 line.
+constexpr int kAmaxSlots = 64;
+
 // Epilogue applied to a finished fp32 output tile (after dequant for the
 // INT8 GEMM, after bias for the FP32 GEMM).
 enum EpiKind : int {
@@ -20,8 +26,8 @@ struct EpiParams {
   int kind = kEpiStore;
   float* C = nullptr;
   long ldc = 0;
-  // When non-null, max|stored value| over the tensor is folded into *amax
-  // (float bits, atomicMax).  Feeds the next GEMM's per-tensor scale.
+  // When non-null, max|stored value| over the tensor is folded into the
+  // kAmaxSlots slots at amax.  Feeds the next GEMM's per-tensor scale.
   uint32_t* amax = nullptr;
   // kEpiQkvRope: the output columns [0,d) | [d,2d) | [2d,3d) go to q | k | v,
   // each [M, d] with row stride d; head_dim must be 64.
@@ -73,7 +79,8 @@ struct GemmF32Args {
 cudaError_t launch_gemm_f32(const GemmF32Args& a, cudaStream_t s);
 
 // ------------------------------------------------------------ quantisation
-// Per-tensor: scale = amax>0 ? amax/127 : 1 (amax read from *amax_bits);
+// Per-tensor: scale = amax>0 ? amax/127 : 1 (amax = max over the kAmaxSlots
+// slots at amax_bits);
 // q = clamp(rne(x * (1/scale)), +-127); writes *scale_out; pads columns
 // [K, ldq) of each row with zeros.
 cudaError_t launch_quantize_per_tensor(const float* x, long ldx, int M, int K,
@@ -94,10 +101,11 @@ cudaError_t launch_layernorm(const float* x, const float* g, const float* b, flo
 
 // --------------------------------------------------------------- attention
 // Packed-varlen attention, q pre-scaled and RoPE'd; q,k,v,out [T, H, dh].
-// Optional absmax of out into *amax.
+// max_len = longest sequence (host-known).  Optional absmax of out into
+// *amax.  head_dim 64 runs on the tensor cores (needs the status word).
 cudaError_t launch_attention_varlen(const float* q, const float* k, const float* v,
                                     const int* cu, int B, int H, int dh, int max_len,
-                                    float* out, uint32_t* amax, cudaStream_t s);
+                                    float* out, uint32_t* amax, uint32_t* status, cudaStream_t s);
 
 // ------------------------------------------------------------- elementwise
 cudaError_t launch_gelu(const float* x, float* out, long n, cudaStream_t s);

@@ -20,8 +20,9 @@ __global__ void layernorm_kernel(const float* __restrict__ x, const float* __res
                                  int rows, int d, uint32_t* amax, int8_t* __restrict__ q,
                                  long ldq, float* __restrict__ row_scales) {
   const int lane = threadIdx.x & 31;
-  const long r = (blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x) >> 5;
-  if (r >= rows) return;
+  const long r0 = (blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x) >> 5;
+  const bool live = r0 < rows;
+  const long r = live ? r0 : rows - 1;  // idle warps recompute the last row, store nothing
   const float* xr = x + r * d;
   float v[NPL];
   double sum = 0.0;
@@ -53,12 +54,13 @@ __global__ void layernorm_kernel(const float* __restrict__ x, const float* __res
       const float normed = __fmul_rn(__fsub_rn(v[i], meanf), inv_std);
       v[i] = __fmaf_rn(normed, __ldg(g + c), __ldg(b + c));
       mx = fmaxf(mx, fabsf(v[i]));
-      if (out) out[r * d + c] = v[i];
+      if (out && live) out[r * d + c] = v[i];
     }
   }
-  if (amax != nullptr || q != nullptr) mx = warp_max(mx);
-  if (amax != nullptr && lane == 0) atomicMax(amax, __float_as_uint(mx));
+  if (amax != nullptr) amax_publish(amax, mx);  // block-wide: every warp gets here
+  if (!live) return;
   if (q != nullptr) {
+    mx = warp_max(mx);
     const float s = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 1.0f;
     const float inv = __fdiv_rn(1.0f, s);
     if (lane == 0) row_scales[r] = s;
@@ -80,8 +82,9 @@ __global__ void layernorm_wide_kernel(const float* __restrict__ x, const float* 
                                       const float* __restrict__ b, float eps,
                                       float* __restrict__ out, int rows, int d, uint32_t* amax) {
   const int lane = threadIdx.x & 31;
-  const long r = (blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x) >> 5;
-  if (r >= rows) return;
+  const long r0 = (blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x) >> 5;
+  const bool live = r0 < rows;
+  const long r = live ? r0 : rows - 1;
   const float* xr = x + r * d;
   double sum = 0.0;
   for (int c = lane; c < d; c += 32) sum += static_cast<double>(xr[c]);
@@ -97,13 +100,10 @@ __global__ void layernorm_wide_kernel(const float* __restrict__ x, const float* 
   float mx = 0.0f;
   for (int c = lane; c < d; c += 32) {
     const float y = __fmaf_rn(__fmul_rn(__fsub_rn(xr[c], meanf), inv_std), g[c], b[c]);
-    out[r * d + c] = y;
+    if (live) out[r * d + c] = y;
     mx = fmaxf(mx, fabsf(y));
   }
-  if (amax != nullptr) {
-    mx = warp_max(mx);
-    if (lane == 0) atomicMax(amax, __float_as_uint(mx));
-  }
+  if (amax != nullptr) amax_publish(amax, mx);
 }
 
 }  // namespace

@@ -33,7 +33,14 @@ __global__ void quantize_per_tensor_kernel(const float* __restrict__ x, long ldx
                                            const uint32_t* __restrict__ amax_bits,
                                            int8_t* __restrict__ q, long ldq,
                                            float* __restrict__ scale_out) {
-  const float s = act_scale_from_amax(__uint_as_float(__ldg(amax_bits)));
+  __shared__ float s_amax;
+  if (threadIdx.x < 32) {
+    const uint32_t m = max(__ldg(amax_bits + threadIdx.x), __ldg(amax_bits + 32 + threadIdx.x));
+    const float v = warp_max(__uint_as_float(m));
+    if (threadIdx.x == 0) s_amax = v;
+  }
+  __syncthreads();
+  const float s = act_scale_from_amax(s_amax);
   const float inv = __fdiv_rn(1.0f, s);
   if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = s;
   const long groups_per_row = ldq / 16;
@@ -85,8 +92,7 @@ __global__ void absmax_kernel(const float* __restrict__ x, long n, uint32_t* ama
   for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<long>(gridDim.x) * blockDim.x)
     mx = fmaxf(mx, fabsf(x[i]));
-  mx = warp_max(mx);
-  if ((threadIdx.x & 31) == 0) atomicMax(amax_bits, __float_as_uint(mx));
+  amax_publish(amax_bits, mx);
 }
 
 int grid_for(long work, int block) {

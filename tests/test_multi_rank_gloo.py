@@ -1,0 +1,119 @@
+"""The N > 1 path on the CPU: world_size-2 gloo ranks shard ForwardScheduled
+by packed group and gather logits to rank 0.  The per-group compute is the
+CPU oracle (a tiny model), so only the sharding / gathering / reordering
+logic is under test; the GPU per-group path is covered by the -m gpu tests.
+A rank that fails makes the others fail on the host (short process-group
+timeout), never hang."""
+import os
+import socket
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+TINY = dict(num_hidden_layers=1, hidden_size=64, num_attention_heads=1, head_dim=64,
+            intermediate_size=128)
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _workload():
+    from esm_b200 import synth
+
+    return synth.residue_ids(synth.varlen_lengths(23, seed=3, mean=40, sd=25, lo=1, hi=90), seed=4)
+
+
+def _worker(rank, world, port, outdir, fail_rank):
+    import datetime
+
+    for p in (str(ROOT / "esm-cpp_b200"), str(ROOT / "oracle")):
+        sys.path.insert(0, p)
+    import torch.distributed as dist
+
+    import oracle as O
+    from esm_b200 import synth
+    from esm_b200.distributed import forward_scheduled_sharded
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=20))
+    try:
+        m = synth.random_model(TINY, seed=9)
+        m.quantize_weights()
+
+        def run_group(ids, cu):
+            if rank == fail_rank:
+                raise RuntimeError("injected failure on rank %d" % rank)
+            return O.forward_packed(m, ids, cu)
+
+        try:
+            out = forward_scheduled_sharded(run_group, _workload(), rank, world, d=64,
+                                            max_batch_size=5)
+            status = "ok"
+        except Exception as e:  # noqa: BLE001
+            out, status = None, f"error: {type(e).__name__}"
+        if rank == 0 and out is not None:
+            np.savez(Path(outdir) / "out.npz", *out)
+        (Path(outdir) / f"status{rank}.txt").write_text(status)
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:  # noqa: BLE001
+            pass
+
+
+def _spawn(tmp_path, fail_rank=-1, world=2):
+    import torch.multiprocessing as mp
+
+    mp.start_processes(_worker, args=(world, _port(), str(tmp_path), fail_rank), nprocs=world,
+                       join=True, start_method="spawn")
+
+
+def test_sharded_scheduled_forward_equals_single_process(tmp_path, O):
+    from esm_b200 import synth
+
+    _spawn(tmp_path)
+    assert (tmp_path / "status0.txt").read_text() == "ok"
+    assert (tmp_path / "status1.txt").read_text() == "ok"
+    got = np.load(tmp_path / "out.npz")
+    seqs = _workload()
+    m = synth.random_model(TINY, seed=9)
+    m.quantize_weights()
+    from esm_b200.ops import plan_batches
+
+    lens = [len(s) for s in seqs]
+    for g in plan_batches(np.array(lens, np.int32), 1.2, 5):  # same groups -> same numerics
+        ids = np.concatenate([seqs[i] for i in g])
+        cu = np.concatenate([[0], np.cumsum([lens[i] for i in g])]).astype(np.int32)
+        want = O.forward_packed(m, ids, cu)
+        for j, i in enumerate(g):
+            assert np.array_equal(got[f"arr_{i}"], want[cu[j]:cu[j + 1]])
+
+
+def test_failing_rank_is_reported_not_hung(tmp_path):
+    _spawn(tmp_path, fail_rank=1)
+    assert (tmp_path / "status1.txt").read_text().startswith("error")
+    assert (tmp_path / "status0.txt").read_text().startswith("error")
+
+
+def test_lpt_assignment_balances_and_covers():
+    from esm_b200.distributed import assign_groups, group_cost
+
+    rng = np.random.default_rng(0)
+    lens = rng.integers(50, 400, 64).tolist()
+    plan = [list(range(i, min(i + 4, 64))) for i in range(0, 64, 4)]
+    for world in (1, 2, 4, 8):
+        a = assign_groups(plan, lens, world, 1280)
+        assert sorted(sum(a, [])) == list(range(len(plan)))
+        loads = [sum(group_cost([lens[i] for i in plan[g]], 1280) for g in r) for r in a]
+        biggest = max(group_cost([lens[i] for i in g], 1280) for g in plan)
+        assert max(loads) - min(loads) <= biggest
