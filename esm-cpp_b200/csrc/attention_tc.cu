@@ -37,6 +37,7 @@ constexpr int DH = 64;       // head dim on this path
 constexpr int KMAX = 256;    // longest sequence on this path
 constexpr int KC = 32;       // keys per P.V chunk (one swizzle row of tf32)
 constexpr int kThreads = 128;
+constexpr int kBatch = 8;     // independent float4 loads in flight per thread
 constexpr uint32_t kRegionA = 0;        // Q hi|lo (32K each) -> P buffers
 constexpr uint32_t kRegionB = 65536;    // K hi|lo (64K each) -> V^T hi|lo
 constexpr uint32_t kSmemUsed = 196608;
@@ -97,18 +98,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_relinquish();
   }
 
-  // ---- 1. Q and K, split into tf32 hi/lo, K-major 128-byte swizzle
-  for (int e = tid; e < QB * 16; e += kThreads) {
-    const int r = e >> 4, c4 = e & 15;
-    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (q0 + r < L) x = __ldg(reinterpret_cast<const float4*>(qg + (q0 + r) * rs + c4 * 4));
-    split_store4(A, A + 32768, sw128_off4(r, c4 * 4, QB), x);
-  }
-  for (int e = tid; e < Lk16 * 16; e += kThreads) {
-    const int r = e >> 4, c4 = e & 15;
-    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (r < L) x = __ldg(reinterpret_cast<const float4*>(kg + r * rs + c4 * 4));
-    split_store4(Bm, Bm + 65536, sw128_off4(r, c4 * 4, Lk16), x);
+  // ---- 1. Q and K, split into tf32 hi/lo, K-major 128-byte swizzle.  One
+  // index space (Q float4s, then K float4s); each thread issues kBatch
+  // independent loads before it stores any, to keep loads in flight.
+  const int nq = QB * 16, nqk = nq + Lk16 * 16;
+  for (int base = tid; base < nqk; base += kThreads * kBatch) {
+    float4 x[kBatch];
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+      const int e = base + i * kThreads;
+      x[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (e < nq) {
+        const int r = e >> 4;
+        if (q0 + r < L) x[i] = __ldg(reinterpret_cast<const float4*>(qg + (q0 + r) * rs + (e & 15) * 4));
+      } else if (e < nqk) {
+        const int r = (e - nq) >> 4;
+        if (r < L) x[i] = __ldg(reinterpret_cast<const float4*>(kg + r * rs + (e & 15) * 4));
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+      const int e = base + i * kThreads;
+      if (e < nq) split_store4(A, A + 32768, sw128_off4(e >> 4, (e & 15) * 4, QB), x[i]);
+      else if (e < nqk) split_store4(Bm, Bm + 65536, sw128_off4((e - nq) >> 4, (e & 15) * 4, Lk16), x[i]);
+    }
   }
   fence_proxy_async_smem();
   tc_fence_before();
@@ -132,6 +145,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mma_commit(&bar[0]);
   }
+  // V^T element e -> key j, dh group c4: a warp covers 32 consecutive keys of
+  // one 4-wide dh group (conflict-free transposed stores).
+  const int nv = Lk32 * 16;
+  auto v_load = [&](int e) {
+    const int j = (e & 31) + ((e >> 9) << 5), c4 = (e >> 5) & 15;
+    return (e < nv && j < L) ? __ldg(reinterpret_cast<const float4*>(vg + j * rs + c4 * 4))
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+  };
+  auto v_store = [&](int e, float4 x) {
+    if (e >= nv) return;
+    const int j = (e & 31) + ((e >> 9) << 5), c4 = (e >> 5) & 15;
+    const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t off = sw128_off4(c4 * 4 + i, j, DH);
+      const float hv = tf32_hi(xs[i]);
+      *reinterpret_cast<float*>(Bm + off) = hv;
+      *reinterpret_cast<float*>(Bm + 65536 + off) = __fsub_rn(xs[i], hv);
+    }
+  };
+  // The first V batch is fetched while the S MMAs run (K's region is only
+  // overwritten after they complete).
+  float4 vx[kBatch];
+#pragma unroll
+  for (int i = 0; i < kBatch; ++i) vx[i] = v_load(tid + i * kThreads);
+
   bool ok = block_wait(&bar[0], 0, status);
   tc_fence_after();
 
@@ -140,20 +179,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   float sum = 0.0f;
   if (ok) {
     // ---- 3a. V^T (hi/lo) over the consumed K region; keys >= L are zero.
-    // A warp covers 32 consecutive keys of one 4-wide dh group (conflict-free).
-    for (int e = tid; e < Lk32 * 16; e += kThreads) {
-      const int j = (e & 31) + ((e >> 9) << 5);
-      const int c4 = (e >> 5) & 15;
-      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (j < L) x = __ldg(reinterpret_cast<const float4*>(vg + j * rs + c4 * 4));
-      const float xs[4] = {x.x, x.y, x.z, x.w};
+    for (int base = tid;; base += kThreads * kBatch) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint32_t off = sw128_off4(c4 * 4 + i, j, DH);
-        const float hv = tf32_hi(xs[i]);
-        *reinterpret_cast<float*>(Bm + off) = hv;
-        *reinterpret_cast<float*>(Bm + 65536 + off) = __fsub_rn(xs[i], hv);
-      }
+      for (int i = 0; i < kBatch; ++i) v_store(base + i * kThreads, vx[i]);
+      const int next = base + kThreads * kBatch;
+      if (next >= nv) break;
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i) vx[i] = v_load(next + i * kThreads);
     }
     // ---- 3b. row max over the valid keys
     float mx = -INFINITY;

@@ -57,6 +57,28 @@ __device__ __forceinline__ float epi_row_run(const EpiParams& e, long m, int c0,
   return mx;
 }
 
+// The q-scale and RoPE of epi_qkv_rope_head on the values only (the caller
+// stores them); which = 0 (q), 1 (k), 2 (v).
+__device__ __forceinline__ void epi_qkv_rope_values(const EpiParams& e, long m, int which,
+                                                    float (&y)[64]) {
+  if (which == 0) {
+#pragma unroll
+    for (int j = 0; j < 64; ++j) y[j] = __fmul_rn(y[j], e.q_scale);
+  }
+  if (which <= 1) {
+    const int p = e.pos[m];
+    const float* c = e.cos_t + static_cast<long>(p) * 64;
+    const float* s = e.sin_t + static_cast<long>(p) * 64;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float lo = y[i], hi = y[i + 32];
+      const float ci = __ldg(c + i), si = __ldg(s + i);
+      y[i] = __fmaf_rn(-hi, si, __fmul_rn(lo, ci));
+      y[i + 32] = __fmaf_rn(hi, ci, __fmul_rn(lo, si));
+    }
+  }
+}
+
 // kEpiQkvRope for one 64-wide head chunk of row m starting at output column
 // n_base (a multiple of 64): q|k|v split by n_base / d, Q scaled before RoPE
 // (model.cpp:976-988), rotate-half RoPE in the AVX-512 form of rope.cpp:109-113

@@ -19,6 +19,7 @@
 #include <cudaTypedefs.h>
 
 #include <atomic>
+#include <cstring>
 
 #include "common.cuh"
 #include "epilogue.cuh"
@@ -38,7 +39,9 @@ struct Cfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  // Epilogue staging for TMA stores: 4 warps x 2 buffers x [32 rows x 128 B].
+  static constexpr int STAGING_BYTES = 4 * 2 * 4096;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 struct Params {
@@ -50,19 +53,24 @@ struct Params {
   EpiParams epi;
   uint32_t* status;
   int32_t* acc_out;
+  int tma;  // epilogue stores through TMA (tensor maps tmC0..2 valid)
 };
 
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA,
-                   const __grid_constant__ CUtensorMap tmB, const Params p) {
+                   const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmC0,
+                   const __grid_constant__ CUtensorMap tmC1,
+                   const __grid_constant__ CUtensorMap tmC2, const Params p) {
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + C::STAGES * C::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint8_t* staging = smem + C::STAGES * C::STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + C::STAGING_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
@@ -85,6 +93,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    if (p.tma) {
+      prefetch_tmap(&tmC0);
+      if (EPI == kEpiQkvRope) {
+        prefetch_tmap(&tmC1);
+        prefetch_tmap(&tmC2);
+      }
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -190,6 +205,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       float as = 1.0f;  // the raw-accumulator mode carries no activation scale
       if (row_ok && p.acc_out == nullptr) as = p.per_token ? __ldg(p.a_scale + m) : __ldg(p.a_scale);
 
+      // Dequant of one accumulator: fma(float(acc), ws[n]*as, bias[n])
+      // (gemm_int8.cpp:109-126); n clamped for the loads of tail columns.
+      auto deq = [&](uint32_t a, int n) {
+        n = min(n, p.N - 1);
+        return __fmaf_rn(__int2float_rn(static_cast<int>(a)), __fmul_rn(__ldg(p.w_scale + n), as),
+                         p.bias ? __ldg(p.bias + n) : 0.0f);
+      };
+      // This warp's staging buffers and the top row of its 32-row slab.
+      uint8_t* stg = staging + (warp - 2) * 8192;
+      const int y0 = m_blk * BM + quad * 32;
+      // Stage y[0..32) of this thread's row (lane) with the 128-byte swizzle
+      // the tensor map expects.
+      auto stage32 = [&](uint8_t* buf, const float* y) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          *reinterpret_cast<float4*>(buf + lane * 128 + ((j ^ (lane & 7)) * 16)) =
+              make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
+      };
+
       if (EPI == kEpiQkvRope) {
 #pragma unroll 1
         for (int c = 0; c < BN / 64; ++c) {
@@ -198,44 +232,78 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld32(t_row + c * 64 + 32, hi);
           tmem_ld_wait();
           const int n_base = n_blk * BN + c * 64;
-          if (row_ok && n_base < p.N) {
+          if (n_base < p.N) {  // warp-uniform
             float y[64];
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-              const int n0 = n_base + j, n1 = n_base + 32 + j;
-              y[j] = __fmaf_rn(__int2float_rn(static_cast<int>(lo[j])),
-                               __fmul_rn(__ldg(p.w_scale + n0), as),
-                               p.bias ? __ldg(p.bias + n0) : 0.0f);
-              y[32 + j] = __fmaf_rn(__int2float_rn(static_cast<int>(hi[j])),
-                                    __fmul_rn(__ldg(p.w_scale + n1), as),
-                                    p.bias ? __ldg(p.bias + n1) : 0.0f);
+              y[j] = deq(lo[j], n_base + j);
+              y[32 + j] = deq(hi[j], n_base + 32 + j);
             }
-            epi_qkv_rope_head(p.epi, m, n_base, y);
+            if (p.tma) {
+              const int which = n_base / p.epi.d;
+              const int col = n_base - which * p.epi.d;
+              epi_qkv_rope_values(p.epi, row_ok ? m : 0, which, y);
+              if (lane == 0) bulk_wait_read<0>();
+              __syncwarp();
+              stage32(stg, y);
+              stage32(stg + 4096, y + 32);
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                const CUtensorMap* mp = which == 0 ? &tmC0 : (which == 1 ? &tmC1 : &tmC2);
+                tma_store_2d(mp, stg, col, y0);
+                tma_store_2d(mp, stg + 4096, col + 32, y0);
+                bulk_commit();
+              }
+            } else if (row_ok) {
+              epi_qkv_rope_head(p.epi, m, n_base, y);
+            }
           }
         }
       } else {
+        int sb = 0;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t r[32];
           tmem_ld32(t_row + c * 32, r);
           tmem_ld_wait();
           const int n0 = n_blk * BN + c * 32;
-          if (row_ok && n0 < p.N) {
-            if (p.acc_out != nullptr) {
+          if (n0 >= p.N) continue;  // warp-uniform
+          if (p.acc_out != nullptr) {
+            if (row_ok)
               for (int j = 0; j < 32; ++j)
                 if (n0 + j < p.N) p.acc_out[m * p.N + n0 + j] = static_cast<int32_t>(r[j]);
-            } else {
-              float y[32];
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const int n = min(n0 + j, p.N - 1);
-                y[j] = __fmaf_rn(__int2float_rn(static_cast<int>(r[j])),
-                                 __fmul_rn(__ldg(p.w_scale + n), as),
-                                 p.bias ? __ldg(p.bias + n) : 0.0f);
-              }
-              amax = fmaxf(amax, epi_row_run<32>(p.epi, m, n0, p.N, y));
-            }
+            continue;
           }
+          float y[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) y[j] = deq(r[j], n0 + j);
+          if (!p.tma) {
+            if (row_ok) amax = fmaxf(amax, epi_row_run<32>(p.epi, m, n0, p.N, y));
+            continue;
+          }
+          if (p.epi.kind == kEpiGelu) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) y[j] = gelu_erf(y[j]);
+          }
+          if (row_ok && p.epi.amax != nullptr) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n0 + j < p.N) amax = fmaxf(amax, fabsf(y[j]));
+          }
+          uint8_t* buf = stg + sb * 4096;
+          if (lane == 0) bulk_wait_read<1>();  // the store that last used buf has read it
+          __syncwarp();
+          stage32(buf, y);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            // hidden += proj (fp32 add in the memory system: h + y rounded once)
+            if (p.epi.kind == kEpiResidual) tma_reduce_add_2d(&tmC0, buf, n0, y0);
+            else tma_store_2d(&tmC0, buf, n0, y0);
+            bulk_commit();
+          }
+          sb ^= 1;
         }
       }
       tc_fence_before();
@@ -245,6 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (acc == 0) acc_phase ^= 1u;
     }
     if (p.epi.amax != nullptr) amax_publish_warp(p.epi.amax, amax);
+    if (p.tma && lane == 0) bulk_wait<0>();  // stores done before the CTA retires
   }
 
   tc_fence_before();
@@ -286,12 +355,38 @@ bool make_tmap_i8(CUtensorMap* map, const int8_t* base, int rows, int cols, long
   return r == CUDA_SUCCESS;
 }
 
+// 2-D fp32 tensor [rows, cols] with row stride `ld` floats; box = 32 x 32
+// (128-byte rows, 128-byte swizzle) for the epilogue's TMA stores.
+bool make_tmap_f32(CUtensorMap* map, const float* base, long rows, long cols, long ld) {
+  auto fn = get_encode_fn();
+  if (fn == nullptr || base == nullptr || (ld & 3) || (reinterpret_cast<uintptr_t>(base) & 15))
+    return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 4)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int BN, int EPI>
 cudaError_t launch_bn(const GemmI8Args& a, cudaStream_t s) {
   using C = Cfg<BN>;
-  CUtensorMap tmA, tmB;
+  CUtensorMap tmA, tmB, tmC[3];
   if (!make_tmap_i8(&tmA, a.A, a.M, a.K, a.lda, BM)) return cudaErrorInvalidValue;
   if (!make_tmap_i8(&tmB, a.W, a.N, a.K, a.ldw, BN)) return cudaErrorInvalidValue;
+  std::memset(tmC, 0, sizeof(tmC));
+  bool tma = false;
+  if (a.acc_out == nullptr) {
+    if (EPI == kEpiQkvRope) {
+      tma = (a.epi.d % 32 == 0) && make_tmap_f32(&tmC[0], a.epi.q, a.M, a.epi.d, a.epi.d) &&
+            make_tmap_f32(&tmC[1], a.epi.k, a.M, a.epi.d, a.epi.d) &&
+            make_tmap_f32(&tmC[2], a.epi.v, a.M, a.epi.d, a.epi.d);
+    } else {
+      tma = make_tmap_f32(&tmC[0], a.epi.C, a.M, a.N, a.epi.ldc);
+    }
+  }
   // The opt-in shared-memory size is a per-device function attribute.
   static std::atomic<uint64_t> attr_set{0};
   int dev = 0;
@@ -314,9 +409,10 @@ cudaError_t launch_bn(const GemmI8Args& a, cudaStream_t s) {
   p.epi = a.epi;
   p.status = a.status;
   p.acc_out = a.acc_out;
+  p.tma = tma ? 1 : 0;
   const int tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
   const int grid = tiles < a.num_sms ? tiles : a.num_sms;
-  gemm_i8_kernel<BN, EPI><<<grid, kThreads, C::SMEM, s>>>(tmA, tmB, p);
+  gemm_i8_kernel<BN, EPI><<<grid, kThreads, C::SMEM, s>>>(tmA, tmB, tmC[0], tmC[1], tmC[2], p);
   return cudaGetLastError();
 }
 
