@@ -8,7 +8,7 @@
 // (not online) softmax -- row max over all keys, exponentials, sum -- then
 // out = (sum_j e_j v_j) / sum_j e_j.
 //
-// One CTA per (sequence, head, 128-query block), 128 threads, 1 CTA/SM:
+// One CTA per (sequence, head, 128-query block), 256 threads, 1 CTA/SM:
 //   1. Q [128 x 64] and K [L x 64] are loaded, split into tf32 hi/lo parts
 //      (hi = top 19 bits, lo = x - hi, exact) and written K-major with the
 //      128-byte swizzle.
@@ -16,12 +16,14 @@
 //      (kind::tf32, M=128, N=round16(L), 8 k-steps) into TMEM columns
 //      [0, 256); the dropped lo*lo term and lo truncation leave ~2^-21
 //      relative error per product, well inside the 1e-4 FP32 class.
-//   3. V^T (hi/lo) replaces K in shared memory.  Each thread owns one query
-//      row (= TMEM lane): row max over its S row, then for every 32-key chunk
-//      p = exp(s - max) -> P chunk (hi/lo, double-buffered) -> one thread
-//      issues O += P_chunk V^T_chunk (3xTF32, N=64) into TMEM [256, 320).
-//   4. O is read back, scaled by 1/sum and stored; absmax folded for the
-//      next GEMM's per-tensor activation scale.
+//   3. V^T (hi/lo) replaces K in shared memory.  Two warps share each TMEM
+//      lane quadrant (query rows); they split the 32-key chunks by parity:
+//      row max over the S row, then per pair of chunks p = exp(s - max) ->
+//      P chunks (hi/lo) in two buffers -> one thread issues
+//      O += P_chunk V^T_chunk (3xTF32, N=64) into TMEM [256, 320).
+//   4. O is read back (each warp of a quadrant one 32-column half), scaled
+//      by 1/sum and stored; absmax folded for the next GEMM's per-tensor
+//      activation scale.
 // Barrier waits are bounded and block-uniform (a timeout sets the status
 // word and the CTA skips to cleanup).
 #include <atomic>
@@ -36,8 +38,8 @@ constexpr int QB = 128;      // queries per CTA
 constexpr int DH = 64;       // head dim on this path
 constexpr int KMAX = 256;    // longest sequence on this path
 constexpr int KC = 32;       // keys per P.V chunk (one swizzle row of tf32)
-constexpr int kThreads = 128;
-constexpr int kBatch = 8;     // independent float4 loads in flight per thread
+constexpr int kThreads = 256;  // 8 warps: two per TMEM lane quadrant
+constexpr int kBatch = 4;     // independent float4 loads in flight per thread
 constexpr uint32_t kRegionA = 0;        // Q hi|lo (32K each) -> P buffers
 constexpr uint32_t kRegionB = 65536;    // K hi|lo (64K each) -> V^T hi|lo
 constexpr uint32_t kSmemUsed = 196608;
@@ -174,9 +176,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   bool ok = block_wait(&bar[0], 0, status);
   tc_fence_after();
 
-  const int row = warp * 32 + lane;  // query row in the block = TMEM lane
-  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-  float sum = 0.0f;
+  // Warp w reads TMEM lane quadrant (w % 4) = query rows 32*(w%4)..+31 and
+  // handles the 32-key chunks of parity par = w / 4 (even chunks go to P
+  // buffer 0, odd chunks to buffer 1, both filled in the same iteration).
+  __shared__ float red_max[2][QB], red_sum[2][QB];
+  const int qd = warp & 3, par = warp >> 2;
+  const int row = qd * 32 + lane;  // query row in the block = TMEM lane
+  const uint32_t lane_off = static_cast<uint32_t>(qd * 32) << 16;
+  const int npairs = (nchunk + 1) >> 1;
+  float total = 0.0f;
   if (ok) {
     // ---- 3a. V^T (hi/lo) over the consumed K region; keys >= L are zero.
     for (int base = tid;; base += kThreads * kBatch) {
@@ -187,9 +195,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int i = 0; i < kBatch; ++i) vx[i] = v_load(next + i * kThreads);
     }
-    // ---- 3b. row max over the valid keys
+    // ---- 3b. row max over the valid keys (each warp over its parity)
     float mx = -INFINITY;
-    for (int c = 0; c < nchunk; ++c) {
+    for (int c = par; c < nchunk; c += 2) {
       uint32_t r32[32];
       tmem_ld32(tS + lane_off + c * 32, r32);
       tmem_ld_wait();
@@ -197,29 +205,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < 32; ++j)
         if (c * 32 + j < L) mx = fmaxf(mx, __uint_as_float(r32[j]));
     }
+    red_max[par][row] = mx;
+    __syncthreads();
+    mx = fmaxf(red_max[0][row], red_max[1][row]);
     const float kLog2e = 1.4426950408889634f;
-    // ---- 3c. P chunks and O += P V^T
-    for (int c = 0; c < nchunk; ++c) {
-      const int buf = c & 1;
-      if (c >= 2 && !block_wait(&bar[1 + buf], ((c - 2) >> 1) & 1, status)) {
-        ok = false;
-        break;
-      }
-      uint32_t r32[32];
-      tmem_ld32(tS + lane_off + c * 32, r32);
-      tmem_ld_wait();
-      uint8_t* P = A + buf * 32768;
-#pragma unroll
-      for (int j4 = 0; j4 < 8; ++j4) {
-        float p4[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int j = j4 * 4 + i;
-          const float s = __uint_as_float(r32[j]);
-          p4[i] = (c * 32 + j < L) ? exp2f(__fmul_rn(__fsub_rn(s, mx), kLog2e)) : 0.0f;
-          sum = __fadd_rn(sum, p4[i]);
+    float sum = 0.0f;
+    // ---- 3c. P chunk pairs and O += P V^T
+    for (int it = 0; it < npairs; ++it) {
+      if (it > 0) {  // the MMAs of the previous pair released both buffers
+        const bool a = mbar_wait(&bar[1], (it - 1) & 1, status);
+        const bool b = (2 * (it - 1) + 1 >= nchunk) || mbar_wait(&bar[2], (it - 1) & 1, status);
+        if (__syncthreads_and(a && b ? 1 : 0) == 0) {
+          ok = false;
+          break;
         }
-        split_store4(P, P + 16384, sw128_off4(row, j4 * 4, QB), make_float4(p4[0], p4[1], p4[2], p4[3]));
+      }
+      const int c = 2 * it + par;
+      if (c < nchunk) {  // warp-uniform
+        uint32_t r32[32];
+        tmem_ld32(tS + lane_off + c * 32, r32);
+        tmem_ld_wait();
+        uint8_t* P = A + par * 32768;
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4) {
+          float p4[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int j = j4 * 4 + i;
+            const float sv = __uint_as_float(r32[j]);
+            p4[i] = (c * 32 + j < L) ? exp2f(__fmul_rn(__fsub_rn(sv, mx), kLog2e)) : 0.0f;
+            sum = __fadd_rn(sum, p4[i]);
+          }
+          split_store4(P, P + 16384, sw128_off4(row, j4 * 4, QB), make_float4(p4[0], p4[1], p4[2], p4[3]));
+        }
       }
       fence_proxy_async_smem();
       tc_fence_before();
@@ -227,43 +245,49 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       if (tid == 0) {
         const uint32_t idO = idesc_tf32(QB, DH);
-        const uint32_t p_hi = smem_u32(P), p_lo = p_hi + 16384;
-        const uint32_t v_hi = smem_u32(Bm) + static_cast<uint32_t>(c * DH * 128), v_lo = v_hi + 65536;
+        for (int pc = 0; pc < 2 && 2 * it + pc < nchunk; ++pc) {
+          const int cc = 2 * it + pc;
+          const uint32_t p_hi = smem_u32(A) + pc * 32768, p_lo = p_hi + 16384;
+          const uint32_t v_hi = smem_u32(Bm) + static_cast<uint32_t>(cc * DH * 128), v_lo = v_hi + 65536;
 #pragma unroll
-        for (int kk = 0; kk < KC / 8; ++kk) {
-          const uint32_t o = kk * 32;
-          mma_tf32(tO, sw128_kmajor_desc(p_hi + o), sw128_kmajor_desc(v_hi + o), idO,
-                   (c | kk) != 0 ? 1u : 0u);
-          mma_tf32(tO, sw128_kmajor_desc(p_hi + o), sw128_kmajor_desc(v_lo + o), idO, 1u);
-          mma_tf32(tO, sw128_kmajor_desc(p_lo + o), sw128_kmajor_desc(v_hi + o), idO, 1u);
+          for (int kk = 0; kk < KC / 8; ++kk) {
+            const uint32_t o = kk * 32;
+            mma_tf32(tO, sw128_kmajor_desc(p_hi + o), sw128_kmajor_desc(v_hi + o), idO,
+                     (cc | kk) != 0 ? 1u : 0u);
+            mma_tf32(tO, sw128_kmajor_desc(p_hi + o), sw128_kmajor_desc(v_lo + o), idO, 1u);
+            mma_tf32(tO, sw128_kmajor_desc(p_lo + o), sw128_kmajor_desc(v_hi + o), idO, 1u);
+          }
+          mma_commit(&bar[1 + pc]);
         }
-        mma_commit(&bar[1 + buf]);
       }
     }
-    if (ok) ok = block_wait(&bar[1 + ((nchunk - 1) & 1)], ((nchunk - 1) >> 1) & 1, status);
+    if (ok) {  // the last pair's MMAs (and so all of them) are done
+      const int it = npairs - 1;
+      const bool a = mbar_wait(&bar[1], it & 1, status);
+      const bool b = (2 * it + 1 >= nchunk) || mbar_wait(&bar[2], it & 1, status);
+      ok = __syncthreads_and(a && b ? 1 : 0) != 0;
+    }
+    red_sum[par][row] = sum;
+    __syncthreads();
+    total = __fadd_rn(red_sum[0][row], red_sum[1][row]);
   }
 
   float mx_out = 0.0f;
   if (ok) {
-    // ---- 4. O / sum -> out
+    // ---- 4. O / sum -> out; warp parity picks the 32-column half of O.
     tc_fence_after();
-    uint32_t o0[32], o1[32];
-    tmem_ld32(tO + lane_off, o0);
-    tmem_ld32(tO + lane_off + 32, o1);
+    uint32_t o[32];
+    tmem_ld32(tO + lane_off + par * 32, o);
     tmem_ld_wait();
     if (q0 + row < L) {
-      const float inv = __fdiv_rn(1.0f, sum);
-      float* op = out + (static_cast<long>(s0) + q0 + row) * rs + h * DH;
+      const float inv = __fdiv_rn(1.0f, total);
+      float* op = out + (static_cast<long>(s0) + q0 + row) * rs + h * DH + par * 32;
 #pragma unroll
       for (int j = 0; j < 32; j += 4) {
-        const float4 a = make_float4(__fmul_rn(__uint_as_float(o0[j]), inv), __fmul_rn(__uint_as_float(o0[j + 1]), inv),
-                                     __fmul_rn(__uint_as_float(o0[j + 2]), inv), __fmul_rn(__uint_as_float(o0[j + 3]), inv));
-        const float4 c = make_float4(__fmul_rn(__uint_as_float(o1[j]), inv), __fmul_rn(__uint_as_float(o1[j + 1]), inv),
-                                     __fmul_rn(__uint_as_float(o1[j + 2]), inv), __fmul_rn(__uint_as_float(o1[j + 3]), inv));
+        const float4 a = make_float4(__fmul_rn(__uint_as_float(o[j]), inv), __fmul_rn(__uint_as_float(o[j + 1]), inv),
+                                     __fmul_rn(__uint_as_float(o[j + 2]), inv), __fmul_rn(__uint_as_float(o[j + 3]), inv));
         *reinterpret_cast<float4*>(op + j) = a;
-        *reinterpret_cast<float4*>(op + 32 + j) = c;
         mx_out = fmaxf(mx_out, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
-        mx_out = fmaxf(mx_out, fmaxf(fmaxf(fabsf(c.x), fabsf(c.y)), fmaxf(fabsf(c.z), fabsf(c.w))));
       }
     }
     if (amax != nullptr) amax_publish(amax, mx_out);  // ok is block-uniform

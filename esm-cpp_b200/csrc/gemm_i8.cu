@@ -37,11 +37,14 @@ struct Cfg {
   static constexpr int A_BYTES = BM * BK;
   static constexpr int B_BYTES = BN * BK;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr int STAGES = (BN == 256) ? 3 : (BN == 128 ? 5 : 7);
   static constexpr int TMEM_COLS = 2 * BN;
-  // Epilogue staging for TMA stores: 4 warps x 2 buffers x [32 rows x 128 B].
+  // Epilogue staging for TMA stores: 4 warps x 2 buffers x [32 rows x 128 B],
+  // then per-warp copies of the tile's w_scale and bias columns.
   static constexpr int STAGING_BYTES = 4 * 2 * 4096;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int COLVEC_BYTES = 4 * 2 * BN * 4;
+  static constexpr int SMEM =
+      STAGES * STAGE_BYTES + STAGING_BYTES + COLVEC_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 struct Params {
@@ -70,7 +73,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + C::STAGES * C::A_BYTES;
   uint8_t* staging = smem + C::STAGES * C::STAGE_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(staging + C::STAGING_BYTES);
+  float* colvec = reinterpret_cast<float*>(staging + C::STAGING_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + C::STAGING_BYTES + C::COLVEC_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
@@ -205,12 +209,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       float as = 1.0f;  // the raw-accumulator mode carries no activation scale
       if (row_ok && p.acc_out == nullptr) as = p.per_token ? __ldg(p.a_scale + m) : __ldg(p.a_scale);
 
-      // Dequant of one accumulator: fma(float(acc), ws[n]*as, bias[n])
-      // (gemm_int8.cpp:109-126); n clamped for the loads of tail columns.
-      auto deq = [&](uint32_t a, int n) {
-        n = min(n, p.N - 1);
-        return __fmaf_rn(__int2float_rn(static_cast<int>(a)), __fmul_rn(__ldg(p.w_scale + n), as),
-                         p.bias ? __ldg(p.bias + n) : 0.0f);
+      // This tile's w_scale / bias columns, copied once into the warp's own
+      // shared-memory vectors (tail columns read the last valid column).
+      float* wsv = colvec + (warp - 2) * 2 * BN;
+      float* bsv = wsv + BN;
+      if (p.acc_out == nullptr) {
+        for (int j = lane; j < BN; j += 32) {
+          const int n = min(n_blk * BN + j, p.N - 1);
+          wsv[j] = __ldg(p.w_scale + n);
+          bsv[j] = p.bias ? __ldg(p.bias + n) : 0.0f;
+        }
+      }
+      __syncwarp();
+      // Dequant of one accumulator at tile column jc: fma(float(acc),
+      // ws[n]*as, bias[n]) (gemm_int8.cpp:109-126).
+      auto deq = [&](uint32_t a, int jc) {
+        return __fmaf_rn(__int2float_rn(static_cast<int>(a)), __fmul_rn(wsv[jc], as), bsv[jc]);
       };
       // This warp's staging buffers and the top row of its 32-row slab.
       uint8_t* stg = staging + (warp - 2) * 8192;
@@ -236,8 +250,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             float y[64];
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-              y[j] = deq(lo[j], n_base + j);
-              y[32 + j] = deq(hi[j], n_base + 32 + j);
+              y[j] = deq(lo[j], c * 64 + j);
+              y[32 + j] = deq(hi[j], c * 64 + 32 + j);
             }
             if (p.tma) {
               const int which = n_base / p.epi.d;
@@ -277,7 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           float y[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) y[j] = deq(r[j], n0 + j);
+          for (int j = 0; j < 32; ++j) y[j] = deq(r[j], c * 32 + j);
           if (!p.tma) {
             if (row_ok) amax = fmaxf(amax, epi_row_run<32>(p.epi, m, n0, p.N, y));
             continue;
@@ -307,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       tc_fence_before();
-      __syncwarp();
+      __syncwarp();  // also: every lane is done with this tile's column vectors
       if (lane == 0) mbar_arrive(&tempty[acc]);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;

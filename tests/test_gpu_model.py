@@ -27,6 +27,8 @@ def _close(got, want, tol=1e-4):
 
 
 W8A8_PEARSON = 0.9999
+# One flipped int8 code moves a tiny model's logits by ~1e-2.
+W8A8_ATOL = 5e-2
 
 
 def _pearson_each(got, want, cu, thr=W8A8_PEARSON):
@@ -88,7 +90,7 @@ def test_w8a8_packed_matches_oracle(tiny_q8, O):
     got = tiny_q8.forward_packed(ids, cu, out=np.empty((ids.size, 33), np.float32))
     want = O.forward_packed(tiny_q8, ids, cu)
     _pearson_each(got, want, cu)
-    np.testing.assert_allclose(got, want, rtol=1e-3, atol=1e-2)
+    np.testing.assert_allclose(got, want, rtol=1e-3, atol=W8A8_ATOL)
 
 
 def test_w8a8_packed_matches_reference_via_gguf(tiny_q8, O, R, tmp_path):
@@ -104,7 +106,7 @@ def test_w8a8_packed_matches_reference_via_gguf(tiny_q8, O, R, tmp_path):
         O.ref_force_isa(None)
     got = tiny_q8.forward_packed(ids, cu, out=np.empty((ids.size, 33), np.float32))
     _pearson_each(got, want, cu)
-    np.testing.assert_allclose(got, want, rtol=1e-3, atol=1e-2)
+    np.testing.assert_allclose(got, want, rtol=1e-3, atol=W8A8_ATOL)
 
 
 def test_gguf_round_trip_of_reference_artefact(tiny_fp32, O, R, tmp_path):
@@ -130,7 +132,7 @@ def test_gguf_round_trip_of_reference_artefact(tiny_fp32, O, R, tmp_path):
         O.ref_force_isa(None)
     got = m.forward_packed(ids, cu, out=np.empty((ids.size, 33), np.float32))
     _pearson_each(got, want, cu)
-    np.testing.assert_allclose(got, want, rtol=1e-3, atol=1e-2)
+    np.testing.assert_allclose(got, want, rtol=1e-3, atol=W8A8_ATOL)
     m.close()
 
 
@@ -203,7 +205,7 @@ def test_forward_scheduled_matches_reference(tiny_q8, O, R, tmp_path):
         if g.size > 33:
             r = np.corrcoef(g.ravel(), w.ravel())[0, 1]
             assert r >= W8A8_PEARSON
-        np.testing.assert_allclose(g, w, rtol=1e-3, atol=1e-2)
+        np.testing.assert_allclose(g, w, rtol=1e-3, atol=W8A8_ATOL)
 
 
 def test_per_token_mode_matches_oracle(cuda, O):
@@ -216,7 +218,7 @@ def test_per_token_mode_matches_oracle(cuda, O):
     got = m.forward_packed(ids, cu, out=np.empty((ids.size, 33), np.float32))
     want = O.forward_packed(m, ids, cu, per_token=True)
     _pearson_each(got, want, cu)
-    np.testing.assert_allclose(got, want, rtol=1e-3, atol=1e-2)
+    np.testing.assert_allclose(got, want, rtol=1e-3, atol=W8A8_ATOL)
     m.close()
 
 
