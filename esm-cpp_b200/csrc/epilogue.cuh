@@ -66,15 +66,20 @@ __device__ __forceinline__ void epi_qkv_rope_values(const EpiParams& e, long m, 
     for (int j = 0; j < 64; ++j) y[j] = __fmul_rn(y[j], e.q_scale);
   }
   if (which <= 1) {
-    const int p = e.pos[m];
-    const float* c = e.cos_t + static_cast<long>(p) * 64;
-    const float* s = e.sin_t + static_cast<long>(p) * 64;
+    const int p = __ldg(e.pos + m);
+    const float4* c4 = reinterpret_cast<const float4*>(e.cos_t + static_cast<long>(p) * 64);
+    const float4* s4 = reinterpret_cast<const float4*>(e.sin_t + static_cast<long>(p) * 64);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const float lo = y[i], hi = y[i + 32];
-      const float ci = __ldg(c + i), si = __ldg(s + i);
-      y[i] = __fmaf_rn(-hi, si, __fmul_rn(lo, ci));
-      y[i + 32] = __fmaf_rn(hi, ci, __fmul_rn(lo, si));
+    for (int i4 = 0; i4 < 8; ++i4) {
+      const float4 cv = __ldg(c4 + i4), sv = __ldg(s4 + i4);
+      const float cc[4] = {cv.x, cv.y, cv.z, cv.w}, ss[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int i = 4 * i4 + k;
+        const float lo = y[i], hi = y[i + 32];
+        y[i] = __fmaf_rn(-hi, ss[k], __fmul_rn(lo, cc[k]));
+        y[i + 32] = __fmaf_rn(hi, cc[k], __fmul_rn(lo, ss[k]));
+      }
     }
   }
 }

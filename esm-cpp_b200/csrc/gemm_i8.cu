@@ -37,11 +37,11 @@ struct Cfg {
   static constexpr int A_BYTES = BM * BK;
   static constexpr int B_BYTES = BN * BK;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN == 256) ? 3 : (BN == 128 ? 5 : 7);
+  static constexpr int STAGES = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
   static constexpr int TMEM_COLS = 2 * BN;
-  // Epilogue staging for TMA stores: 4 warps x 2 buffers x [32 rows x 128 B],
-  // then per-warp copies of the tile's w_scale and bias columns.
-  static constexpr int STAGING_BYTES = 4 * 2 * 4096;
+  // Epilogue staging for TMA stores: 4 warps x [32 rows x 128 B], then
+  // per-warp copies of the tile's (w_scale * a_scale) and bias columns.
+  static constexpr int STAGING_BYTES = 4 * 4096;
   static constexpr int COLVEC_BYTES = 4 * 2 * BN * 4;
   static constexpr int SMEM =
       STAGES * STAGE_BYTES + STAGING_BYTES + COLVEC_BYTES + 1024 /*align*/ + 256 /*barriers*/;
@@ -213,10 +213,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       // shared-memory vectors (tail columns read the last valid column).
       float* wsv = colvec + (warp - 2) * 2 * BN;
       float* bsv = wsv + BN;
+      // Per-tensor scale: ws[n]*as is the same for every row, so the rounded
+      // product (the reference rounds it before the fma) is formed once.
+      const float as_col = p.per_token ? 1.0f : (p.acc_out ? 1.0f : __ldg(p.a_scale));
       if (p.acc_out == nullptr) {
         for (int j = lane; j < BN; j += 32) {
           const int n = min(n_blk * BN + j, p.N - 1);
-          wsv[j] = __ldg(p.w_scale + n);
+          wsv[j] = p.per_token ? __ldg(p.w_scale + n) : __fmul_rn(__ldg(p.w_scale + n), as_col);
           bsv[j] = p.bias ? __ldg(p.bias + n) : 0.0f;
         }
       }
@@ -224,10 +227,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Dequant of one accumulator at tile column jc: fma(float(acc),
       // ws[n]*as, bias[n]) (gemm_int8.cpp:109-126).
       auto deq = [&](uint32_t a, int jc) {
-        return __fmaf_rn(__int2float_rn(static_cast<int>(a)), __fmul_rn(wsv[jc], as), bsv[jc]);
+        const float sc = p.per_token ? __fmul_rn(wsv[jc], as) : wsv[jc];
+        return __fmaf_rn(__int2float_rn(static_cast<int>(a)), sc, bsv[jc]);
       };
-      // This warp's staging buffers and the top row of its 32-row slab.
-      uint8_t* stg = staging + (warp - 2) * 8192;
+      // This warp's staging buffer and the top row of its 32-row slab.
+      uint8_t* stg = staging + (warp - 2) * 4096;
       const int y0 = m_blk * BM + quad * 32;
       // Stage y[0..32) of this thread's row (lane) with the 128-byte swizzle
       // the tensor map expects.
@@ -236,6 +240,46 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < 8; ++j)
           *reinterpret_cast<float4*>(buf + lane * 128 + ((j ^ (lane & 7)) * 16)) =
               make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
+      };
+
+      // One 32-column chunk of the plain epilogues (store / residual / GELU /
+      // raw int32), from accumulators already in registers.
+      auto epi_chunk = [&](int c, const uint32_t(&r)[32]) {
+        const int n0 = n_blk * BN + c * 32;
+        if (n0 >= p.N) return;  // warp-uniform
+        if (p.acc_out != nullptr) {
+          if (row_ok)
+            for (int j = 0; j < 32; ++j)
+              if (n0 + j < p.N) p.acc_out[m * p.N + n0 + j] = static_cast<int32_t>(r[j]);
+          return;
+        }
+        float y[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) y[j] = deq(r[j], c * 32 + j);
+        if (!p.tma) {
+          if (row_ok) amax = fmaxf(amax, epi_row_run<32>(p.epi, m, n0, p.N, y));
+          return;
+        }
+        if (p.epi.kind == kEpiGelu) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) y[j] = gelu_erf(y[j]);
+        }
+        if (row_ok && p.epi.amax != nullptr) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n0 + j < p.N) amax = fmaxf(amax, fabsf(y[j]));
+        }
+        if (lane == 0) bulk_wait_read<0>();  // the buffer's last store has read it
+        __syncwarp();
+        stage32(stg, y);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          // hidden += proj (fp32 add in the memory system: h + y rounded once)
+          if (p.epi.kind == kEpiResidual) tma_reduce_add_2d(&tmC0, stg, n0, y0);
+          else tma_store_2d(&tmC0, stg, n0, y0);
+          bulk_commit();
+        }
       };
 
       if (EPI == kEpiQkvRope) {
@@ -257,17 +301,18 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int which = n_base / p.epi.d;
               const int col = n_base - which * p.epi.d;
               epi_qkv_rope_values(p.epi, row_ok ? m : 0, which, y);
-              if (lane == 0) bulk_wait_read<0>();
-              __syncwarp();
-              stage32(stg, y);
-              stage32(stg + 4096, y + 32);
-              fence_proxy_async_smem();
-              __syncwarp();
-              if (lane == 0) {
-                const CUtensorMap* mp = which == 0 ? &tmC0 : (which == 1 ? &tmC1 : &tmC2);
-                tma_store_2d(mp, stg, col, y0);
-                tma_store_2d(mp, stg + 4096, col + 32, y0);
-                bulk_commit();
+              const CUtensorMap* mp = which == 0 ? &tmC0 : (which == 1 ? &tmC1 : &tmC2);
+#pragma unroll
+              for (int half = 0; half < 2; ++half) {
+                if (lane == 0) bulk_wait_read<0>();  // the buffer's last store has read it
+                __syncwarp();
+                stage32(stg, y + 32 * half);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                  tma_store_2d(mp, stg, col + 32 * half, y0);
+                  bulk_commit();
+                }
               }
             } else if (row_ok) {
               epi_qkv_rope_head(p.epi, m, n_base, y);
@@ -275,49 +320,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else {
-        int sb = 0;
+        // TMEM loads run one chunk ahead of the dequant / store of the
+        // previous chunk (two register buffers, manually unrolled).
+        uint32_t ra[32], rb[32];
+        tmem_ld32(t_row, ra);
+        tmem_ld_wait();
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(t_row + c * 32, r);
+        for (int c = 0; c < BN / 32; c += 2) {
+          tmem_ld32(t_row + (c + 1) * 32, rb);
+          epi_chunk(c, ra);
           tmem_ld_wait();
-          const int n0 = n_blk * BN + c * 32;
-          if (n0 >= p.N) continue;  // warp-uniform
-          if (p.acc_out != nullptr) {
-            if (row_ok)
-              for (int j = 0; j < 32; ++j)
-                if (n0 + j < p.N) p.acc_out[m * p.N + n0 + j] = static_cast<int32_t>(r[j]);
-            continue;
-          }
-          float y[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) y[j] = deq(r[j], c * 32 + j);
-          if (!p.tma) {
-            if (row_ok) amax = fmaxf(amax, epi_row_run<32>(p.epi, m, n0, p.N, y));
-            continue;
-          }
-          if (p.epi.kind == kEpiGelu) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) y[j] = gelu_erf(y[j]);
-          }
-          if (row_ok && p.epi.amax != nullptr) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (n0 + j < p.N) amax = fmaxf(amax, fabsf(y[j]));
-          }
-          uint8_t* buf = stg + sb * 4096;
-          if (lane == 0) bulk_wait_read<1>();  // the store that last used buf has read it
-          __syncwarp();
-          stage32(buf, y);
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            // hidden += proj (fp32 add in the memory system: h + y rounded once)
-            if (p.epi.kind == kEpiResidual) tma_reduce_add_2d(&tmC0, buf, n0, y0);
-            else tma_store_2d(&tmC0, buf, n0, y0);
-            bulk_commit();
-          }
-          sb ^= 1;
+          if (c + 2 < BN / 32) tmem_ld32(t_row + (c + 2) * 32, ra);
+          epi_chunk(c + 1, rb);
+          tmem_ld_wait();
         }
       }
       tc_fence_before();
