@@ -30,19 +30,20 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 128;  // bytes of K per stage = one 128-byte swizzle row
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;    // producer, MMA issuer, 8 epilogue warps
+constexpr int kEpiWarps = 8;
 
 template <int BN>
 struct Cfg {
   static constexpr int A_BYTES = BM * BK;
   static constexpr int B_BYTES = BN * BK;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr int STAGES = (BN == 256) ? 3 : (BN == 128 ? 5 : 7);
   static constexpr int TMEM_COLS = 2 * BN;
-  // Epilogue staging for TMA stores: 4 warps x [32 rows x 128 B], then
-  // per-warp copies of the tile's (w_scale * a_scale) and bias columns.
-  static constexpr int STAGING_BYTES = 4 * 4096;
-  static constexpr int COLVEC_BYTES = 4 * 2 * BN * 4;
+  // Epilogue staging for TMA stores: 8 warps x [32 rows x 128 B], then the
+  // tile's (w_scale * a_scale) and bias columns shared by the epilogue warps.
+  static constexpr int STAGING_BYTES = kEpiWarps * 4096;
+  static constexpr int COLVEC_BYTES = 2 * BN * 4;
   static constexpr int SMEM =
       STAGES * STAGE_BYTES + STAGING_BYTES + COLVEC_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
@@ -58,6 +59,26 @@ struct Params {
   int32_t* acc_out;
   int tma;  // epilogue stores through TMA (tensor maps tmC0..2 valid)
 };
+
+// Named barrier 1 across the kEpiWarps epilogue warps only.
+__device__ __forceinline__ void epi_barrier() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
+}
+// The same barrier with an AND-vote: every epilogue warp gets the same answer,
+// so a timeout leaves the loop in all of them together (none is left waiting
+// at a later barrier).
+__device__ __forceinline__ bool epi_all(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "barrier.cta.red.and.pred po, 1, %2, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(r)
+      : "r"(v ? 1u : 0u), "n"(kEpiWarps * 32)
+      : "memory");
+  return r != 0;
+}
 
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -90,7 +111,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);  // one arrive per epilogue warp
+      mbar_init(&tempty[a], kEpiWarps);  // one arrive per epilogue warp
     }
     fence_barrier_init();
   }
@@ -192,7 +213,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // --------------------------------------------------------- epilogue
-    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    // Warps 2..9: TMEM lane quadrant warp % 4 (the hardware rule), and the
+    // column half `half`: the two warps of a quadrant take alternate chunks.
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int etid = (warp - 2) * 32 + lane;  // 0..255 among epilogue threads
     const int row_in_tile = quad * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -200,7 +225,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       const int m_blk = tile % m_blocks;
       const int n_blk = tile / m_blocks;
-      if (!mbar_wait(&tfull[acc], acc_phase, p.status)) break;
+      if (!epi_all(mbar_wait(&tfull[acc], acc_phase, p.status))) break;
       tc_fence_after();
       const long m = static_cast<long>(m_blk) * BM + row_in_tile;
       const bool row_ok = m < p.M;
@@ -209,21 +234,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       float as = 1.0f;  // the raw-accumulator mode carries no activation scale
       if (row_ok && p.acc_out == nullptr) as = p.per_token ? __ldg(p.a_scale + m) : __ldg(p.a_scale);
 
-      // This tile's w_scale / bias columns, copied once into the warp's own
-      // shared-memory vectors (tail columns read the last valid column).
-      float* wsv = colvec + (warp - 2) * 2 * BN;
-      float* bsv = wsv + BN;
+      // This tile's w_scale / bias columns, copied once into shared memory by
+      // the epilogue warps (tail columns read the last valid column).
+      float* wsv = colvec;
+      float* bsv = colvec + BN;
       // Per-tensor scale: ws[n]*as is the same for every row, so the rounded
       // product (the reference rounds it before the fma) is formed once.
       const float as_col = p.per_token ? 1.0f : (p.acc_out ? 1.0f : __ldg(p.a_scale));
       if (p.acc_out == nullptr) {
-        for (int j = lane; j < BN; j += 32) {
+        for (int j = etid; j < BN; j += kEpiWarps * 32) {
           const int n = min(n_blk * BN + j, p.N - 1);
           wsv[j] = p.per_token ? __ldg(p.w_scale + n) : __fmul_rn(__ldg(p.w_scale + n), as_col);
           bsv[j] = p.bias ? __ldg(p.bias + n) : 0.0f;
         }
       }
-      __syncwarp();
+      epi_barrier();  // vectors filled
       // Dequant of one accumulator at tile column jc: fma(float(acc),
       // ws[n]*as, bias[n]) (gemm_int8.cpp:109-126).
       auto deq = [&](uint32_t a, int jc) {
@@ -284,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       if (EPI == kEpiQkvRope) {
 #pragma unroll 1
-        for (int c = 0; c < BN / 64; ++c) {
+        for (int c = half; c < BN / 64; c += 2) {
           uint32_t lo[32], hi[32];
           tmem_ld32(t_row + c * 64, lo);
           tmem_ld32(t_row + c * 64 + 32, hi);
@@ -320,24 +345,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else {
-        // TMEM loads run one chunk ahead of the dequant / store of the
-        // previous chunk (two register buffers, manually unrolled).
+        // This warp's chunks are half, half+2, ...; the TMEM load of the next
+        // one runs while the previous one is dequantised and stored.
+        constexpr int NC = BN / 64;  // chunks per warp (>= 1)
         uint32_t ra[32], rb[32];
-        tmem_ld32(t_row, ra);
+        tmem_ld32(t_row + half * 32, ra);
         tmem_ld_wait();
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; c += 2) {
-          tmem_ld32(t_row + (c + 1) * 32, rb);
-          epi_chunk(c, ra);
+        for (int i = 0; i < NC; i += 2) {
+          const int c0 = half + 2 * i;
+          if (i + 1 < NC) tmem_ld32(t_row + (c0 + 2) * 32, rb);
+          epi_chunk(c0, ra);
           tmem_ld_wait();
-          if (c + 2 < BN / 32) tmem_ld32(t_row + (c + 2) * 32, ra);
-          epi_chunk(c + 1, rb);
-          tmem_ld_wait();
+          if (i + 1 < NC) {
+            if (i + 2 < NC) tmem_ld32(t_row + (c0 + 4) * 32, ra);
+            epi_chunk(c0 + 2, rb);
+            tmem_ld_wait();
+          }
         }
       }
       tc_fence_before();
-      __syncwarp();  // also: every lane is done with this tile's column vectors
+      __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
+      epi_barrier();  // every epilogue warp is done with this tile's vectors
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
