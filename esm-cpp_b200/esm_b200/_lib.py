@@ -73,6 +73,8 @@ _SIGS = {
     "esmcu_linear": (C.c_int, [_VP, _VP, _VP, _VP, _VP, C.c_int, C.c_int, C.c_int]),
     "esmcu_linear_int8": (C.c_int, [_VP, _VP, _VP, _VP, _VP, _VP, C.c_int, C.c_int, C.c_int,
                                     C.c_int]),
+    "esmcu_linear_int8_noalloc": (C.c_int, [_VP, _VP, _VP, _VP, _VP, _VP, C.c_int, C.c_int,
+                                            C.c_int, C.c_int]),
     "esmcu_quantize_activations": (C.c_int, [_VP, _VP, C.c_int, C.c_int, _VP, C.c_int, _VP,
                                              C.c_int]),
     "esmcu_gemm_int8_s32": (C.c_int, [_VP, _VP, C.c_int, _VP, C.c_int, _VP, C.c_int, C.c_int,

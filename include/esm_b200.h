@@ -91,6 +91,20 @@ int esmcu_linear_int8(esmcu_context* ctx, const float* A, const int8_t* W,
                       const float* w_scales, const float* bias, float* C, int M, int N, int K,
                       int act_quant);
 
+/* No counterpart in the reference.  esmcu_linear_int8 without any device
+ * allocation, for callers that cannot let the library call cudaMalloc (a
+ * process whose HBM is all handed to its own pool, or one that cannot take
+ * the synchronisation an allocation implies).  Same arguments and results;
+ * its scratch is one fixed 16 MiB array per device, built into the library,
+ * so 256 + 4*M (to 256) + M*ldq (+ N*ldq when K % 16 != 0) bytes must fit,
+ * ldq = K rounded up to 16, else ESMCU_ERR_OUT_OF_RANGE.  All calls on a
+ * device share that array: calls that overlap on the GPU race.  The first
+ * call on a device looks up the array's address; make it before any stream
+ * capture. */
+int esmcu_linear_int8_noalloc(esmcu_context* ctx, const float* A, const int8_t* W,
+                              const float* w_scales, const float* bias, float* C, int M, int N,
+                              int K, int act_quant);
+
 /* The two halves of LinearInt8, exposed for the bit-exact parity gates.
  * esmcu_quantize_activations: QuantizeActPrefixAvx512 (gemm_int8.cpp:391-508)
  * in its symmetric s8 form q = clamp(rne(A*(1/s)), +-127), q_out [M, ldq]
