@@ -158,6 +158,13 @@ __global__ void __maxnreg__(168)
     // of one 4-wide dh group (conflict-free transposed stores).
     auto v_key = [](int e) { return (e & 31) + ((e >> 9) << 5); };
     auto v_c4 = [](int e) { return (e >> 5) & 15; };
+    // Row-major staging in region A (free once S is done) for V on its way
+    // in and O on its way out: 256-byte rows, 16-byte group c4 of row j at
+    // slot c4 ^ (j & 15), conflict-free both for a warp covering two whole
+    // rows and for one covering 32 rows at one c4.
+    auto stage_off = [](int j, int c4) {
+      return static_cast<uint32_t>(j * 256 + ((c4 ^ (j & 15)) << 4));
+    };
     // Q block and the first 128 K rows of item w.
     auto prefetch = [&](const Item& w, float4 (&x)[16]) {
       const long base = static_cast<long>(w.s0) * rs + w.h * DH;
@@ -223,25 +230,30 @@ __global__ void __maxnreg__(168)
       tc_fence_after();
       const uint32_t tmem = *tslot;
 
-      // V (all Lk32 keys) while S runs.
-      const int nv = Lk32 * 16;
+      // V rows [0, Lk32) while S runs, row-coalesced (16 threads per row).
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        const int e = tid + i * kSoftThreads;
-        const int j = v_key(e);
-        x[i] = (e < nv && j < L)
-                   ? __ldg(reinterpret_cast<const float4*>(v + base + j * rs + v_c4(e) * 4))
-                   : make_float4(0.f, 0.f, 0.f, 0.f);
+        const int r = lrow + i * 16;
+        x[i] = r < L ? __ldg(reinterpret_cast<const float4*>(v + base + r * rs + col4))
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
       }
       if (ok) ok = mbar_wait(&bar[0], nS & 1, status);
       ++nS;
       tc_fence_after();
 
-      // ---- 3a. V^T (hi/lo) over the consumed K region; keys >= L are zero.
+      // ---- 3a. V -> staging (region A, Q consumed) -> V^T (hi/lo) over the
+      // consumed K region; keys >= L are zero.
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int r = lrow + i * 16;
+        if (r < Lk32) *reinterpret_cast<float4*>(A + stage_off(r, col4 >> 2)) = x[i];
+      }
+      soft_sync();
+      const int nv = Lk32 * 16;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const int e = tid + i * kSoftThreads;
-        if (e < nv) vt_store(e, x[i]);
+        if (e < nv) vt_store(e, *reinterpret_cast<const float4*>(A + stage_off(v_key(e), v_c4(e))));
       }
       fence_proxy_async_smem();
       // Next item's loads fly during this item's softmax and P.V.
@@ -309,16 +321,28 @@ __global__ void __maxnreg__(168)
       uint32_t o[32];
       tmem_ld32(tmem + kColO + lane_off + par * 32, o);
       tmem_ld_wait();
-      if (ok && q0 + row < L) {
+      {  // O / sum -> staging (region A) -> row-coalesced stores
         const float inv = __fdiv_rn(1.0f, total);
-        float* op = out + base + static_cast<long>(q0 + row) * rs + par * 32;
+        const bool live = q0 + row < L;
 #pragma unroll
         for (int j = 0; j < 32; j += 4) {
           const float4 a = make_float4(__fmul_rn(__uint_as_float(o[j]), inv), __fmul_rn(__uint_as_float(o[j + 1]), inv),
                                        __fmul_rn(__uint_as_float(o[j + 2]), inv), __fmul_rn(__uint_as_float(o[j + 3]), inv));
-          *reinterpret_cast<float4*>(op + j) = a;
-          mx_out = fmaxf(mx_out, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
+          *reinterpret_cast<float4*>(A + stage_off(row, par * 8 + (j >> 2))) = a;
+          if (live)
+            mx_out = fmaxf(mx_out, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
         }
+        soft_sync();
+        if (ok) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int r = lrow + i * 16;
+            if (q0 + r < L)
+              *reinterpret_cast<float4*>(out + base + static_cast<long>(q0 + r) * rs + col4) =
+                  *reinterpret_cast<const float4*>(A + stage_off(r, col4 >> 2));
+          }
+        }
+        soft_sync();  // staging read out before the next item's Q lands in A
       }
       if (it_next >= n_items) break;
       it = it_next;
