@@ -58,15 +58,14 @@ __device__ __forceinline__ float epi_row_run(const EpiParams& e, long m, int c0,
 }
 
 // The q-scale and RoPE of epi_qkv_rope_head on the values only (the caller
-// stores them); which = 0 (q), 1 (k), 2 (v).
-__device__ __forceinline__ void epi_qkv_rope_values(const EpiParams& e, long m, int which,
+// stores them); which = 0 (q), 1 (k), 2 (v); p = the row's position.
+__device__ __forceinline__ void epi_qkv_rope_values(const EpiParams& e, int p, int which,
                                                     float (&y)[64]) {
   if (which == 0) {
 #pragma unroll
     for (int j = 0; j < 64; ++j) y[j] = __fmul_rn(y[j], e.q_scale);
   }
   if (which <= 1) {
-    const int p = __ldg(e.pos + m);
     const float4* c4 = reinterpret_cast<const float4*>(e.cos_t + static_cast<long>(p) * 64);
     const float4* s4 = reinterpret_cast<const float4*>(e.sin_t + static_cast<long>(p) * 64);
 #pragma unroll

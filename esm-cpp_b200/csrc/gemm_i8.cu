@@ -6,18 +6,25 @@
 // u8 with zero point 128 and subtracts 128*col_sum afterwards; the tensor
 // cores take s8 x s8 directly, which yields the same int32 sum_k q*w.
 //
-// Structure (persistent, one CTA per SM, 192 threads):
-//   warp 0      TMA producer: A [BM x 128] and W [BN x 128] int8 tiles,
+// Structure (persistent, one CTA per SM, 320 threads):
+//   warp 0      TMA producer: A [128 x 128] and W [BN x 128] int8 tiles,
 //               128-byte swizzle, into a STAGES-deep shared-memory ring.
 //   warp 1      TMEM owner + MMA issuer: 4 x (M=128, N=BN, K=32) MMAs per
 //               stage into one of two TMEM accumulators (2*BN columns).
-//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (one output row
-//               per thread), dequant fma(float(acc), ws[n]*as, bias[n]),
-//               then store / residual / GELU / QKV-split+RoPE.
+//   warps 2..9  epilogue, two warps per TMEM lane quadrant: tcgen05.ld 32
+//               columns at a time (one output row per thread), dequant
+//               fma(float(acc), ws[n]*as, bias[n]), then store / residual /
+//               GELU / QKV-split+RoPE through TMA stores.
+// The BN = 256 tiles run on CTA pairs (2-CTA clusters, tcgen05 cta_group::2):
+// the pair computes a 256 x 256 tile with M = 256 MMAs issued by CTA 0, each
+// CTA loading its own 128 rows of A and 128 rows of W, so a stage moves 32 KB
+// into each SM instead of 48 KB for the same math.  Each CTA's epilogue
+// drains its own 128 TMEM rows.
 // The epilogue of tile i overlaps the mainloop of tile i+1.  Every barrier
 // wait is bounded; a timeout sets a status bit and the CTA unwinds.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstring>
 
@@ -30,20 +37,25 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 128;  // bytes of K per stage = one 128-byte swizzle row
-constexpr int kThreads = 320;    // producer, MMA issuer, 8 epilogue warps
-constexpr int kEpiWarps = 8;
+// Epilogue warps per CTA (EW): 16 (four per TMEM lane quadrant) for the
+// instruction-heavy GELU epilogue, 8 for the others.
+constexpr int threads_for(int ew) { return 64 + 32 * ew; }  // + producer, MMA issuer
+constexpr int kSmemLimit = 232448;                            // opt-in maximum per CTA
 
-template <int BN>
+template <int BN, bool PAIR, int EW>
 struct Cfg {
   static constexpr int A_BYTES = BM * BK;
-  static constexpr int B_BYTES = BN * BK;
+  static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * BK;  // this CTA's rows of W
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN == 256) ? 3 : (BN == 128 ? 5 : 7);
+
   static constexpr int TMEM_COLS = 2 * BN;
-  // Epilogue staging for TMA stores: 8 warps x [32 rows x 128 B], then the
+  // Epilogue staging for TMA stores: one [32 rows x 128 B] per warp, then the
   // tile's (w_scale * a_scale) and bias columns shared by the epilogue warps.
-  static constexpr int STAGING_BYTES = kEpiWarps * 4096;
+  static constexpr int STAGING_BYTES = EW * 4096;
   static constexpr int COLVEC_BYTES = 2 * BN * 4;
+  // As many stages as the rest of shared memory holds (at most 8).
+  static constexpr int FIT = (kSmemLimit - 1024 - 256 - STAGING_BYTES - COLVEC_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES = FIT < 8 ? FIT : 8;
   static constexpr int SMEM =
       STAGES * STAGE_BYTES + STAGING_BYTES + COLVEC_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
@@ -60,13 +72,15 @@ struct Params {
   int tma;  // epilogue stores through TMA (tensor maps tmC0..2 valid)
 };
 
-// Named barrier 1 across the kEpiWarps epilogue warps only.
+// Named barrier 1 across the EW epilogue warps only.
+template <int EW>
 __device__ __forceinline__ void epi_barrier() {
-  asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
+  asm volatile("bar.sync 1, %0;" ::"n"(EW * 32) : "memory");
 }
 // The same barrier with an AND-vote: every epilogue warp gets the same answer,
 // so a timeout leaves the loop in all of them together (none is left waiting
 // at a later barrier).
+template <int EW>
 __device__ __forceinline__ bool epi_all(bool v) {
   uint32_t r;
   asm volatile(
@@ -75,19 +89,22 @@ __device__ __forceinline__ bool epi_all(bool v) {
       "barrier.cta.red.and.pred po, 1, %2, pi;\n\t"
       "selp.u32 %0, 1, 0, po;\n\t}"
       : "=r"(r)
-      : "r"(v ? 1u : 0u), "n"(kEpiWarps * 32)
+      : "r"(v ? 1u : 0u), "n"(EW * 32)
       : "memory");
   return r != 0;
 }
 
-template <int BN, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+// Register cap: with EW = 16, 18 warps put five on one SM sub-partition (16K
+// registers each) -> 96; with EW = 8, three -> 168.
+template <int BN, int EPI, bool PAIR, int EW>
+__global__ void __maxnreg__(EW == 16 ? 96 : 168)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA,
                    const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC0,
                    const __grid_constant__ CUtensorMap tmC1,
                    const __grid_constant__ CUtensorMap tmC2, const Params p) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, PAIR, EW>;
+  constexpr int kEpiPerQuad = EW / 4;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -111,7 +128,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], kEpiWarps);  // one arrive per epilogue warp
+      // one arrive per epilogue warp (of both CTAs of a pair: CTA 0's copy)
+      mbar_init(&tempty[a], EW * (PAIR ? 2 : 1));
     }
     fence_barrier_init();
   }
@@ -127,18 +145,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, C::TMEM_COLS);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, C::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync();  // CTA 0's barriers exist before CTA 1 signals them
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int m_blocks = (p.M + BM - 1) / BM;
+  // Tiles: m_units row slabs (128 rows, or 256 per pair) x n_blocks.  A pair
+  // shares one tile index; CTA `rank` takes rows [128 rank, 128 rank + 128).
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const int first_tile = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int tile_stride = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  const int m_units = PAIR ? (p.M + 2 * BM - 1) / (2 * BM) : (p.M + BM - 1) / BM;
   const int n_blocks = (p.N + BN - 1) / BN;
-  const int num_tiles = m_blocks * n_blocks;
+  const int num_tiles = m_units * n_blocks;
   const int num_kb = (p.K + BK - 1) / BK;
+  auto tile_m_base = [&](int tile) {
+    const int mu = tile % m_units;
+    return PAIR ? mu * 2 * BM + static_cast<int>(rank) * BM : mu * BM;
+  };
 
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
@@ -146,17 +179,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int m_blk = tile % m_blocks;
-        const int n_blk = tile / m_blocks;
+      for (int tile = first_tile; tile < num_tiles && ok; tile += tile_stride) {
+        const int m_base = tile_m_base(tile);
+        const int n_blk = tile / m_units;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.status)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-          tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * BK, m_blk * BM);
-          tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * BK, n_blk * BN);
+          if (PAIR) {
+            // Both CTAs' bytes complete on CTA 0's full barrier, which CTA 0
+            // arms for the pair.
+            if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+            const uint32_t bar0 = mapa_shared(smem_u32(&full[stage]), 0);
+            tma_load_2d_pair(sA + stage * C::A_BYTES, &tmA, bar0, kb * BK, m_base);
+            tma_load_2d_pair(sB + stage * C::B_BYTES, &tmB, bar0, kb * BK,
+                             n_blk * BN + static_cast<int>(rank) * (BN / 2));
+          } else {
+            mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+            tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * BK, m_base);
+            tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * BK, n_blk * BN);
+          }
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -175,14 +218,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_i8(BM, BN);
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = idesc_i8(PAIR ? 2 * BM : BM, BN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int tile = first_tile; tile < num_tiles && ok; tile += tile_stride) {
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.status)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
@@ -196,38 +239,64 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t b0 = smem_u32(sB + stage * C::B_BYTES);
 #pragma unroll
           for (int k = 0; k < BK / 32; ++k) {
-            mma_i8(d_tmem, sw128_kmajor_desc(a0 + k * 32), sw128_kmajor_desc(b0 + k * 32), idesc,
-                   (kb | k) != 0 ? 1u : 0u);
+            if (PAIR)
+              mma_i8_pair(d_tmem, sw128_kmajor_desc(a0 + k * 32), sw128_kmajor_desc(b0 + k * 32),
+                          idesc, (kb | k) != 0 ? 1u : 0u);
+            else
+              mma_i8(d_tmem, sw128_kmajor_desc(a0 + k * 32), sw128_kmajor_desc(b0 + k * 32), idesc,
+                     (kb | k) != 0 ? 1u : 0u);
           }
-          mma_commit(&empty[stage]);
+          if (PAIR) {  // the stage is free in both CTAs
+            mma_commit_pair(smem_u32(&empty[stage]));
+            mma_commit_pair(mapa_shared(smem_u32(&empty[stage]), 1));
+          } else {
+            mma_commit(&empty[stage]);
+          }
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        mma_commit(&tfull[acc]);
+        if (PAIR) {
+          mma_commit_pair(smem_u32(&tfull[acc]));
+          mma_commit_pair(mapa_shared(smem_u32(&tfull[acc]), 1));
+        } else {
+          mma_commit(&tfull[acc]);
+        }
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1u;
       }
     }
   } else {
     // --------------------------------------------------------- epilogue
-    // Warps 2..9: TMEM lane quadrant warp % 4 (the hardware rule), and the
-    // column half `half`: the two warps of a quadrant take alternate chunks.
+    // Warps 2..: TMEM lane quadrant warp % 4 (the hardware rule); the
+    // kEpiPerQuad warps of a quadrant (index `sub`) take every kEpiPerQuad-th
+    // column chunk.
     const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;
-    const int etid = (warp - 2) * 32 + lane;  // 0..255 among epilogue threads
+    const int sub = (warp - 2) >> 2;
+    const int etid = (warp - 2) * 32 + lane;  // index among epilogue threads
     const int row_in_tile = quad * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
     float amax = 0.0f;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      const int m_blk = tile % m_blocks;
-      const int n_blk = tile / m_blocks;
-      if (!epi_all(mbar_wait(&tfull[acc], acc_phase, p.status))) break;
+    for (int tile = first_tile; tile < num_tiles; tile += tile_stride) {
+      const int m_base = tile_m_base(tile);
+      const int n_blk = tile / m_units;
+      // RoPE: this row's position, and its cos / sin table rows prefetched
+      // into L1 while the accumulator is still being computed.
+      int pos_m = 0;
+      if (EPI == kEpiQkvRope && p.tma) {
+        const long mm = static_cast<long>(m_base) + row_in_tile;
+        if (mm < p.M) {
+          pos_m = __ldg(p.epi.pos + mm);
+          prefetch_l1(p.epi.cos_t + static_cast<long>(pos_m) * 64);
+          prefetch_l1(p.epi.sin_t + static_cast<long>(pos_m) * 64);
+        }
+      }
+      if (!epi_all<EW>(mbar_wait(&tfull[acc], acc_phase, p.status))) break;
       tc_fence_after();
-      const long m = static_cast<long>(m_blk) * BM + row_in_tile;
+      const long m = static_cast<long>(m_base) + row_in_tile;
       const bool row_ok = m < p.M;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
@@ -242,22 +311,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       // product (the reference rounds it before the fma) is formed once.
       const float as_col = p.per_token ? 1.0f : (p.acc_out ? 1.0f : __ldg(p.a_scale));
       if (p.acc_out == nullptr) {
-        for (int j = etid; j < BN; j += kEpiWarps * 32) {
+        for (int j = etid; j < BN; j += EW * 32) {
           const int n = min(n_blk * BN + j, p.N - 1);
           wsv[j] = p.per_token ? __ldg(p.w_scale + n) : __fmul_rn(__ldg(p.w_scale + n), as_col);
           bsv[j] = p.bias ? __ldg(p.bias + n) : 0.0f;
         }
       }
-      epi_barrier();  // vectors filled
-      // Dequant of one accumulator at tile column jc: fma(float(acc),
-      // ws[n]*as, bias[n]) (gemm_int8.cpp:109-126).
-      auto deq = [&](uint32_t a, int jc) {
-        const float sc = p.per_token ? __fmul_rn(wsv[jc], as) : wsv[jc];
-        return __fmaf_rn(__int2float_rn(static_cast<int>(a)), sc, bsv[jc]);
+      epi_barrier<EW>();  // vectors filled
+      // Dequant of 32 accumulators at tile columns jc0.. (jc0 a multiple of
+      // 4): fma(float(acc), ws[n]*as, bias[n]) (gemm_int8.cpp:109-126), the
+      // column vectors read as float4.
+      auto deq32 = [&](const uint32_t(&r)[32], int jc0, float* y) {
+        const float4* w4 = reinterpret_cast<const float4*>(wsv + jc0);
+        const float4* b4 = reinterpret_cast<const float4*>(bsv + jc0);
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4) {
+          const float4 w = w4[j4], b = b4[j4];
+          const float ws[4] = {w.x, w.y, w.z, w.w}, bs[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float sc = p.per_token ? __fmul_rn(ws[u], as) : ws[u];
+            y[4 * j4 + u] = __fmaf_rn(__int2float_rn(static_cast<int>(r[4 * j4 + u])), sc, bs[u]);
+          }
+        }
       };
       // This warp's staging buffer and the top row of its 32-row slab.
-      uint8_t* stg = staging + (warp - 2) * 4096;
-      const int y0 = m_blk * BM + quad * 32;
+      uint8_t* stg_one = staging + (warp - 2) * 4096;
+      auto next_stg = [&]() {
+        if (lane == 0) bulk_wait_read<0>();  // the buffer's last store has read it
+        __syncwarp();
+        return stg_one;
+      };
+      const int y0 = m_base + quad * 32;
       // Stage y[0..32) of this thread's row (lane) with the 128-byte swizzle
       // the tensor map expects.
       auto stage32 = [&](uint8_t* buf, const float* y) {
@@ -279,8 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           return;
         }
         float y[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) y[j] = deq(r[j], c * 32 + j);
+        deq32(r, c * 32, y);
         if (!p.tma) {
           if (row_ok) amax = fmaxf(amax, epi_row_run<32>(p.epi, m, n0, p.N, y));
           return;
@@ -290,12 +374,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 32; ++j) y[j] = gelu_erf(y[j]);
         }
         if (row_ok && p.epi.amax != nullptr) {
+          if (n0 + 32 <= p.N) {  // warp-uniform: the whole chunk is in range
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (n0 + j < p.N) amax = fmaxf(amax, fabsf(y[j]));
+            for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(y[j]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n0 + j < p.N) amax = fmaxf(amax, fabsf(y[j]));
+          }
         }
-        if (lane == 0) bulk_wait_read<0>();  // the buffer's last store has read it
-        __syncwarp();
+        uint8_t* stg = next_stg();
         stage32(stg, y);
         fence_proxy_async_smem();
         __syncwarp();
@@ -309,7 +397,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       if (EPI == kEpiQkvRope) {
 #pragma unroll 1
-        for (int c = half; c < BN / 64; c += 2) {
+        for (int c = sub; c < BN / 64; c += kEpiPerQuad) {
           uint32_t lo[32], hi[32];
           tmem_ld32(t_row + c * 64, lo);
           tmem_ld32(t_row + c * 64 + 32, hi);
@@ -317,20 +405,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int n_base = n_blk * BN + c * 64;
           if (n_base < p.N) {  // warp-uniform
             float y[64];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              y[j] = deq(lo[j], c * 64 + j);
-              y[32 + j] = deq(hi[j], c * 64 + 32 + j);
-            }
+            deq32(lo, c * 64, y);
+            deq32(hi, c * 64 + 32, y + 32);
             if (p.tma) {
               const int which = n_base / p.epi.d;
               const int col = n_base - which * p.epi.d;
-              epi_qkv_rope_values(p.epi, row_ok ? m : 0, which, y);
+              epi_qkv_rope_values(p.epi, pos_m, which, y);
               const CUtensorMap* mp = which == 0 ? &tmC0 : (which == 1 ? &tmC1 : &tmC2);
 #pragma unroll
               for (int half = 0; half < 2; ++half) {
-                if (lane == 0) bulk_wait_read<0>();  // the buffer's last store has read it
-                __syncwarp();
+                uint8_t* stg = next_stg();
                 stage32(stg, y + 32 * half);
                 fence_proxy_async_smem();
                 __syncwarp();
@@ -345,29 +429,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else {
-        // This warp's chunks are half, half+2, ...; the TMEM load of the next
-        // one runs while the previous one is dequantised and stored.
-        constexpr int NC = BN / 64;  // chunks per warp (>= 1)
-        uint32_t ra[32], rb[32];
-        tmem_ld32(t_row + half * 32, ra);
-        tmem_ld_wait();
+        // This warp's 32-column chunks: sub, sub + kEpiPerQuad, ...
 #pragma unroll 1
-        for (int i = 0; i < NC; i += 2) {
-          const int c0 = half + 2 * i;
-          if (i + 1 < NC) tmem_ld32(t_row + (c0 + 2) * 32, rb);
-          epi_chunk(c0, ra);
+        for (int c = sub; c < BN / 32; c += kEpiPerQuad) {
+          uint32_t r[32];
+          tmem_ld32(t_row + c * 32, r);
           tmem_ld_wait();
-          if (i + 1 < NC) {
-            if (i + 2 < NC) tmem_ld32(t_row + (c0 + 4) * 32, ra);
-            epi_chunk(c0 + 2, rb);
-            tmem_ld_wait();
-          }
+          epi_chunk(c, r);
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
-      epi_barrier();  // every epilogue warp is done with this tile's vectors
+      if (lane == 0) {
+        if (PAIR && rank != 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+        else mbar_arrive(&tempty[acc]);
+      }
+      epi_barrier<EW>();  // every epilogue warp is done with this tile's vectors
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
@@ -377,9 +454,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  // A pair retires together: CTA 1's epilogue arrives on CTA 0's barriers and
+  // CTA 0's MMAs read CTA 1's shared memory until the last tile is done.
+  if (PAIR) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::TMEM_COLS);
+    if (PAIR) tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+    else tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
 }
 
@@ -429,12 +510,13 @@ bool make_tmap_f32(CUtensorMap* map, const float* base, long rows, long cols, lo
             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool PAIR, int EW>
 cudaError_t launch_bn(const GemmI8Args& a, cudaStream_t s) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, PAIR, EW>;
+  constexpr int kThreads = threads_for(EW);
   CUtensorMap tmA, tmB, tmC[3];
   if (!make_tmap_i8(&tmA, a.A, a.M, a.K, a.lda, BM)) return cudaErrorInvalidValue;
-  if (!make_tmap_i8(&tmB, a.W, a.N, a.K, a.ldw, BN)) return cudaErrorInvalidValue;
+  if (!make_tmap_i8(&tmB, a.W, a.N, a.K, a.ldw, PAIR ? BN / 2 : BN)) return cudaErrorInvalidValue;
   std::memset(tmC, 0, sizeof(tmC));
   bool tma = false;
   if (a.acc_out == nullptr) {
@@ -452,7 +534,7 @@ cudaError_t launch_bn(const GemmI8Args& a, cudaStream_t s) {
   cudaGetDevice(&dev);
   const uint64_t bit = 1ull << (dev & 63);
   if ((attr_set.load() & bit) == 0) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_i8_kernel<BN, EPI>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_i8_kernel<BN, EPI, PAIR, EW>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
     attr_set.fetch_or(bit);
@@ -469,10 +551,31 @@ cudaError_t launch_bn(const GemmI8Args& a, cudaStream_t s) {
   p.status = a.status;
   p.acc_out = a.acc_out;
   p.tma = tma ? 1 : 0;
-  const int tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
-  const int grid = tiles < a.num_sms ? tiles : a.num_sms;
-  gemm_i8_kernel<BN, EPI><<<grid, kThreads, C::SMEM, s>>>(tmA, tmB, tmC[0], tmC[1], tmC[2], p);
-  return cudaGetLastError();
+  if constexpr (!PAIR) {
+    const int tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
+    const int grid = tiles < a.num_sms ? tiles : a.num_sms;
+    gemm_i8_kernel<BN, EPI, false, EW><<<grid, kThreads, C::SMEM, s>>>(tmA, tmB, tmC[0], tmC[1],
+                                                                    tmC[2], p);
+    return cudaGetLastError();
+  } else {
+  // CTA pairs: one 2-CTA cluster per pair tile, at most num_sms / 2 pairs.
+  const int tiles = ((a.M + 2 * BM - 1) / (2 * BM)) * ((a.N + BN - 1) / BN);
+  const int pairs = std::max(1, std::min(tiles, a.num_sms / 2));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemm_i8_kernel<BN, EPI, true, EW>, tmA, tmB, tmC[0], tmC[1], tmC[2],
+                            p);
+  }
 }
 
 }  // namespace
@@ -488,15 +591,21 @@ cudaError_t launch_gemm_i8(const GemmI8Args& a, cudaStream_t s) {
   const int epi = a.acc_out ? kEpiStore : a.epi.kind;
   if (epi == kEpiQkvRope) {
     // One tile never straddles q|k|v and holds whole 64-wide heads.
-    if (a.epi.d % 256 == 0) return launch_bn<256, kEpiQkvRope>(a, s);
-    if (a.epi.d % 64 == 0) return launch_bn<64, kEpiQkvRope>(a, s);
+    if (a.epi.d % 256 == 0) return launch_bn<256, kEpiQkvRope, false, 8>(a, s);
+    if (a.epi.d % 64 == 0) return launch_bn<64, kEpiQkvRope, false, 8>(a, s);
     return cudaErrorInvalidValue;
   }
   // Wide tiles when N is large, narrower ones to fill the SMs otherwise.
+  // CTA pairs where the mainloop dominates (long K): there the operand feed,
+  // not the epilogue, sets the pace, and pairs cut it by a third.
   const long tiles256 = ((a.M + BM - 1) / BM) * static_cast<long>((a.N + 255) / 256);
   const bool wide = a.N >= 256 && tiles256 >= a.num_sms;
-  if (wide) return launch_bn<256, kEpiStore>(a, s);  // epilogue kind is a runtime field
-  return launch_bn<128, kEpiStore>(a, s);
+  // The epilogue kind is a runtime field; the heavy GELU epilogue gets 16 warps.
+  const bool gelu = a.acc_out == nullptr && a.epi.kind == kEpiGelu;
+  if (wide && a.K >= 2560) return launch_bn<256, kEpiStore, true, 8>(a, s);
+  if (wide) return gelu ? launch_bn<256, kEpiStore, false, 16>(a, s)
+                        : launch_bn<256, kEpiStore, false, 8>(a, s);
+  return gelu ? launch_bn<128, kEpiStore, false, 16>(a, s) : launch_bn<128, kEpiStore, false, 8>(a, s);
 }
 
 }  // namespace esmb200
