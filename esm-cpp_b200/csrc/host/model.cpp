@@ -45,6 +45,7 @@ struct DevLayer {
 // Byte offsets of the per-forward buffers inside the arena.
 struct Arena {
   size_t ids, masks, cu, pos, hidden, ln, q8, ascale, q, k, v, attn, inter, qkv, logits, amax;
+  size_t lnstat;  // per-row LayerNorm statistics of the fused LN + quantise kernel
   size_t total;
 };
 
@@ -138,6 +139,14 @@ int upload_concat_f32(esmcu_model* m, float** dst, const float* const* parts, co
   return upload(m, reinterpret_cast<void**>(dst), host.data(), total * sizeof(float));
 }
 
+// The per-forward reduction state, zeroed at the start of every forward: 4
+// absmax slot groups per layer (+8 spare), then one grid-barrier counter per
+// fused LayerNorm + quantise launch (2 per layer, +8 spare).
+size_t amax_region_bytes(int num_layers) {
+  return static_cast<size_t>(4 * num_layers + 8) * kAmaxSlots * 4 +
+         static_cast<size_t>(2 * num_layers + 8) * 4;
+}
+
 Arena plan_arena(const esmcu_model* m, int T, int B) {
   const auto& c = m->cfg;
   Arena a{};
@@ -164,7 +173,8 @@ Arena plan_arena(const esmcu_model* m, int T, int B) {
   a.inter = take(Tz * ffn * 4);
   a.qkv = take(Tz * 3 * d * 4);
   a.logits = take(Tz * static_cast<size_t>(c.vocab_size) * 4);
-  a.amax = take(static_cast<size_t>(4 * c.num_layers + 8) * kAmaxSlots * 4);
+  a.amax = take(amax_region_bytes(c.num_layers));
+  a.lnstat = take(Tz * 8);
   a.total = cur;
   return a;
 }
@@ -300,7 +310,12 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
 
   Sections sec(m);
 
-  ESMCU_CUDA(cudaMemsetAsync(amax, 0, static_cast<size_t>(4 * c.num_layers + 8) * kAmaxSlots * 4, s));
+  ESMCU_CUDA(cudaMemsetAsync(amax, 0, amax_region_bytes(c.num_layers), s));
+  uint32_t* ln_sync = amax + static_cast<size_t>(4 * c.num_layers + 8) * kAmaxSlots;
+  float2* lnstat = reinterpret_cast<float2*>(base + a.lnstat);
+  // LayerNorm + per-tensor quantisation in one kernel (no fp32 LN output)
+  // unless an observer needs that output.
+  const bool ln_fused = quant && !per_token && stats == nullptr && d % 128 == 0 && d <= 2048;
   LAUNCH(m, launch_positions(cu, B, pos, s));
   sec.begin("embed");
   LAUNCH(m, launch_embed(m->embed, d, ids, mk, cu, B, c.mask_token_id, hidden, s));
@@ -358,7 +373,10 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
     uint32_t* am = amax + 4 * li * kAmaxSlots;  // 4 tensors x kAmaxSlots slots
     // ---- attention block
     sec.begin("attn_ln");
-    if (quant && per_token) {
+    if (ln_fused) {
+      LAUNCH(m, launch_layernorm_quant(hidden, L.ln1_w, L.ln1_b, c.layer_norm_eps, T, d, am, lnstat,
+                                       ln_sync + 2 * li, q8, m->ldk_d, ascale, ctx->d_status, s));
+    } else if (quant && per_token) {
       LAUNCH(m, launch_layernorm(hidden, L.ln1_w, L.ln1_b, c.layer_norm_eps, nullptr, T, d, nullptr,
                                  q8, m->ldk_d, ascale, s));
     } else {
@@ -367,7 +385,7 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
     }
     sec.end();
     observe(li, 0, ln, Td);
-    if (quant && !per_token) {
+    if (quant && !per_token && !ln_fused) {
       sec.begin("quantize");
       TRY(quantize(ln, d, m->ldk_d, am));
       sec.end();
@@ -429,7 +447,11 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
     sec.end();
     // ---- FFN block
     sec.begin("ffn_ln");
-    if (quant && per_token) {
+    if (ln_fused) {
+      LAUNCH(m, launch_layernorm_quant(hidden, L.ln2_w, L.ln2_b, c.layer_norm_eps, T, d,
+                                       am + 2 * kAmaxSlots, lnstat, ln_sync + 2 * li + 1, q8,
+                                       m->ldk_d, ascale, ctx->d_status, s));
+    } else if (quant && per_token) {
       LAUNCH(m, launch_layernorm(hidden, L.ln2_w, L.ln2_b, c.layer_norm_eps, nullptr, T, d, nullptr,
                                  q8, m->ldk_d, ascale, s));
     } else {
@@ -438,7 +460,7 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
     }
     sec.end();
     observe(li, 2, ln, Td);
-    if (quant && !per_token) {
+    if (quant && !per_token && !ln_fused) {
       sec.begin("quantize");
       TRY(quantize(ln, d, m->ldk_d, am + 2 * kAmaxSlots));
       sec.end();

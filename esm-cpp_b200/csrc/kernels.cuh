@@ -99,6 +99,20 @@ cudaError_t launch_layernorm(const float* x, const float* g, const float* b, flo
                              float* out, int rows, int d, uint32_t* amax, int8_t* q,
                              long ldq, float* row_scales, cudaStream_t s);
 
+// LayerNorm fused with the per-tensor int8 quantisation of its output; the
+// fp32 output is never written.  Phase 1 computes every row's statistics
+// (into stats [rows]) and the absmax of y (into the kAmaxSlots slots of
+// amax, zeroed by the caller); after a grid-wide barrier (cooperative launch;
+// *counter must be zero, one counter per launch) phase 2 recomputes y with
+// the same arithmetic and writes q [rows x ldq] (columns >= d zeroed) and
+// *scale_out = max(absmax/127, or 1 if 0).  Returns cudaErrorNotSupported for
+// widths other than d = 128 k (k <= 16) or unaligned buffers; callers then
+// use launch_layernorm + launch_quantize_per_tensor.
+cudaError_t launch_layernorm_quant(const float* x, const float* g, const float* b, float eps,
+                                   int rows, int d, uint32_t* amax, float2* stats,
+                                   uint32_t* counter, int8_t* q, long ldq, float* scale_out,
+                                   uint32_t* status, cudaStream_t s);
+
 // --------------------------------------------------------------- attention
 // Packed-varlen attention, q pre-scaled and RoPE'd; q,k,v,out [T, H, dh].
 // max_len = longest sequence (host-known).  Optional absmax of out into

@@ -9,6 +9,9 @@
 //
 // Fused outputs for the W8A8 path: the absmax of y (per-tensor activation
 // scale of the next GEMM) and/or the per-token int8 quantisation of y.
+#include <algorithm>
+#include <atomic>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -150,7 +153,180 @@ __global__ void layernorm_wide_kernel(const float* __restrict__ x, const float* 
   if (amax != nullptr) amax_publish(amax, mx);
 }
 
+// ------------------------------------------------ LayerNorm + quantisation
+// The per-tensor W8A8 path only needs LN(x) as int8 with one scale over the
+// whole [rows, d] output, so the fp32 output is never written: phase 1 finds
+// every row's statistics and the absmax of y; after a grid-wide barrier
+// phase 2 recomputes y from x (still in L2) and quantises it.  One warp per
+// row, lane l holding columns 4 l + 128 i (d = 128 NV).
+
+// Grid-wide barrier for a cooperative launch, used once per launch: `counter`
+// is zero before the launch; the wait is bounded like the mbarrier waits.
+__device__ __forceinline__ void grid_barrier_once(uint32_t* counter, uint32_t* status) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(counter, 1u);
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t i = 1;; ++i) {
+      uint32_t cur;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(cur) : "l"(counter) : "memory");
+      if (cur >= gridDim.x) break;
+      if ((i & 255u) == 0 && global_timer_ns() - t0 > kWaitNs) {
+        atomicOr(status, kStatusTimeout);
+        break;
+      }
+      __nanosleep(64);
+    }
+    __threadfence();
+  }
+  __syncthreads();
+}
+
+// y = fma((x - mean) * inv_std, g, b) on four columns.
+__device__ __forceinline__ float4 ln_y4(float4 v, float meanf, float inv_std, float4 gg, float4 bv) {
+  return make_float4(__fmaf_rn(__fmul_rn(__fsub_rn(v.x, meanf), inv_std), gg.x, bv.x),
+                     __fmaf_rn(__fmul_rn(__fsub_rn(v.y, meanf), inv_std), gg.y, bv.y),
+                     __fmaf_rn(__fmul_rn(__fsub_rn(v.z, meanf), inv_std), gg.z, bv.z),
+                     __fmaf_rn(__fmul_rn(__fsub_rn(v.w, meanf), inv_std), gg.w, bv.w));
+}
+
+__device__ __forceinline__ uint32_t quant4(float4 y, float inv) {
+  const int a0 = max(-127, min(127, __float2int_rn(__fmul_rn(y.x, inv))));
+  const int a1 = max(-127, min(127, __float2int_rn(__fmul_rn(y.y, inv))));
+  const int a2 = max(-127, min(127, __float2int_rn(__fmul_rn(y.z, inv))));
+  const int a3 = max(-127, min(127, __float2int_rn(__fmul_rn(y.w, inv))));
+  return (static_cast<uint32_t>(a0) & 0xffu) | ((static_cast<uint32_t>(a1) & 0xffu) << 8) |
+         ((static_cast<uint32_t>(a2) & 0xffu) << 16) | ((static_cast<uint32_t>(a3) & 0xffu) << 24);
+}
+
+constexpr int kLqThreads = 384;  // 12 warps: one block per SM at up to 168 registers
+
+template <int NV>
+__global__ void __launch_bounds__(kLqThreads, 1)
+    ln_quant_kernel(const float* __restrict__ x, const float* __restrict__ g,
+                    const float* __restrict__ b, float eps, int rows, int d, uint32_t* amax,
+                    float2* stats, uint32_t* counter, int8_t* __restrict__ q, long ldq,
+                    float* scale_out, uint32_t* status) {
+  const int lane = threadIdx.x & 31;
+  const long warp_g = static_cast<long>(blockIdx.x) * (kLqThreads / 32) + (threadIdx.x >> 5);
+  const long nwarps = static_cast<long>(gridDim.x) * (kLqThreads / 32);
+  // ---- phase 1: statistics and absmax of y
+  float tmax = 0.0f;
+  for (long r = warp_g; r < rows; r += nwarps) {
+    const float* xr = x + r * d;
+    float4 v[NV];
+    double sum = 0.0;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      v[i] = __ldg(reinterpret_cast<const float4*>(xr + 4 * lane + 128 * i));
+      sum += static_cast<double>(v[i].x) + static_cast<double>(v[i].y) +
+             (static_cast<double>(v[i].z) + static_cast<double>(v[i].w));
+    }
+    const double mean = warp_sum_d(sum) / d;
+    double var = 0.0;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const double a = static_cast<double>(v[i].x) - mean, bb = static_cast<double>(v[i].y) - mean;
+      const double cc = static_cast<double>(v[i].z) - mean, dd = static_cast<double>(v[i].w) - mean;
+      var += a * a + bb * bb + (cc * cc + dd * dd);
+    }
+    var = warp_sum_d(var) / d;
+    const float inv_std = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(var), eps)));
+    const float meanf = static_cast<float>(mean);
+    float mx = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = 4 * lane + 128 * i;
+      const float4 y = ln_y4(v[i], meanf, inv_std, __ldg(reinterpret_cast<const float4*>(g + c)),
+                             __ldg(reinterpret_cast<const float4*>(b + c)));
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(y.x), fabsf(y.y)), fmaxf(fabsf(y.z), fabsf(y.w))));
+    }
+    if (lane == 0) stats[r] = make_float2(meanf, inv_std);
+    tmax = fmaxf(tmax, mx);
+  }
+  amax_publish(amax, tmax);
+  grid_barrier_once(counter, status);
+  // ---- phase 2: scale from the finished absmax, then y -> int8
+  __shared__ float s_inv;
+  if (threadIdx.x < 32) {
+    uint32_t m0, m1;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(m0) : "l"(amax + threadIdx.x) : "memory");
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(m1) : "l"(amax + 32 + threadIdx.x) : "memory");
+    const float am = warp_max(__uint_as_float(max(m0, m1)));
+    if (threadIdx.x == 0) {
+      const float sc = am > 0.0f ? __fdiv_rn(am, 127.0f) : 1.0f;
+      s_inv = __fdiv_rn(1.0f, sc);
+      if (blockIdx.x == 0) *scale_out = sc;
+    }
+  }
+  __syncthreads();
+  const float inv = s_inv;
+  for (long r = warp_g; r < rows; r += nwarps) {
+    const float* xr = x + r * d;
+    const float2 st = __ldcg(stats + r);
+    int8_t* qr = q + r * ldq;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = 4 * lane + 128 * i;
+      const float4 y = ln_y4(__ldg(reinterpret_cast<const float4*>(xr + c)), st.x, st.y,
+                             __ldg(reinterpret_cast<const float4*>(g + c)),
+                             __ldg(reinterpret_cast<const float4*>(b + c)));
+      *reinterpret_cast<uint32_t*>(qr + c) = quant4(y, inv);
+    }
+    for (long c = d + lane; c < ldq; c += 32) qr[c] = 0;
+  }
+}
+
+template <int NV>
+cudaError_t launch_lq(const float* x, const float* g, const float* b, float eps, int rows, int d,
+                      uint32_t* amax, float2* stats, uint32_t* counter, int8_t* q, long ldq,
+                      float* scale_out, uint32_t* status, cudaStream_t s) {
+  static std::atomic<int> blocks_per_sm[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int per_sm = blocks_per_sm[dev & 63].load();
+  int sms = 0;
+  cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
+  if (per_sm == 0) {
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, ln_quant_kernel<NV>, kLqThreads, 0);
+    if (e != cudaSuccess) return e;
+    if (per_sm <= 0) return cudaErrorNotSupported;
+    blocks_per_sm[dev & 63].store(per_sm);
+  }
+  const long want = (static_cast<long>(rows) + kLqThreads / 32 - 1) / (kLqThreads / 32);
+  const int grid = static_cast<int>(std::max(1L, std::min<long>(want, static_cast<long>(per_sm) * sms)));
+  void* args[] = {&x, &g, &b, &eps, &rows, &d, &amax, &stats, &counter, &q, &ldq, &scale_out, &status};
+  return cudaLaunchCooperativeKernel(reinterpret_cast<void*>(ln_quant_kernel<NV>), dim3(grid),
+                                     dim3(kLqThreads), args, 0, s);
+}
+
 }  // namespace
+
+cudaError_t launch_layernorm_quant(const float* x, const float* g, const float* b, float eps,
+                                   int rows, int d, uint32_t* amax, float2* stats,
+                                   uint32_t* counter, int8_t* q, long ldq, float* scale_out,
+                                   uint32_t* status, cudaStream_t s) {
+  if (rows <= 0) return cudaSuccess;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(g) |
+                         reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(q)) & 15) == 0;
+  if (d % 128 != 0 || d > 2048 || !aligned || ldq < d || (ldq % 16) != 0 || status == nullptr)
+    return cudaErrorNotSupported;
+  switch (d / 128) {
+    case 1: return launch_lq<1>(x, g, b, eps, rows, d, amax, stats, counter, q, ldq, scale_out, status, s);
+    case 2: return launch_lq<2>(x, g, b, eps, rows, d, amax, stats, counter, q, ldq, scale_out, status, s);
+    case 3: return launch_lq<3>(x, g, b, eps, rows, d, amax, stats, counter, q, ldq, scale_out, status, s);
+    case 4: return launch_lq<4>(x, g, b, eps, rows, d, amax, stats, counter, q, ldq, scale_out, status, s);
+    case 5: return launch_lq<5>(x, g, b, eps, rows, d, amax, stats, counter, q, ldq, scale_out, status, s);
+    case 6: return launch_lq<6>(x, g, b, eps, rows, d, amax, stats, counter, q, ldq, scale_out, status, s);
+    case 8: return launch_lq<8>(x, g, b, eps, rows, d, amax, stats, counter, q, ldq, scale_out, status, s);
+    case 10: return launch_lq<10>(x, g, b, eps, rows, d, amax, stats, counter, q, ldq, scale_out, status, s);
+    case 12: return launch_lq<12>(x, g, b, eps, rows, d, amax, stats, counter, q, ldq, scale_out, status, s);
+    case 16: return launch_lq<16>(x, g, b, eps, rows, d, amax, stats, counter, q, ldq, scale_out, status, s);
+    default: return cudaErrorNotSupported;
+  }
+}
 
 cudaError_t launch_layernorm(const float* x, const float* g, const float* b, float eps,
                              float* out, int rows, int d, uint32_t* amax, int8_t* q, long ldq,
