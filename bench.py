@@ -120,6 +120,14 @@ def build_model(device: int, seed: int = 0):
     return m, time.time() - t0
 
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of the four INT8
+# GEMM launches of one layer, per token: ncu capture of the layer case of
+# esm_b200.kernel_cases (first config-3a group, 13,305 tokens; QKV 176.4 MB,
+# out-proj 97.0 MB, fc1 247.7 MB, fc2 253.2 MB).  Traffic grows with the
+# tokens of a launch (activations and outputs; the weights are ~3% of it).
+GEMM_DRAM_BYTES_PER_TOKEN_LAYER = 774.30e6 / 13305
+
+
 def gemm_ops_per_step(groups_T, cfg) -> float:
     d, f, L = cfg.hidden_size, cfg.intermediate_size, cfg.num_hidden_layers
     per_token = 2.0 * L * (d * 3 * d + d * d + d * f + f * d)  # = 24 d^2 L for f = 4d
@@ -250,7 +258,9 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
                      "achieved": round(achieved, 1), "peak": round(int8_peak, 1), "unit": "TOP/s",
                      "frac": round(achieved / int8_peak, 4),
                      "peak_source": f"2 x bf16_tflops_sustained ({peak_kind}); dense INT8 = 2 x dense BF16",
-                     "traffic": None},
+                     "traffic": round(GEMM_DRAM_BYTES_PER_TOKEN_LAYER * tokens / (4 * len(groups))),
+                     "traffic_unit": "bytes per launch (mean over the step's GEMM launches)",
+                     "traffic_source": "ncu capture of the first config-3a group, scaled by tokens"},
         "sections_ms_per_step": sections,
         "init_s": round(init_s, 1),
     }
