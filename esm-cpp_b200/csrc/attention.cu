@@ -128,27 +128,39 @@ __global__ void __launch_bounds__(QT)
 }  // namespace
 
 cudaError_t launch_attention_tc(const float* q, const float* k, const float* v, const int* cu,
-                                int B, int H, int max_len, float* out, uint32_t* amax,
-                                uint32_t* status, cudaStream_t s);
+                                int B, int H, int min_len, int max_len, float* out,
+                                uint32_t* amax, uint32_t* status, cudaStream_t s);
+cudaError_t launch_attention_tma(const float* q, const float* k, const float* v, const int* cu,
+                                 int B, int H, long T, float* out, uint32_t* amax,
+                                 uint32_t* status, int num_sms, cudaStream_t s);
 
 cudaError_t launch_attention_varlen(const float* q, const float* k, const float* v,
-                                    const int* cu, int B, int H, int dh, int max_len,
-                                    float* out, uint32_t* amax, uint32_t* status, cudaStream_t s) {
+                                    const int* cu, int B, int H, int dh, long T, int min_len,
+                                    int max_len, float* out, uint32_t* amax, uint32_t* status,
+                                    int num_sms, cudaStream_t s) {
   if (B <= 0 || H <= 0 || max_len <= 0) return cudaSuccess;
   if (dh <= 0 || dh > 128 || (dh & 3)) return cudaErrorInvalidValue;
-  // head_dim 64, length <= 256: tensor cores (3xTF32); the rest: FP32 SIMT.
-  int min_len = 0;
+  // head_dim 64: tensor cores (3xTF32) up to 256 tokens -- the TMA-fed
+  // kernel for L <= 128, the register-fed one above; the rest: FP32 SIMT.
+  int simt_min = 0;
   if (dh == 64 && status != nullptr) {
-    cudaError_t e = launch_attention_tc(q, k, v, cu, B, H, max_len, out, amax, status, s);
-    if (e != cudaSuccess) return e;
+    if (min_len <= 128) {
+      cudaError_t e = launch_attention_tma(q, k, v, cu, B, H, T, out, amax, status, num_sms, s);
+      if (e != cudaSuccess) return e;
+    }
+    if (max_len > 128 && min_len <= 256) {
+      cudaError_t e = launch_attention_tc(q, k, v, cu, B, H, 129, max_len, out, amax, status, s);
+      if (e != cudaSuccess) return e;
+    }
     if (max_len <= 256) return cudaSuccess;
-    min_len = 256;
+    simt_min = 256;
   }
+  const int min_len_simt = simt_min;
   dim3 grid(H, B);
-  if (dh <= 16) attention_varlen_kernel<16><<<grid, QT, 0, s>>>(q, k, v, cu, H, dh, out, amax, min_len);
-  else if (dh <= 32) attention_varlen_kernel<32><<<grid, QT, 0, s>>>(q, k, v, cu, H, dh, out, amax, min_len);
-  else if (dh <= 64) attention_varlen_kernel<64><<<grid, QT, 0, s>>>(q, k, v, cu, H, dh, out, amax, min_len);
-  else attention_varlen_kernel<128><<<grid, QT, 0, s>>>(q, k, v, cu, H, dh, out, amax, min_len);
+  if (dh <= 16) attention_varlen_kernel<16><<<grid, QT, 0, s>>>(q, k, v, cu, H, dh, out, amax, min_len_simt);
+  else if (dh <= 32) attention_varlen_kernel<32><<<grid, QT, 0, s>>>(q, k, v, cu, H, dh, out, amax, min_len_simt);
+  else if (dh <= 64) attention_varlen_kernel<64><<<grid, QT, 0, s>>>(q, k, v, cu, H, dh, out, amax, min_len_simt);
+  else attention_varlen_kernel<128><<<grid, QT, 0, s>>>(q, k, v, cu, H, dh, out, amax, min_len_simt);
   return cudaGetLastError();
 }
 

@@ -83,8 +83,8 @@ struct Item {
 // Items are numbered query-block-major, then sequence, then head, so the
 // second query blocks (only sequences longer than 128) come last.  Returns
 // whether item `it` has work on this path.
-__device__ __forceinline__ bool decode_item(int it, int B, int H, const int* __restrict__ cu,
-                                            Item& w) {
+__device__ __forceinline__ bool decode_item(int it, int B, int H, int min_len,
+                                            const int* __restrict__ cu, Item& w) {
   const int per_qb = B * H;
   const int qb = it / per_qb;
   const int rem = it - qb * per_qb;
@@ -93,14 +93,14 @@ __device__ __forceinline__ bool decode_item(int it, int B, int H, const int* __r
   w.qb = qb;
   w.s0 = __ldg(cu + b);
   w.L = __ldg(cu + b + 1) - w.s0;
-  return w.L > 0 && w.L <= KMAX && qb * QB < w.L;
+  return w.L >= min_len && w.L > 0 && w.L <= KMAX && qb * QB < w.L;
 }
 
 // First item with work at or after `it` in steps of `stride` (n_items if none).
 __device__ __forceinline__ int next_item(int it, int stride, int n_items, int B, int H,
-                                         const int* __restrict__ cu, Item& w) {
+                                         int min_len, const int* __restrict__ cu, Item& w) {
   for (; it < n_items; it += stride)
-    if (decode_item(it, B, H, cu, w)) return it;
+    if (decode_item(it, B, H, min_len, cu, w)) return it;
   return n_items;
 }
 
@@ -110,7 +110,8 @@ __device__ __forceinline__ int next_item(int it, int stride, int n_items, int B,
 __global__ void __maxnreg__(168)
     attention_tc_kernel(const float* __restrict__ q, const float* __restrict__ k,
                         const float* __restrict__ v, const int* __restrict__ cu, int B, int H,
-                        int n_items, float* __restrict__ out, uint32_t* amax, uint32_t* status) {
+                        int min_len, int n_items, float* __restrict__ out, uint32_t* amax,
+                        uint32_t* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -122,7 +123,7 @@ __global__ void __maxnreg__(168)
 
   const int stride = gridDim.x;
   Item cur;
-  int it = next_item(blockIdx.x, stride, n_items, B, H, cu, cur);
+  int it = next_item(blockIdx.x, stride, n_items, B, H, min_len, cu, cur);
   if (it >= n_items) return;  // CTA-uniform, before any barrier
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -258,7 +259,7 @@ __global__ void __maxnreg__(168)
       fence_proxy_async_smem();
       // Next item's loads fly during this item's softmax and P.V.
       Item nxt;
-      const int it_next = next_item(it + stride, stride, n_items, B, H, cu, nxt);
+      const int it_next = next_item(it + stride, stride, n_items, B, H, min_len, cu, nxt);
       if (it_next < n_items) prefetch(nxt, x);
 
       // ---- 3b. row max over the valid keys (each warp over its parity)
@@ -398,7 +399,7 @@ __global__ void __maxnreg__(168)
       }
       __syncwarp();
       Item nxt;
-      const int it_next = next_item(it + stride, stride, n_items, B, H, cu, nxt);
+      const int it_next = next_item(it + stride, stride, n_items, B, H, min_len, cu, nxt);
       if (it_next >= n_items) break;
       it = it_next;
       cur = nxt;
@@ -418,11 +419,11 @@ __global__ void __maxnreg__(168)
 }  // namespace
 
 // Launches the persistent tensor-core kernel (one CTA per SM) over every
-// sequence of length <= 256 (at most 2 query blocks); longer sequences are
-// skipped here.
+// sequence with min_len <= L <= 256 (at most 2 query blocks); other
+// sequences are skipped here.
 cudaError_t launch_attention_tc(const float* q, const float* k, const float* v, const int* cu,
-                                int B, int H, int max_len, float* out, uint32_t* amax,
-                                uint32_t* status, cudaStream_t s) {
+                                int B, int H, int min_len, int max_len, float* out,
+                                uint32_t* amax, uint32_t* status, cudaStream_t s) {
   static std::atomic<uint64_t> attr_set{0};
   static std::atomic<int> sm_count[64];
   int dev = 0;
@@ -443,7 +444,7 @@ cudaError_t launch_attention_tc(const float* q, const float* k, const float* v, 
   const long n_items = static_cast<long>(qblocks) * B * H;
   if (n_items > (1L << 30)) return cudaErrorInvalidValue;
   const int grid = static_cast<int>(std::min<long>(n_items, sm_count[dev & 63].load()));
-  attention_tc_kernel<<<grid, kThreads, kSmemBytes, s>>>(q, k, v, cu, B, H,
+  attention_tc_kernel<<<grid, kThreads, kSmemBytes, s>>>(q, k, v, cu, B, H, min_len,
                                                          static_cast<int>(n_items), out, amax,
                                                          status);
   return cudaGetLastError();

@@ -1,0 +1,495 @@
+// Packed-varlen attention for sequences of at most 128 tokens (head_dim 64)
+// on the tcgen05 tensor cores, FP32-accurate (3xTF32), fed by TMA.
+//
+// Same contract as the reference's AttentionVarlen (attention.cpp:99-144):
+// q pre-scaled and RoPE'd, per-sequence softmax over cu_seqlens, exact
+// (not online) softmax -- row max over all keys, exponentials, sum -- then
+// out = (sum_j e_j v_j) / sum_j e_j.
+//
+// 3xTF32 without a hi copy: the tensor core reads an fp32 operand as tf32 by
+// dropping its low 13 bits, so the raw fp32 word is the hi part and only
+// lo = x - hi is formed (in shared memory for K and V, in TMEM for Q).
+//   S = Q K^T  = Q_raw K_raw^T + Q_raw K_lo^T + Q_lo K_raw^T
+//   O = P V    = P_hi V_raw + P_hi V_lo + P_lo V_raw
+// V is used in its natural [key][dh] layout as an MN-major B operand (TMA
+// writes it in the 128-byte swizzle with 32-byte atoms, the MN-major layout
+// kind::tf32 accepts).
+//
+// Persistent, one CTA per SM, items = (sequence, head) with L <= 128,
+// double-buffered: while item n is in its softmax, item n+1's Q and K land
+// in the other 96 KB slot, are split, and its S is computed.
+//   warp 0      TMA producer (Q, K, then V once S has consumed K)
+//   warp 1      TMEM owner + MMA issuer (S into one of two TMEM buffers,
+//               then O += P_chunk V_chunk as the softmax finishes chunks)
+//   warps 2-5   prep, one per TMEM lane quadrant: K_lo, Q_lo (TMEM), V_lo
+//               (V rows >= L zeroed)
+//   warps 6-13  softmax (two per lane quadrant, 32-key chunks by parity) and
+//               the epilogue (O / sum staged in the slot, stored in rows)
+// TMEM: S0 [0,128) S1 [128,256) O [256,320) P_lo [320,448) Q_lo [448,512).
+// Every mbarrier is used at most once per item (or per use of its slot), so
+// no parity wait can alias a later phase.  Waits are bounded; a timeout (or
+// another waiter's) ends all roles' loops.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstring>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace esmb200 {
+namespace {
+
+constexpr int QB = 128;    // query rows per item (all of a short sequence)
+constexpr int DH = 64;     // head dim on this path
+constexpr int KC = 32;     // keys per P.V chunk
+constexpr int LMAX = 128;  // longest sequence on this path
+constexpr int kThreads = 448;
+constexpr int kPrepWarp0 = 2, kSoftWarp0 = 6;
+constexpr uint32_t kSlotBytes = 98304;  // Q raw | K or V raw | K or V lo, 32 KB each
+constexpr uint32_t kOffQ = 0, kOffKV = 32768, kOffLo = 65536;
+constexpr uint32_t kBarOff = 2 * kSlotBytes;
+constexpr int kSmemBytes = static_cast<int>(kBarOff) + 256 + 1024;
+constexpr uint32_t kColS0 = 0, kColO = 256, kColPlo = 320, kColQlo = 448;
+
+enum : int {
+  kFullQK = 0,     // [2] TMA Q + K landed in slot s
+  kFullV = 2,      // [2] TMA V landed
+  kQKReady = 4,    // [2] K_lo and Q_lo written (4 prep warps)
+  kVReady = 6,     // [2] V_lo written (4 prep warps)
+  kSDone = 8,      // [2] S MMAs of the slot's item done
+  kODone = 10,     // [2] P.V MMAs done (by item parity)
+  kSlotFree = 12,  // [2] epilogue done with the slot (8 softmax warps)
+  kChunk = 14,     // [4] P chunk c written (4 softmax warps)
+  kNumBars = 18
+};
+
+struct Item {
+  int h, s0, L;
+};
+
+__device__ __forceinline__ bool decode_item(int it, int H, const int* __restrict__ cu, Item& w) {
+  const int b = it / H;
+  w.h = it - b * H;
+  w.s0 = __ldg(cu + b);
+  w.L = __ldg(cu + b + 1) - w.s0;
+  return w.L > 0 && w.L <= LMAX;
+}
+
+__device__ __forceinline__ int next_item(int it, int stride, int n_items, int H,
+                                         const int* __restrict__ cu, Item& w) {
+  for (; it < n_items; it += stride)
+    if (decode_item(it, H, cu, w)) return it;
+  return n_items;
+}
+
+__device__ __forceinline__ float tf32_lo(float x) {
+  return __fsub_rn(x, __uint_as_float(__float_as_uint(x) & 0xFFFFE000u));
+}
+__device__ __forceinline__ float4 tf32_lo4(float4 x) {
+  return make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w));
+}
+
+// Named barrier 2 over the softmax warps, with an AND-vote.
+__device__ __forceinline__ bool soft_all(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "barrier.cta.red.and.pred po, 2, 256, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(r)
+      : "r"(v ? 1u : 0u)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void soft_sync() { asm volatile("bar.sync 2, 256;" ::: "memory"); }
+
+// Row-major staging of O in a slot: 256-byte rows, 16-byte group c4 of row j
+// at slot c4 ^ (j & 15) (conflict-free for row-per-thread writes and for
+// two-rows-per-warp reads).
+__device__ __forceinline__ uint32_t stage_off(int j, int c4) {
+  return static_cast<uint32_t>(j * 256 + ((c4 ^ (j & 15)) << 4));
+}
+
+__global__ void __maxnreg__(128)
+    attention_tma_kernel(const __grid_constant__ CUtensorMap tmQ,
+                         const __grid_constant__ CUtensorMap tmK,
+                         const __grid_constant__ CUtensorMap tmV, const int* __restrict__ cu,
+                         int H, int n_items, float* __restrict__ out, uint32_t* amax,
+                         uint32_t* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kBarOff);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + kNumBars);
+  volatile uint32_t* abort_flag = tslot + 1;
+  __shared__ float red_max[2][QB], red_sum[2][QB];
+
+  const int stride = gridDim.x;
+  Item first;
+  const int it0 = next_item(blockIdx.x, stride, n_items, H, cu, first);
+  if (it0 >= n_items) return;  // CTA-uniform, before any barrier
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const long rs = static_cast<long>(H) * DH;  // token row stride (floats)
+
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar[kFullQK + i], 1);
+      mbar_init(&bar[kFullV + i], 1);
+      mbar_init(&bar[kQKReady + i], 4);
+      mbar_init(&bar[kVReady + i], 4);
+      mbar_init(&bar[kSDone + i], 1);
+      mbar_init(&bar[kODone + i], 1);
+      mbar_init(&bar[kSlotFree + i], 8);
+    }
+    for (int c = 0; c < LMAX / KC; ++c) mbar_init(&bar[kChunk + c], 4);
+    *abort_flag = 0u;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tslot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  bool ok = true;
+  float mx_out = 0.0f;
+  Item cur = first;
+  int it = it0;
+  int n = 0;  // this CTA's item counter
+
+  if (warp == 0) {
+    // ================================================== TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmV);
+      while (true) {
+        const int s = n & 1;
+        uint8_t* slot = smem + s * kSlotBytes;
+        if (n >= 2 && !(ok = mbar_wait_abort(&bar[kSlotFree + s], ((n >> 1) + 1) & 1, status, abort_flag)))
+          break;
+        mbar_arrive_expect_tx(&bar[kFullQK + s], 4 * 16384);
+        for (int blk = 0; blk < 2; ++blk) {
+          tma_load_2d(slot + kOffQ + blk * 16384, &tmQ, &bar[kFullQK + s], cur.h * DH + 32 * blk, cur.s0);
+          tma_load_2d(slot + kOffKV + blk * 16384, &tmK, &bar[kFullQK + s], cur.h * DH + 32 * blk, cur.s0);
+        }
+        // V replaces K once S has consumed it.
+        if (!(ok = mbar_wait_abort(&bar[kSDone + s], (n >> 1) & 1, status, abort_flag))) break;
+        mbar_arrive_expect_tx(&bar[kFullV + s], 2 * 16384);
+        for (int blk = 0; blk < 2; ++blk)
+          tma_load_2d(slot + kOffKV + blk * 16384, &tmV, &bar[kFullV + s], cur.h * DH + 32 * blk, cur.s0);
+        Item nxt;
+        const int itn = next_item(it + stride, stride, n_items, H, cu, nxt);
+        if (itn >= n_items) break;
+        it = itn;
+        cur = nxt;
+        ++n;
+      }
+    }
+  } else if (warp == 1) {
+    // ==================================================== MMA issuer
+    if (lane == 0) {
+      uint32_t cpar = 0;  // bit c: parity of the next completion of chunk barrier c
+      const uint32_t idO = idesc_tf32_bmn(QB, DH);
+      while (true) {
+        const int s = n & 1;
+        const uint32_t slot = smem_u32(smem + s * kSlotBytes);
+        const int L = cur.L, Lk16 = (L + 15) & ~15, nchunk = (L + KC - 1) / KC;
+        if (!(ok = mbar_wait_abort(&bar[kQKReady + s], (n >> 1) & 1, status, abort_flag))) break;
+        // S buffer s was last used by item n-2: its P.V must be done.
+        if (n >= 2 && !(ok = mbar_wait_abort(&bar[kODone + s], ((n >> 1) + 1) & 1, status, abort_flag)))
+          break;
+        tc_fence_after();
+        const uint32_t tS = tmem + kColS0 + 128u * s;
+        const uint32_t idS = idesc_tf32(QB, Lk16);
+#pragma unroll
+        for (int kk = 0; kk < DH / 8; ++kk) {
+          const uint32_t o = static_cast<uint32_t>((kk >> 2) * 16384 + (kk & 3) * 32);
+          const uint64_t a_raw = sw128_kmajor_desc(slot + kOffQ + o);
+          const uint64_t b_raw = sw128_kmajor_desc(slot + kOffKV + o);
+          const uint64_t b_lo = sw128_kmajor_desc(slot + kOffLo + o);
+          mma_tf32(tS, a_raw, b_raw, idS, kk > 0 ? 1u : 0u);
+          mma_tf32(tS, a_raw, b_lo, idS, 1u);
+          mma_tf32_ts(tS, tmem + kColQlo + 8u * kk, b_raw, idS, 1u);
+        }
+        mma_commit(&bar[kSDone + s]);
+        if (!(ok = mbar_wait_abort(&bar[kVReady + s], (n >> 1) & 1, status, abort_flag))) break;
+        for (int c = 0; c < nchunk; ++c) {
+          if (!(ok = mbar_wait_abort(&bar[kChunk + c], (cpar >> c) & 1u, status, abort_flag))) break;
+          cpar ^= 1u << c;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < KC / 8; ++kk) {
+            const uint32_t vo = static_cast<uint32_t>(c * 4096 + kk * 1024);
+            const uint64_t v_raw = sw128b32_mnmajor_desc(slot + kOffKV + vo, 16384);
+            const uint64_t v_lo = sw128b32_mnmajor_desc(slot + kOffLo + vo, 16384);
+            const uint32_t p_hi = tS + 32u * c + 8u * kk;
+            const uint32_t p_lo = tmem + kColPlo + 32u * c + 8u * kk;
+            mma_tf32_ts(tmem + kColO, p_hi, v_raw, idO, (c | kk) != 0 ? 1u : 0u);
+            mma_tf32_ts(tmem + kColO, p_hi, v_lo, idO, 1u);
+            mma_tf32_ts(tmem + kColO, p_lo, v_raw, idO, 1u);
+          }
+        }
+        if (!ok) break;
+        mma_commit(&bar[kODone + s]);
+        Item nxt;
+        const int itn = next_item(it + stride, stride, n_items, H, cu, nxt);
+        if (itn >= n_items) break;
+        it = itn;
+        cur = nxt;
+        ++n;
+      }
+    }
+  } else if (warp < kSoftWarp0) {
+    // ================================================== prep warps
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const int ptid = (warp - kPrepWarp0) * 32 + lane;  // 0..127
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    while (true) {
+      const int s = n & 1;
+      uint8_t* slot = smem + s * kSlotBytes;
+      const int L = cur.L;
+      if (!(ok = mbar_wait_abort(&bar[kFullQK + s], (n >> 1) & 1, status, abort_flag))) break;
+      // K_lo over the K tile (both 32-column blocks, all 128 rows).
+#pragma unroll 4
+      for (int i = 0; i < 16; ++i) {
+        const uint32_t o = static_cast<uint32_t>((ptid + i * 128) * 16);
+        *reinterpret_cast<float4*>(slot + kOffLo + o) =
+            tf32_lo4(*reinterpret_cast<const float4*>(slot + kOffKV + o));
+      }
+      // Q_lo of this thread's row into TMEM, once S of item n-1 has read the
+      // previous Q_lo.
+      if (n >= 1 && !(ok = mbar_wait_abort(&bar[kSDone + ((n - 1) & 1)], ((n - 1) >> 1) & 1, status, abort_flag)))
+        break;
+      tc_fence_after();
+#pragma unroll
+      for (int blk = 0; blk < 2; ++blk) {
+        uint32_t lo[32];
+#pragma unroll
+        for (int c4 = 0; c4 < 8; ++c4) {
+          const float4 x = *reinterpret_cast<const float4*>(
+              slot + kOffQ + blk * 16384 + row * 128 + ((c4 ^ (row & 7)) << 4));
+          const float4 l = tf32_lo4(x);
+          lo[4 * c4] = __float_as_uint(l.x);
+          lo[4 * c4 + 1] = __float_as_uint(l.y);
+          lo[4 * c4 + 2] = __float_as_uint(l.z);
+          lo[4 * c4 + 3] = __float_as_uint(l.w);
+        }
+        tmem_st32(tmem + kColQlo + 32u * blk + lane_off, lo);
+      }
+      tmem_st_wait();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[kQKReady + s]);
+      // V_lo; rows (keys) >= L are zeroed in both parts.
+      if (!(ok = mbar_wait_abort(&bar[kFullV + s], (n >> 1) & 1, status, abort_flag))) break;
+#pragma unroll 4
+      for (int i = 0; i < 16; ++i) {
+        const uint32_t o = static_cast<uint32_t>((ptid + i * 128) * 16);
+        const int key = static_cast<int>((o & 16383u) >> 7);
+        float4 x = *reinterpret_cast<const float4*>(slot + kOffKV + o);
+        if (key >= L) {
+          x = make_float4(0.f, 0.f, 0.f, 0.f);
+          *reinterpret_cast<float4*>(slot + kOffKV + o) = x;
+        }
+        *reinterpret_cast<float4*>(slot + kOffLo + o) = tf32_lo4(x);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[kVReady + s]);
+      Item nxt;
+      const int itn = next_item(it + stride, stride, n_items, H, cu, nxt);
+      if (itn >= n_items) break;
+      it = itn;
+      cur = nxt;
+      ++n;
+    }
+  } else {
+    // ================================================ softmax warps
+    const int sw = warp - kSoftWarp0;  // 0..7
+    const int quad = warp & 3, par = sw >> 2;
+    const int row = quad * 32 + lane;  // query row = TMEM lane
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const int stid = sw * 32 + lane;  // 0..255
+    const int lrow = stid >> 4, col4 = (stid & 15) * 4;
+    const float kLog2e = 1.4426950408889634f;
+    while (true) {
+      const int s = n & 1;
+      uint8_t* slot = smem + s * kSlotBytes;
+      const int L = cur.L, nchunk = (L + KC - 1) / KC;
+      const bool w0 = ok && mbar_wait_abort(&bar[kSDone + s], (n >> 1) & 1, status, abort_flag);
+      tc_fence_after();
+      const uint32_t tS = tmem + kColS0 + 128u * s;
+      // ---- row max over the valid keys (each warp over its parity's chunks)
+      float mx = -INFINITY;
+      for (int c = par; c < nchunk; c += 2) {
+        uint32_t r32[32];
+        tmem_ld32(tS + lane_off + 32u * c, r32);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (c * 32 + j < L) mx = fmaxf(mx, __uint_as_float(r32[j]));
+      }
+      red_max[par][row] = mx;
+      if (!soft_all(w0)) {
+        ok = false;
+        break;
+      }
+      mx = fmaxf(red_max[0][row], red_max[1][row]);
+      // ---- P chunks into TMEM (P_hi over S, P_lo into its slot)
+      float sum = 0.0f;
+      for (int c = par; c < nchunk; c += 2) {
+        uint32_t hi[32];
+        tmem_ld32(tS + lane_off + 32u * c, hi);
+        tmem_ld_wait();
+#pragma unroll
+        for (int h16 = 0; h16 < 2; ++h16) {
+          uint32_t lo[16];
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) {
+            const int j = h16 * 16 + jj;
+            const float sv = __uint_as_float(hi[j]);
+            const float pv = (c * 32 + j < L) ? exp2f(__fmul_rn(__fsub_rn(sv, mx), kLog2e)) : 0.0f;
+            sum = __fadd_rn(sum, pv);
+            const float ph = __uint_as_float(__float_as_uint(pv) & 0xFFFFE000u);
+            hi[j] = __float_as_uint(ph);
+            lo[jj] = __float_as_uint(__fsub_rn(pv, ph));
+          }
+          tmem_st16(tmem + kColPlo + lane_off + 32u * c + 16u * h16, lo);
+        }
+        tmem_st32(tS + lane_off + 32u * c, hi);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar[kChunk + c]);
+      }
+      red_sum[par][row] = sum;
+      soft_sync();
+      const float total = __fadd_rn(red_sum[0][row], red_sum[1][row]);
+      // ---- O / sum -> staging (the slot's V region, free once P.V is done)
+      const bool w1 = ok && mbar_wait_abort(&bar[kODone + s], (n >> 1) & 1, status, abort_flag);
+      tc_fence_after();
+      uint32_t o[32];
+      tmem_ld32(tmem + kColO + lane_off + 32u * par, o);
+      tmem_ld_wait();
+      {
+        const float inv = __fdiv_rn(1.0f, total);
+        const bool live = row < L;
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          const float4 a = make_float4(__fmul_rn(__uint_as_float(o[j]), inv), __fmul_rn(__uint_as_float(o[j + 1]), inv),
+                                       __fmul_rn(__uint_as_float(o[j + 2]), inv), __fmul_rn(__uint_as_float(o[j + 3]), inv));
+          *reinterpret_cast<float4*>(slot + kOffKV + stage_off(row, par * 8 + (j >> 2))) = a;
+          if (live)
+            mx_out = fmaxf(mx_out, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
+        }
+      }
+      tc_fence_before();
+      if (!soft_all(w1)) {  // also: staging complete
+        ok = false;
+        break;
+      }
+      {
+        float* ob = out + static_cast<long>(cur.s0) * rs + cur.h * DH + col4;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int r = lrow + i * 16;
+          if (r < L)
+            *reinterpret_cast<float4*>(ob + static_cast<long>(r) * rs) =
+                *reinterpret_cast<const float4*>(slot + kOffKV + stage_off(r, col4 >> 2));
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[kSlotFree + s]);
+      Item nxt;
+      const int itn = next_item(it + stride, stride, n_items, H, cu, nxt);
+      if (itn >= n_items) break;
+      it = itn;
+      cur = nxt;
+      ++n;
+    }
+  }
+
+  __syncwarp();
+  const bool all_ok = __syncthreads_and(ok ? 1 : 0) != 0;
+  if (all_ok && amax != nullptr) amax_publish(amax, mx_out);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// [T, H*64] fp32 with 128 x 32-float boxes; rows past T read as zero.
+// Q and K use the 128-byte swizzle (K-major MMA operands), V the 128-byte
+// swizzle with 32-byte atoms (MN-major operand).
+bool make_tmap_rows(CUtensorMap* map, const float* base, long T, long cols,
+                    CUtensorMapSwizzle swizzle) {
+  auto fn = encode_fn();
+  if (fn == nullptr || (reinterpret_cast<uintptr_t>(base) & 15) || (cols % 4)) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(T)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * 4)};
+  cuuint32_t box[2] = {32, 128};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+// Every sequence of 1..128 tokens; others are skipped (callers run the
+// longer ones elsewhere).  T = cu[B] (host-known), num_sms = grid bound.
+cudaError_t launch_attention_tma(const float* q, const float* k, const float* v, const int* cu,
+                                 int B, int H, long T, float* out, uint32_t* amax,
+                                 uint32_t* status, int num_sms, cudaStream_t s) {
+  if (B <= 0 || H <= 0 || T <= 0) return cudaSuccess;
+  CUtensorMap tmQ, tmK, tmV;
+  const long cols = static_cast<long>(H) * DH;
+  if (!make_tmap_rows(&tmQ, q, T, cols, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tmap_rows(&tmK, k, T, cols, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tmap_rows(&tmV, v, T, cols, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
+    return cudaErrorInvalidValue;
+  static std::atomic<uint64_t> attr_set{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if ((attr_set.load() & bit) == 0) {
+    cudaError_t e = cudaFuncSetAttribute(attention_tma_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_set.fetch_or(bit);
+  }
+  const long n_items = static_cast<long>(B) * H;
+  if (n_items > (1L << 30)) return cudaErrorInvalidValue;
+  const int grid = static_cast<int>(std::min<long>(n_items, std::max(1, num_sms)));
+  attention_tma_kernel<<<grid, kThreads, kSmemBytes, s>>>(tmQ, tmK, tmV, cu, H,
+                                                          static_cast<int>(n_items), out, amax,
+                                                          status);
+  return cudaGetLastError();
+}
+
+}  // namespace esmb200

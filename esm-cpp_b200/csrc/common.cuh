@@ -78,6 +78,25 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   return false;
 }
 
+// mbar_wait that also gives up as soon as *abort (shared memory) is set by
+// another waiter of the CTA, and sets it itself on a timeout.
+__device__ __forceinline__ bool mbar_wait_abort(uint64_t* bar, uint32_t parity, uint32_t* status,
+                                                volatile uint32_t* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63u) == 0) {
+      if (*abort) return false;
+      if (global_timer_ns() - t0 > kWaitNs) break;
+    }
+    if (i > 64) __nanosleep(32);
+  }
+  atomicOr(status, kStatusTimeout);
+  *abort = 1u;
+  return false;
+}
+
 // --------------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map,
                                             uint64_t* bar, int c0, int c1) {
@@ -332,6 +351,23 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t smem_addr) {
   return d;
 }
 
+// Shared-memory matrix descriptor for an MN-major 4-byte operand tile in the
+// 128-byte swizzle with 32-byte atoms (the one MN-major layout kind::tf32
+// takes; TMA writes it with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B): each
+// 128-byte row holds 32 consecutive MN elements of one K index, the 32-byte
+// chunks of row k XORed with (k % 4); 4-row K groups 512 bytes apart (SBO),
+// consecutive 32-element MN blocks `lbo` bytes apart (LBO).  A K step of 8 is
+// taken by adding 1024 to the start address.
+__device__ __forceinline__ uint64_t sw128b32_mnmajor_desc(uint32_t smem_addr, uint32_t lbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>(512u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(1u) << 61;
+  return d;
+}
+
 // Instruction descriptor for kind::i8: D s32, A/B signed 8-bit, both
 // K-major, N>>3 at bit 17, M>>4 at bit 24.
 __host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
@@ -343,6 +379,10 @@ __host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
 __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
   return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
          (static_cast<uint32_t>(M >> 4) << 24);
+}
+// The same with B MN-major (bit 16).
+__host__ __device__ constexpr uint32_t idesc_tf32_bmn(int M, int N) {
+  return idesc_tf32(M, N) | (1u << 16);
 }
 
 // Byte offset of element (row, col) of a K-major tile stored with 128-byte

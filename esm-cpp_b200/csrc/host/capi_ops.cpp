@@ -381,10 +381,13 @@ int esmcu_attention_varlen(esmcu_context* ctx, const float* q, const float* k, c
   ESMCU_CUDA(cudaMemcpyAsync(cu_h.data(), cu, cu_h.size() * sizeof(int), cudaMemcpyDeviceToHost,
                              ctx->stream));
   ESMCU_CUDA(cudaStreamSynchronize(ctx->stream));
-  int max_len = 0;
-  for (int b = 0; b < B; ++b) max_len = std::max(max_len, cu_h[b + 1] - cu_h[b]);
-  ESMCU_CUDA(launch_attention_varlen(q, k, v, cu, B, H, dh, max_len, out, nullptr, ctx->d_status,
-                                     ctx->stream));
+  int max_len = 0, min_len = cu_h[1] - cu_h[0];
+  for (int b = 0; b < B; ++b) {
+    max_len = std::max(max_len, cu_h[b + 1] - cu_h[b]);
+    min_len = std::min(min_len, cu_h[b + 1] - cu_h[b]);
+  }
+  ESMCU_CUDA(launch_attention_varlen(q, k, v, cu, B, H, dh, cu_h[B], min_len, max_len, out, nullptr,
+                                     ctx->d_status, ctx->num_sms, ctx->stream));
   return ESMCU_OK;
 }
 

@@ -47,6 +47,7 @@ struct Arena {
   size_t ids, masks, cu, pos, hidden, ln, q8, ascale, q, k, v, attn, inter, qkv, logits, amax;
   size_t lnstat;  // per-row LayerNorm statistics of the fused LN + quantise kernel
   size_t total;
+  int min_len = 0;  // shortest sequence of the batch (kernel choice)
 };
 
 }  // namespace
@@ -423,8 +424,9 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
       sec.end();
     }
     sec.begin("attention");
-    LAUNCH(m, launch_attention_varlen(q, k, v, cu, B, H, dh, max_len, attn,
-                                      (quant && !per_token) ? am + 1 * kAmaxSlots : nullptr, ctx->d_status, s));
+    LAUNCH(m, launch_attention_varlen(q, k, v, cu, B, H, dh, T, a.min_len, max_len, attn,
+                                      (quant && !per_token) ? am + 1 * kAmaxSlots : nullptr,
+                                      ctx->d_status, ctx->num_sms, s));
     sec.end();
     observe(li, 1, attn, Td);
     if (quant) {
@@ -548,10 +550,14 @@ int prepare(esmcu_model* m, int T, bool has_masks, const int32_t* cu, int B, Are
   if (cu == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "cu_seqlens is null");
   std::string msg = ValidateBatchView(T, has_masks ? T : 0, cu, B + 1, B);
   if (!msg.empty()) return fail(ESMCU_ERR_INVALID_ARGUMENT, msg);
-  int max_len = 0;
-  for (int b = 0; b < B; ++b) max_len = std::max(max_len, cu[b + 1] - cu[b]);
+  int max_len = 0, min_len = B > 0 ? cu[1] - cu[0] : 0;
+  for (int b = 0; b < B; ++b) {
+    max_len = std::max(max_len, cu[b + 1] - cu[b]);
+    min_len = std::min(min_len, cu[b + 1] - cu[b]);
+  }
   TRY(ensure_rope(m, max_len));
   *a = plan_arena(m, T, B);
+  a->min_len = min_len;
   TRY(ensure_arena(m, a->total));
   *max_len_out = max_len;
   return ESMCU_OK;

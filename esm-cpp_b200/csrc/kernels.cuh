@@ -115,11 +115,14 @@ cudaError_t launch_layernorm_quant(const float* x, const float* g, const float* 
 
 // --------------------------------------------------------------- attention
 // Packed-varlen attention, q pre-scaled and RoPE'd; q,k,v,out [T, H, dh].
-// max_len = longest sequence (host-known).  Optional absmax of out into
-// *amax.  head_dim 64 runs on the tensor cores (needs the status word).
+// T = cu[B], min_len / max_len = shortest / longest sequence (host-known).
+// Optional absmax of out into *amax.  head_dim 64 runs on the tensor cores
+// (needs the status word): L <= 128 on the TMA-fed kernel, 128 < L <= 256 on
+// the register-fed one; other shapes on FP32 SIMT.
 cudaError_t launch_attention_varlen(const float* q, const float* k, const float* v,
-                                    const int* cu, int B, int H, int dh, int max_len,
-                                    float* out, uint32_t* amax, uint32_t* status, cudaStream_t s);
+                                    const int* cu, int B, int H, int dh, long T, int min_len,
+                                    int max_len, float* out, uint32_t* amax, uint32_t* status,
+                                    int num_sms, cudaStream_t s);
 
 // ------------------------------------------------------------- elementwise
 cudaError_t launch_gelu(const float* x, float* out, long n, cudaStream_t s);
