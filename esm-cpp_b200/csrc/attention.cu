@@ -4,7 +4,7 @@
 // sequence b attends to the keys of sequence b only (cu_seqlens isolation).
 //
 // This FP32 SIMT kernel serves head dims other than 64 and sequences longer
-// than 256 tokens; attention_tc.cu covers the rest on the tensor cores.
+// than 256 tokens; attention_tma.cu covers the rest on the tensor cores.
 // One CTA per (sequence, head); each thread owns one query
 // row (q and the output accumulator live in registers) and streams the
 // sequence's keys/values through shared memory in 32-row tiles with an
@@ -127,12 +127,13 @@ __global__ void __launch_bounds__(QT)
 
 }  // namespace
 
-cudaError_t launch_attention_tc(const float* q, const float* k, const float* v, const int* cu,
-                                int B, int H, int min_len, int max_len, float* out,
-                                uint32_t* amax, uint32_t* status, cudaStream_t s);
 cudaError_t launch_attention_tma(const float* q, const float* k, const float* v, const int* cu,
                                  int B, int H, long T, float* out, uint32_t* amax,
                                  uint32_t* status, int num_sms, cudaStream_t s);
+cudaError_t launch_attention_tma_pair(const float* q, const float* k, const float* v,
+                                      const int* cu, int B, int H, long T, float* out,
+                                      uint32_t* amax, uint32_t* status, int num_sms,
+                                      cudaStream_t s);
 
 cudaError_t launch_attention_varlen(const float* q, const float* k, const float* v,
                                     const int* cu, int B, int H, int dh, long T, int min_len,
@@ -140,8 +141,8 @@ cudaError_t launch_attention_varlen(const float* q, const float* k, const float*
                                     int num_sms, cudaStream_t s) {
   if (B <= 0 || H <= 0 || max_len <= 0) return cudaSuccess;
   if (dh <= 0 || dh > 128 || (dh & 3)) return cudaErrorInvalidValue;
-  // head_dim 64: tensor cores (3xTF32) up to 256 tokens -- the TMA-fed
-  // kernel for L <= 128, the register-fed one above; the rest: FP32 SIMT.
+  // head_dim 64: tensor cores (3xTF32) up to 256 tokens -- one CTA per
+  // (sequence, head) for L <= 128, a CTA pair above; the rest: FP32 SIMT.
   int simt_min = 0;
   if (dh == 64 && status != nullptr) {
     if (min_len <= 128) {
@@ -149,7 +150,7 @@ cudaError_t launch_attention_varlen(const float* q, const float* k, const float*
       if (e != cudaSuccess) return e;
     }
     if (max_len > 128 && min_len <= 256) {
-      cudaError_t e = launch_attention_tc(q, k, v, cu, B, H, 129, max_len, out, amax, status, s);
+      cudaError_t e = launch_attention_tma_pair(q, k, v, cu, B, H, T, out, amax, status, num_sms, s);
       if (e != cudaSuccess) return e;
     }
     if (max_len <= 256) return cudaSuccess;

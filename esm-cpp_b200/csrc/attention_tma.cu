@@ -430,6 +430,378 @@ __global__ void __maxnreg__(128)
   }
 }
 
+// ===================================================================== pairs
+// Sequences of 129..256 tokens: one CTA pair (2-CTA cluster) per (sequence,
+// head), M = 256 MMAs (tcgen05 cta_group::2) issued by CTA 0.  CTA r owns
+// query rows [128 r, 128 r + 128), keys [r N/2, (r+1) N/2) of K
+// (N = round16(L)) and dh columns [32 r, 32 r + 32) of V for all keys, so
+// each CTA keeps the same 96 KB double-buffered slots as the single-CTA
+// kernel.  Prep and softmax warps of both CTAs arrive on CTA 0's ready
+// barriers; CTA 0's MMA completions are committed to both CTAs' barriers.
+// TMEM (each CTA): S [0,256) O [256,320) P_lo [320,448) Q_lo [448,512);
+// chunks 4..7 reuse the P_lo slots of chunks 0..3 once those are consumed.
+constexpr int LMAX2 = 256;
+enum : int {
+  kPFullQK = 0,    // [2] own TMA Q + K landed
+  kPFullV = 2,     // [2] own TMA V landed
+  kPQKReady = 4,   // [2] CTA 0: K_lo + Q_lo of both CTAs (8 prep warps)
+  kPVReady = 6,    // [2] CTA 0: V_lo of both CTAs (8 prep warps)
+  kPSDone = 8,     // S MMAs done (both CTAs, once per item)
+  kPODone = 9,     // P.V MMAs done (both CTAs, once per item)
+  kPLoFree = 10,   // chunks 0..3 consumed: P_lo slots free (both CTAs)
+  kPSlotFree = 11, // [2] own epilogue done with the slot (8 softmax warps)
+  kPChunk = 13,    // [8] CTA 0: P chunk c written in both CTAs (8 softmax warps)
+  kPNumBars = 21
+};
+
+__device__ __forceinline__ bool decode_long(int it, int H, const int* __restrict__ cu, Item& w) {
+  const int b = it / H;
+  w.h = it - b * H;
+  w.s0 = __ldg(cu + b);
+  w.L = __ldg(cu + b + 1) - w.s0;
+  return w.L > LMAX && w.L <= LMAX2;
+}
+__device__ __forceinline__ int next_long(int it, int stride, int n_items, int H,
+                                         const int* __restrict__ cu, Item& w) {
+  for (; it < n_items; it += stride)
+    if (decode_long(it, H, cu, w)) return it;
+  return n_items;
+}
+
+__global__ void __maxnreg__(128)
+    attention_tma_pair_kernel(const __grid_constant__ CUtensorMap tmQ,
+                              const __grid_constant__ CUtensorMap tmK,
+                              const __grid_constant__ CUtensorMap tmV, const int* __restrict__ cu,
+                              int H, int n_items, float* __restrict__ out, uint32_t* amax,
+                              uint32_t* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kBarOff);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + kPNumBars);
+  volatile uint32_t* abort_flag = tslot + 1;
+  __shared__ float red_max[2][QB], red_sum[2][QB];
+
+  const uint32_t rank = cluster_ctarank();
+  const int stride = static_cast<int>(gridDim.x >> 1);
+  Item first;
+  const int it0 = next_long(static_cast<int>(blockIdx.x >> 1), stride, n_items, H, cu, first);
+  if (it0 >= n_items) return;  // uniform over the pair, before any barrier
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const long rs = static_cast<long>(H) * DH;
+  // CTA 0's copy of a barrier (cluster address) for arrivals from either CTA.
+  auto leader = [&](int i) { return mapa_shared(smem_u32(&bar[i]), 0); };
+  auto arrive_leader = [&](int i) {
+    if (rank == 0) mbar_arrive(&bar[i]);
+    else mbar_arrive_cluster(leader(i));
+  };
+
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar[kPFullQK + i], 1);
+      mbar_init(&bar[kPFullV + i], 1);
+      mbar_init(&bar[kPQKReady + i], 8);
+      mbar_init(&bar[kPVReady + i], 8);
+      mbar_init(&bar[kPSlotFree + i], 8);
+    }
+    mbar_init(&bar[kPSDone], 1);
+    mbar_init(&bar[kPODone], 1);
+    mbar_init(&bar[kPLoFree], 1);
+    for (int c = 0; c < LMAX2 / KC; ++c) mbar_init(&bar[kPChunk + c], 8);
+    *abort_flag = 0u;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tslot, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist before either signals the other
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  bool ok = true;
+  float mx_out = 0.0f;
+  Item cur = first;
+  int it = it0;
+  int n = 0;
+
+  if (warp == 0) {
+    // ================================================== TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmV);
+      while (true) {
+        const int s = n & 1;
+        uint8_t* slot = smem + s * kSlotBytes;
+        const int half = ((cur.L + 15) & ~15) >> 1;  // this CTA's K rows start at rank * half
+        if (n >= 2 && !(ok = mbar_wait_abort(&bar[kPSlotFree + s], ((n >> 1) + 1) & 1, status, abort_flag)))
+          break;
+        mbar_arrive_expect_tx(&bar[kPFullQK + s], 4 * 16384);
+        for (int blk = 0; blk < 2; ++blk) {
+          tma_load_2d(slot + kOffQ + blk * 16384, &tmQ, &bar[kPFullQK + s], cur.h * DH + 32 * blk,
+                      cur.s0 + 128 * static_cast<int>(rank));
+          tma_load_2d(slot + kOffKV + blk * 16384, &tmK, &bar[kPFullQK + s], cur.h * DH + 32 * blk,
+                      cur.s0 + half * static_cast<int>(rank));
+        }
+        if (!(ok = mbar_wait_abort(&bar[kPSDone], n & 1, status, abort_flag))) break;
+        mbar_arrive_expect_tx(&bar[kPFullV + s], 2 * 16384);
+        for (int kb = 0; kb < 2; ++kb)
+          tma_load_2d(slot + kOffKV + kb * 16384, &tmV, &bar[kPFullV + s],
+                      cur.h * DH + 32 * static_cast<int>(rank), cur.s0 + 128 * kb);
+        Item nxt;
+        const int itn = next_long(it + stride, stride, n_items, H, cu, nxt);
+        if (itn >= n_items) break;
+        it = itn;
+        cur = nxt;
+        ++n;
+      }
+    }
+  } else if (warp == 1) {
+    // ============================================ MMA issuer (CTA 0)
+    if (lane == 0 && rank == 0) {
+      uint32_t cpar = 0;
+      const uint32_t idO = idesc_tf32_bmn(2 * QB, DH);
+      auto commit_both = [&](int i) {
+        mma_commit_pair(smem_u32(&bar[i]));
+        mma_commit_pair(mapa_shared(smem_u32(&bar[i]), 1));
+      };
+      while (true) {
+        const int s = n & 1;
+        const uint32_t slot = smem_u32(smem + s * kSlotBytes);
+        const int L = cur.L, Lk16 = (L + 15) & ~15, nchunk = (L + KC - 1) / KC;
+        if (!(ok = mbar_wait_cluster_abort(&bar[kPQKReady + s], (n >> 1) & 1, status, abort_flag))) break;
+        // The single S buffer: item n-1's P.V must be done with it.
+        if (n >= 1 && !(ok = mbar_wait_abort(&bar[kPODone], (n - 1) & 1, status, abort_flag))) break;
+        tc_fence_after();
+        const uint32_t idS = idesc_tf32(2 * QB, Lk16);
+#pragma unroll
+        for (int kk = 0; kk < DH / 8; ++kk) {
+          const uint32_t o = static_cast<uint32_t>((kk >> 2) * 16384 + (kk & 3) * 32);
+          const uint64_t a_raw = sw128_kmajor_desc(slot + kOffQ + o);
+          const uint64_t b_raw = sw128_kmajor_desc(slot + kOffKV + o);
+          const uint64_t b_lo = sw128_kmajor_desc(slot + kOffLo + o);
+          mma_tf32_pair(tmem, a_raw, b_raw, idS, kk > 0 ? 1u : 0u);
+          mma_tf32_pair(tmem, a_raw, b_lo, idS, 1u);
+          mma_tf32_ts_pair(tmem, tmem + kColQlo + 8u * kk, b_raw, idS, 1u);
+        }
+        commit_both(kPSDone);
+        if (!(ok = mbar_wait_cluster_abort(&bar[kPVReady + s], (n >> 1) & 1, status, abort_flag))) break;
+        for (int c = 0; c < nchunk; ++c) {
+          if (!(ok = mbar_wait_cluster_abort(&bar[kPChunk + c], (cpar >> c) & 1u, status, abort_flag))) break;
+          cpar ^= 1u << c;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < KC / 8; ++kk) {
+            const uint32_t vo = static_cast<uint32_t>(c * 4096 + kk * 1024);
+            const uint64_t v_raw = sw128b32_mnmajor_desc(slot + kOffKV + vo, 16384);
+            const uint64_t v_lo = sw128b32_mnmajor_desc(slot + kOffLo + vo, 16384);
+            const uint32_t p_hi = tmem + 32u * c + 8u * kk;
+            const uint32_t p_lo = tmem + kColPlo + 32u * (c & 3) + 8u * kk;
+            mma_tf32_ts_pair(tmem + kColO, p_hi, v_raw, idO, (c | kk) != 0 ? 1u : 0u);
+            mma_tf32_ts_pair(tmem + kColO, p_hi, v_lo, idO, 1u);
+            mma_tf32_ts_pair(tmem + kColO, p_lo, v_raw, idO, 1u);
+          }
+          if (c == 3) commit_both(kPLoFree);
+        }
+        if (!ok) break;
+        commit_both(kPODone);
+        Item nxt;
+        const int itn = next_long(it + stride, stride, n_items, H, cu, nxt);
+        if (itn >= n_items) break;
+        it = itn;
+        cur = nxt;
+        ++n;
+      }
+    }
+  } else if (warp < kSoftWarp0) {
+    // ================================================== prep warps
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const int ptid = (warp - kPrepWarp0) * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    while (true) {
+      const int s = n & 1;
+      uint8_t* slot = smem + s * kSlotBytes;
+      const int L = cur.L;
+      if (!(ok = mbar_wait_abort(&bar[kPFullQK + s], (n >> 1) & 1, status, abort_flag))) break;
+#pragma unroll 4
+      for (int i = 0; i < 16; ++i) {
+        const uint32_t o = static_cast<uint32_t>((ptid + i * 128) * 16);
+        *reinterpret_cast<float4*>(slot + kOffLo + o) =
+            tf32_lo4(*reinterpret_cast<const float4*>(slot + kOffKV + o));
+      }
+      if (n >= 1 && !(ok = mbar_wait_abort(&bar[kPSDone], (n - 1) & 1, status, abort_flag))) break;
+      tc_fence_after();
+#pragma unroll
+      for (int blk = 0; blk < 2; ++blk) {
+        uint32_t lo[32];
+#pragma unroll
+        for (int c4 = 0; c4 < 8; ++c4) {
+          const float4 x = *reinterpret_cast<const float4*>(
+              slot + kOffQ + blk * 16384 + row * 128 + ((c4 ^ (row & 7)) << 4));
+          const float4 l = tf32_lo4(x);
+          lo[4 * c4] = __float_as_uint(l.x);
+          lo[4 * c4 + 1] = __float_as_uint(l.y);
+          lo[4 * c4 + 2] = __float_as_uint(l.z);
+          lo[4 * c4 + 3] = __float_as_uint(l.w);
+        }
+        tmem_st32(tmem + kColQlo + 32u * blk + lane_off, lo);
+      }
+      tmem_st_wait();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) arrive_leader(kPQKReady + s);
+      if (!(ok = mbar_wait_abort(&bar[kPFullV + s], (n >> 1) & 1, status, abort_flag))) break;
+      // V_lo over this CTA's 32 dh columns x 256 keys; keys >= L zeroed.
+#pragma unroll 4
+      for (int i = 0; i < 16; ++i) {
+        const uint32_t o = static_cast<uint32_t>((ptid + i * 128) * 16);
+        const int key = static_cast<int>(o >> 7);
+        float4 x = *reinterpret_cast<const float4*>(slot + kOffKV + o);
+        if (key >= L) {
+          x = make_float4(0.f, 0.f, 0.f, 0.f);
+          *reinterpret_cast<float4*>(slot + kOffKV + o) = x;
+        }
+        *reinterpret_cast<float4*>(slot + kOffLo + o) = tf32_lo4(x);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) arrive_leader(kPVReady + s);
+      Item nxt;
+      const int itn = next_long(it + stride, stride, n_items, H, cu, nxt);
+      if (itn >= n_items) break;
+      it = itn;
+      cur = nxt;
+      ++n;
+    }
+  } else {
+    // ================================================ softmax warps
+    const int sw = warp - kSoftWarp0;
+    const int quad = warp & 3, par = sw >> 2;
+    const int row = quad * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const int stid = sw * 32 + lane;
+    const int lrow = stid >> 4, col4 = (stid & 15) * 4;
+    const int q0 = QB * static_cast<int>(rank);
+    const float kLog2e = 1.4426950408889634f;
+    while (true) {
+      const int s = n & 1;
+      uint8_t* slot = smem + s * kSlotBytes;
+      const int L = cur.L, nchunk = (L + KC - 1) / KC;
+      const bool w0 = ok && mbar_wait_abort(&bar[kPSDone], n & 1, status, abort_flag);
+      tc_fence_after();
+      float mx = -INFINITY;
+      for (int c = par; c < nchunk; c += 2) {
+        uint32_t r32[32];
+        tmem_ld32(tmem + lane_off + 32u * c, r32);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (c * 32 + j < L) mx = fmaxf(mx, __uint_as_float(r32[j]));
+      }
+      red_max[par][row] = mx;
+      if (!soft_all(w0)) {
+        ok = false;
+        break;
+      }
+      mx = fmaxf(red_max[0][row], red_max[1][row]);
+      float sum = 0.0f;
+      bool lo_waited = false;
+      for (int c = par; c < nchunk; c += 2) {
+        if (c >= 4 && !lo_waited) {  // P_lo slots of chunks 0..3 consumed
+          if (ok) ok = mbar_wait_abort(&bar[kPLoFree], n & 1, status, abort_flag);
+          lo_waited = true;
+          tc_fence_after();
+        }
+        uint32_t hi[32];
+        tmem_ld32(tmem + lane_off + 32u * c, hi);
+        tmem_ld_wait();
+#pragma unroll
+        for (int h16 = 0; h16 < 2; ++h16) {
+          uint32_t lo[16];
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) {
+            const int j = h16 * 16 + jj;
+            const float sv = __uint_as_float(hi[j]);
+            const float pv = (c * 32 + j < L) ? exp2f(__fmul_rn(__fsub_rn(sv, mx), kLog2e)) : 0.0f;
+            sum = __fadd_rn(sum, pv);
+            const float ph = __uint_as_float(__float_as_uint(pv) & 0xFFFFE000u);
+            hi[j] = __float_as_uint(ph);
+            lo[jj] = __float_as_uint(__fsub_rn(pv, ph));
+          }
+          tmem_st16(tmem + kColPlo + lane_off + 32u * (c & 3) + 16u * h16, lo);
+        }
+        tmem_st32(tmem + lane_off + 32u * c, hi);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) arrive_leader(kPChunk + c);
+      }
+      red_sum[par][row] = sum;
+      soft_sync();
+      const float total = __fadd_rn(red_sum[0][row], red_sum[1][row]);
+      const bool w1 = ok && mbar_wait_abort(&bar[kPODone], n & 1, status, abort_flag);
+      tc_fence_after();
+      uint32_t o[32];
+      tmem_ld32(tmem + kColO + lane_off + 32u * par, o);
+      tmem_ld_wait();
+      {
+        const float inv = __fdiv_rn(1.0f, total);
+        const bool live = q0 + row < L;
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          const float4 a = make_float4(__fmul_rn(__uint_as_float(o[j]), inv), __fmul_rn(__uint_as_float(o[j + 1]), inv),
+                                       __fmul_rn(__uint_as_float(o[j + 2]), inv), __fmul_rn(__uint_as_float(o[j + 3]), inv));
+          *reinterpret_cast<float4*>(slot + kOffKV + stage_off(row, par * 8 + (j >> 2))) = a;
+          if (live)
+            mx_out = fmaxf(mx_out, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
+        }
+      }
+      tc_fence_before();
+      if (!soft_all(w1)) {
+        ok = false;
+        break;
+      }
+      {
+        float* ob = out + static_cast<long>(cur.s0 + q0) * rs + cur.h * DH + col4;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int r = lrow + i * 16;
+          if (q0 + r < L)
+            *reinterpret_cast<float4*>(ob + static_cast<long>(r) * rs) =
+                *reinterpret_cast<const float4*>(slot + kOffKV + stage_off(r, col4 >> 2));
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[kPSlotFree + s]);
+      Item nxt;
+      const int itn = next_long(it + stride, stride, n_items, H, cu, nxt);
+      if (itn >= n_items) break;
+      it = itn;
+      cur = nxt;
+      ++n;
+    }
+  }
+
+  __syncwarp();
+  const bool all_ok = __syncthreads_and(ok ? 1 : 0) != 0;
+  if (all_ok && amax != nullptr) amax_publish(amax, mx_out);
+  tc_fence_before();
+  __syncthreads();
+  // The pair retires together: CTA 1 arrives on CTA 0's barriers and CTA 0's
+  // MMAs read CTA 1's shared memory and TMEM until the last item is done.
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 512);
+  }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (fn == nullptr) {
@@ -490,6 +862,47 @@ cudaError_t launch_attention_tma(const float* q, const float* k, const float* v,
                                                           static_cast<int>(n_items), out, amax,
                                                           status);
   return cudaGetLastError();
+}
+
+// Every sequence of 129..256 tokens, one CTA pair per (sequence, head).
+cudaError_t launch_attention_tma_pair(const float* q, const float* k, const float* v,
+                                      const int* cu, int B, int H, long T, float* out,
+                                      uint32_t* amax, uint32_t* status, int num_sms,
+                                      cudaStream_t s) {
+  if (B <= 0 || H <= 0 || T <= 0) return cudaSuccess;
+  CUtensorMap tmQ, tmK, tmV;
+  const long cols = static_cast<long>(H) * DH;
+  if (!make_tmap_rows(&tmQ, q, T, cols, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tmap_rows(&tmK, k, T, cols, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tmap_rows(&tmV, v, T, cols, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
+    return cudaErrorInvalidValue;
+  static std::atomic<uint64_t> attr_set{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if ((attr_set.load() & bit) == 0) {
+    cudaError_t e = cudaFuncSetAttribute(attention_tma_pair_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_set.fetch_or(bit);
+  }
+  const long n_items = static_cast<long>(B) * H;
+  if (n_items > (1L << 30)) return cudaErrorInvalidValue;
+  const int pairs = static_cast<int>(std::max<long>(1, std::min<long>(n_items, std::max(1, num_sms / 2))));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, attention_tma_pair_kernel, tmQ, tmK, tmV, cu, H,
+                            static_cast<int>(n_items), out, amax, status);
 }
 
 }  // namespace esmb200

@@ -97,6 +97,37 @@ __device__ __forceinline__ bool mbar_wait_abort(uint64_t* bar, uint32_t parity, 
   return false;
 }
 
+// mbar_wait_abort for a barrier that threads of another CTA of the cluster
+// arrive on (release.cluster): the wait acquires at cluster scope.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster_abort(uint64_t* bar, uint32_t parity,
+                                                        uint32_t* status,
+                                                        volatile uint32_t* abort) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((i & 63u) == 0) {
+      if (*abort) return false;
+      if (global_timer_ns() - t0 > kWaitNs) break;
+    }
+    if (i > 64) __nanosleep(32);
+  }
+  atomicOr(status, kStatusTimeout);
+  *abort = 1u;
+  return false;
+}
+
 // --------------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map,
                                             uint64_t* bar, int c0, int c1) {
@@ -199,6 +230,28 @@ __device__ __forceinline__ void mma_i8_pair(uint32_t d_tmem, uint64_t a_desc, ui
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// tf32 pair MMAs (M = 256 over the CTA pair, issued by one thread of CTA 0):
+// A from shared memory (descriptor, the same offset in both CTAs) or from
+// TMEM (each CTA's own lanes), B split by N over the two CTAs.
+__device__ __forceinline__ void mma_tf32_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_tf32_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive on the mbarrier at `bar_cluster_addr` (either CTA of the pair) once
 // every pair MMA issued so far by this thread has completed.
 __device__ __forceinline__ void mma_commit_pair(uint32_t bar_cluster_addr) {

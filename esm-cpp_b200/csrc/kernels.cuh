@@ -117,8 +117,8 @@ cudaError_t launch_layernorm_quant(const float* x, const float* g, const float* 
 // Packed-varlen attention, q pre-scaled and RoPE'd; q,k,v,out [T, H, dh].
 // T = cu[B], min_len / max_len = shortest / longest sequence (host-known).
 // Optional absmax of out into *amax.  head_dim 64 runs on the tensor cores
-// (needs the status word): L <= 128 on the TMA-fed kernel, 128 < L <= 256 on
-// the register-fed one; other shapes on FP32 SIMT.
+// (needs the status word): one CTA per (sequence, head) for L <= 128, a CTA
+// pair for 128 < L <= 256; other shapes on FP32 SIMT.
 cudaError_t launch_attention_varlen(const float* q, const float* k, const float* v,
                                     const int* cu, int B, int H, int dh, long T, int min_len,
                                     int max_len, float* out, uint32_t* amax, uint32_t* status,
