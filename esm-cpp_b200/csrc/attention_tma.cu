@@ -18,14 +18,16 @@
 // Persistent, one CTA per SM, items = (sequence, head) with L <= 128,
 // double-buffered: while item n is in its softmax, item n+1's Q and K land
 // in the other 96 KB slot, are split, and its S is computed.
-//   warp 0      TMA producer (Q, K, then V once S has consumed K)
+//   warp 0      TMA producer (Q, K into the slot; V into a prefetch buffer)
 //   warp 1      TMEM owner + MMA issuer (S into one of two TMEM buffers,
 //               then O += P_chunk V_chunk as the softmax finishes chunks)
-//   warps 2-5   prep, one per TMEM lane quadrant: K_lo, Q_lo (TMEM), V_lo
-//               (V rows >= L zeroed)
+//   warps 2-5   prep, one per TMEM lane quadrant: K_lo, Q_lo (TMEM), then V
+//               and V_lo into the slot once S has consumed K (rows >= L
+//               zeroed)
 //   warps 6-13  softmax (two per lane quadrant, 32-key chunks by parity) and
 //               the epilogue (O / sum staged in the slot, stored in rows)
-// TMEM: S0 [0,128) S1 [128,256) O [256,320) P_lo [320,448) Q_lo [448,512).
+// TMEM (CTA-pair kernel): S [0,256) O [256,320) P_lo [320,448) Q_lo [448,512);
+// the single-CTA kernel's layout is next to its shared-memory constants.
 // Every mbarrier is used at most once per item (or per use of its slot), so
 // no parity wait can alias a later phase.  Waits are bounded; a timeout (or
 // another waiter's) ends all roles' loops.
@@ -51,7 +53,14 @@ constexpr uint32_t kSlotBytes = 98304;  // Q raw | K or V raw | K or V lo, 32 KB
 constexpr uint32_t kOffQ = 0, kOffKV = 32768, kOffLo = 65536;
 constexpr uint32_t kBarOff = 2 * kSlotBytes;
 constexpr int kSmemBytes = static_cast<int>(kBarOff) + 256 + 1024;
-constexpr uint32_t kColS0 = 0, kColO = 256, kColPlo = 320, kColQlo = 448;
+// Single-CTA kernel: a V prefetch buffer after the two slots, then the
+// barriers.  Its TMEM: S [0,128), O [128,256) as two halves (P_hi V + P_lo V,
+// P_hi V_lo; summed by the epilogue), four P_lo slots [256,384), Q_lo
+// [384,448).
+constexpr uint32_t kSVpre = 2 * kSlotBytes, kSBarOff = kSVpre + 32768;
+constexpr int kSSmemBytes = static_cast<int>(kSBarOff) + 256 + 1024;
+constexpr uint32_t kSColO = 128, kSColPlo = 256, kSColQlo = 384;
+constexpr uint32_t kColO = 256, kColPlo = 320, kColQlo = 448;  // CTA-pair kernel
 
 enum : int {
   kFullQK = 0,     // [2] TMA Q + K landed in slot s
@@ -62,7 +71,9 @@ enum : int {
   kODone = 10,     // [2] P.V MMAs done (by item parity)
   kSlotFree = 12,  // [2] epilogue done with the slot (8 softmax warps)
   kChunk = 14,     // [4] P chunk c written (4 softmax warps)
-  kNumBars = 18
+  kFullVpre = 18,  // TMA V landed in the prefetch buffer (once per item)
+  kVpreFree = 19,  // prep has copied it into the slot (4 prep warps)
+  kNumBars = 20
 };
 
 struct Item {
@@ -122,10 +133,10 @@ __global__ void __maxnreg__(128)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kBarOff);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kSBarOff);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + kNumBars);
   volatile uint32_t* abort_flag = tslot + 1;
-  __shared__ float red_max[2][QB], red_sum[2][QB];
+  uint8_t* vpre = smem + kSVpre;
 
   const int stride = gridDim.x;
   Item first;
@@ -146,6 +157,8 @@ __global__ void __maxnreg__(128)
       mbar_init(&bar[kSlotFree + i], 8);
     }
     for (int c = 0; c < LMAX / KC; ++c) mbar_init(&bar[kChunk + c], 4);
+    mbar_init(&bar[kFullVpre], 1);
+    mbar_init(&bar[kVpreFree], 4);
     *abort_flag = 0u;
     fence_barrier_init();
   }
@@ -180,11 +193,12 @@ __global__ void __maxnreg__(128)
           tma_load_2d(slot + kOffQ + blk * 16384, &tmQ, &bar[kFullQK + s], cur.h * DH + 32 * blk, cur.s0);
           tma_load_2d(slot + kOffKV + blk * 16384, &tmK, &bar[kFullQK + s], cur.h * DH + 32 * blk, cur.s0);
         }
-        // V replaces K once S has consumed it.
-        if (!(ok = mbar_wait_abort(&bar[kSDone + s], (n >> 1) & 1, status, abort_flag))) break;
-        mbar_arrive_expect_tx(&bar[kFullV + s], 2 * 16384);
+        // V right behind, into the prefetch buffer once prep has moved item
+        // n-1's V out of it.
+        if (n >= 1 && !(ok = mbar_wait_abort(&bar[kVpreFree], (n - 1) & 1, status, abort_flag))) break;
+        mbar_arrive_expect_tx(&bar[kFullVpre], 2 * 16384);
         for (int blk = 0; blk < 2; ++blk)
-          tma_load_2d(slot + kOffKV + blk * 16384, &tmV, &bar[kFullV + s], cur.h * DH + 32 * blk, cur.s0);
+          tma_load_2d(vpre + blk * 16384, &tmV, &bar[kFullVpre], cur.h * DH + 32 * blk, cur.s0);
         Item nxt;
         const int itn = next_item(it + stride, stride, n_items, H, cu, nxt);
         if (itn >= n_items) break;
@@ -198,16 +212,17 @@ __global__ void __maxnreg__(128)
     if (lane == 0) {
       uint32_t cpar = 0;  // bit c: parity of the next completion of chunk barrier c
       const uint32_t idO = idesc_tf32_bmn(QB, DH);
+      const uint32_t idO2 = idesc_tf32_bmn(QB, 2 * DH);
       while (true) {
         const int s = n & 1;
         const uint32_t slot = smem_u32(smem + s * kSlotBytes);
         const int L = cur.L, Lk16 = (L + 15) & ~15, nchunk = (L + KC - 1) / KC;
         if (!(ok = mbar_wait_abort(&bar[kQKReady + s], (n >> 1) & 1, status, abort_flag))) break;
-        // S buffer s was last used by item n-2: its P.V must be done.
-        if (n >= 2 && !(ok = mbar_wait_abort(&bar[kODone + s], ((n >> 1) + 1) & 1, status, abort_flag)))
+        // The single S buffer holds item n-1's P_hi until its P.V is done.
+        if (n >= 1 && !(ok = mbar_wait_abort(&bar[kODone + ((n - 1) & 1)], ((n - 1) >> 1) & 1, status, abort_flag)))
           break;
         tc_fence_after();
-        const uint32_t tS = tmem + kColS0 + 128u * s;
+        const uint32_t tS = tmem;
         const uint32_t idS = idesc_tf32(QB, Lk16);
 #pragma unroll
         for (int kk = 0; kk < DH / 8; ++kk) {
@@ -217,7 +232,7 @@ __global__ void __maxnreg__(128)
           const uint64_t b_lo = sw128_kmajor_desc(slot + kOffLo + o);
           mma_tf32(tS, a_raw, b_raw, idS, kk > 0 ? 1u : 0u);
           mma_tf32(tS, a_raw, b_lo, idS, 1u);
-          mma_tf32_ts(tS, tmem + kColQlo + 8u * kk, b_raw, idS, 1u);
+          mma_tf32_ts(tS, tmem + kSColQlo + 8u * kk, b_raw, idS, 1u);
         }
         mma_commit(&bar[kSDone + s]);
         if (!(ok = mbar_wait_abort(&bar[kVReady + s], (n >> 1) & 1, status, abort_flag))) break;
@@ -225,16 +240,17 @@ __global__ void __maxnreg__(128)
           if (!(ok = mbar_wait_abort(&bar[kChunk + c], (cpar >> c) & 1u, status, abort_flag))) break;
           cpar ^= 1u << c;
           tc_fence_after();
+          // P_hi [V | V_lo] as one N = 128 MMA (V's two 32-column blocks and
+          // V_lo's follow one another 16 KB apart, the LBO stride), then
+          // P_lo V at N = 64 into the first half.
 #pragma unroll
           for (int kk = 0; kk < KC / 8; ++kk) {
             const uint32_t vo = static_cast<uint32_t>(c * 4096 + kk * 1024);
-            const uint64_t v_raw = sw128b32_mnmajor_desc(slot + kOffKV + vo, 16384);
-            const uint64_t v_lo = sw128b32_mnmajor_desc(slot + kOffLo + vo, 16384);
+            const uint64_t v_all = sw128b32_mnmajor_desc(slot + kOffKV + vo, 16384);
             const uint32_t p_hi = tS + 32u * c + 8u * kk;
-            const uint32_t p_lo = tmem + kColPlo + 32u * c + 8u * kk;
-            mma_tf32_ts(tmem + kColO, p_hi, v_raw, idO, (c | kk) != 0 ? 1u : 0u);
-            mma_tf32_ts(tmem + kColO, p_hi, v_lo, idO, 1u);
-            mma_tf32_ts(tmem + kColO, p_lo, v_raw, idO, 1u);
+            const uint32_t p_lo = tmem + kSColPlo + 32u * c + 8u * kk;
+            mma_tf32_ts(tmem + kSColO, p_hi, v_all, idO2, (c | kk) != 0 ? 1u : 0u);
+            mma_tf32_ts(tmem + kSColO, p_lo, v_all, idO, 1u);
           }
         }
         if (!ok) break;
@@ -283,29 +299,32 @@ __global__ void __maxnreg__(128)
           lo[4 * c4 + 2] = __float_as_uint(l.z);
           lo[4 * c4 + 3] = __float_as_uint(l.w);
         }
-        tmem_st32(tmem + kColQlo + 32u * blk + lane_off, lo);
+        tmem_st32(tmem + kSColQlo + 32u * blk + lane_off, lo);
       }
       tmem_st_wait();
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[kQKReady + s]);
-      // V_lo; rows (keys) >= L are zeroed in both parts.
-      if (!(ok = mbar_wait_abort(&bar[kFullV + s], (n >> 1) & 1, status, abort_flag))) break;
+      // V (prefetched) into the slot once S has consumed K, with V_lo;
+      // rows (keys) >= L are zeroed in both parts.
+      if (!(ok = mbar_wait_abort(&bar[kSDone + s], (n >> 1) & 1, status, abort_flag))) break;
+      if (!(ok = mbar_wait_abort(&bar[kFullVpre], n & 1, status, abort_flag))) break;
 #pragma unroll 4
       for (int i = 0; i < 16; ++i) {
         const uint32_t o = static_cast<uint32_t>((ptid + i * 128) * 16);
         const int key = static_cast<int>((o & 16383u) >> 7);
-        float4 x = *reinterpret_cast<const float4*>(slot + kOffKV + o);
-        if (key >= L) {
-          x = make_float4(0.f, 0.f, 0.f, 0.f);
-          *reinterpret_cast<float4*>(slot + kOffKV + o) = x;
-        }
+        float4 x = *reinterpret_cast<const float4*>(vpre + o);
+        if (key >= L) x = make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(slot + kOffKV + o) = x;
         *reinterpret_cast<float4*>(slot + kOffLo + o) = tf32_lo4(x);
       }
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[kVReady + s]);
+      if (lane == 0) {
+        mbar_arrive(&bar[kVReady + s]);
+        mbar_arrive(&bar[kVpreFree]);
+      }
       Item nxt;
       const int itn = next_item(it + stride, stride, n_items, H, cu, nxt);
       if (itn >= n_items) break;
@@ -325,10 +344,13 @@ __global__ void __maxnreg__(128)
     while (true) {
       const int s = n & 1;
       uint8_t* slot = smem + s * kSlotBytes;
+      // Row max / sum exchange in the slot's Q region (dead once S is done).
+      float (*red_max)[QB] = reinterpret_cast<float (*)[QB]>(slot + kOffQ);
+      float (*red_sum)[QB] = reinterpret_cast<float (*)[QB]>(slot + kOffQ + 1024);
       const int L = cur.L, nchunk = (L + KC - 1) / KC;
       const bool w0 = ok && mbar_wait_abort(&bar[kSDone + s], (n >> 1) & 1, status, abort_flag);
       tc_fence_after();
-      const uint32_t tS = tmem + kColS0 + 128u * s;
+      const uint32_t tS = tmem;
       // ---- row max over the valid keys (each warp over its parity's chunks)
       float mx = -INFINITY;
       for (int c = par; c < nchunk; c += 2) {
@@ -364,7 +386,7 @@ __global__ void __maxnreg__(128)
             hi[j] = __float_as_uint(ph);
             lo[jj] = __float_as_uint(__fsub_rn(pv, ph));
           }
-          tmem_st16(tmem + kColPlo + lane_off + 32u * c + 16u * h16, lo);
+          tmem_st16(tmem + kSColPlo + lane_off + 32u * c + 16u * h16, lo);
         }
         tmem_st32(tS + lane_off + 32u * c, hi);
         tmem_st_wait();
@@ -378,9 +400,13 @@ __global__ void __maxnreg__(128)
       // ---- O / sum -> staging (the slot's V region, free once P.V is done)
       const bool w1 = ok && mbar_wait_abort(&bar[kODone + s], (n >> 1) & 1, status, abort_flag);
       tc_fence_after();
-      uint32_t o[32];
-      tmem_ld32(tmem + kColO + lane_off + 32u * par, o);
+      uint32_t o[32], ob[32];
+      tmem_ld32(tmem + kSColO + lane_off + 32u * par, o);
+      tmem_ld32(tmem + kSColO + 64u + lane_off + 32u * par, ob);
       tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        o[j] = __float_as_uint(__fadd_rn(__uint_as_float(o[j]), __uint_as_float(ob[j])));
       {
         const float inv = __fdiv_rn(1.0f, total);
         const bool live = row < L;
@@ -408,6 +434,7 @@ __global__ void __maxnreg__(128)
                 *reinterpret_cast<const float4*>(slot + kOffKV + stage_off(r, col4 >> 2));
         }
       }
+      fence_proxy_async_smem();  // generic writes in the slot precede its next TMA fill
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[kSlotFree + s]);
       Item nxt;
@@ -777,6 +804,7 @@ __global__ void __maxnreg__(128)
                 *reinterpret_cast<const float4*>(slot + kOffKV + stage_off(r, col4 >> 2));
         }
       }
+      fence_proxy_async_smem();  // generic writes in the slot precede its next TMA fill
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[kPSlotFree + s]);
       Item nxt;
@@ -851,14 +879,14 @@ cudaError_t launch_attention_tma(const float* q, const float* k, const float* v,
   const uint64_t bit = 1ull << (dev & 63);
   if ((attr_set.load() & bit) == 0) {
     cudaError_t e = cudaFuncSetAttribute(attention_tma_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSSmemBytes);
     if (e != cudaSuccess) return e;
     attr_set.fetch_or(bit);
   }
   const long n_items = static_cast<long>(B) * H;
   if (n_items > (1L << 30)) return cudaErrorInvalidValue;
   const int grid = static_cast<int>(std::min<long>(n_items, std::max(1, num_sms)));
-  attention_tma_kernel<<<grid, kThreads, kSmemBytes, s>>>(tmQ, tmK, tmV, cu, H,
+  attention_tma_kernel<<<grid, kThreads, kSSmemBytes, s>>>(tmQ, tmK, tmV, cu, H,
                                                           static_cast<int>(n_items), out, amax,
                                                           status);
   return cudaGetLastError();
