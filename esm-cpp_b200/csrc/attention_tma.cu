@@ -51,11 +51,9 @@ constexpr int kThreads = 448;
 constexpr int kPrepWarp0 = 2, kSoftWarp0 = 6;
 constexpr uint32_t kSlotBytes = 98304;  // Q raw | K or V raw | K or V lo, 32 KB each
 constexpr uint32_t kOffQ = 0, kOffKV = 32768, kOffLo = 65536;
-constexpr uint32_t kBarOff = 2 * kSlotBytes;
-constexpr int kSmemBytes = static_cast<int>(kBarOff) + 256 + 1024;
-// Single-CTA kernel: a V prefetch buffer after the two slots, then the
-// barriers.  Its TMEM: S [0,128), O [128,256) as two halves (P_hi V + P_lo V,
-// P_hi V_lo; summed by the epilogue), four P_lo slots [256,384), Q_lo
+// Both kernels: a 32 KB V prefetch buffer after the two slots, then the
+// barriers.  Single-CTA TMEM: S [0,128), O [128,256) as two halves (P_hi V +
+// P_lo V, P_hi V_lo; summed by the epilogue), four P_lo slots [256,384), Q_lo
 // [384,448).
 constexpr uint32_t kSVpre = 2 * kSlotBytes, kSBarOff = kSVpre + 32768;
 constexpr int kSSmemBytes = static_cast<int>(kSBarOff) + 256 + 1024;
@@ -122,6 +120,76 @@ __device__ __forceinline__ void soft_sync() { asm volatile("bar.sync 2, 256;" ::
 // two-rows-per-warp reads).
 __device__ __forceinline__ uint32_t stage_off(int j, int c4) {
   return static_cast<uint32_t>(j * 256 + ((c4 ^ (j & 15)) << 4));
+}
+
+// 2^x by the PTX ex2.approx.ftz.f32 instruction (relative error about
+// 2^-22; results below 2^-126 flush to zero, which the softmax sum of at
+// least 1 cannot see).
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Row max over the valid keys of one softmax warp's chunks (c = par, par+2,
+// ...; 32 keys each, S chunk c at TMEM column tS + 32 c).
+__device__ __forceinline__ float s_row_max(uint32_t tS, int par, int nchunk, int L) {
+  float mx = -INFINITY;
+  for (int c = par; c < nchunk; c += 2) {
+    uint32_t r[32];
+    tmem_ld32(tS + 32u * c, r);
+    tmem_ld_wait();
+    if (c * 32 + 32 <= L) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) mx = fmaxf(mx, __uint_as_float(r[j]));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (c * 32 + j < L) mx = fmaxf(mx, __uint_as_float(r[j]));
+    }
+  }
+  return mx;
+}
+
+// One softmax warp's P chunks (c = par, par+2, ...): P = 2^((S - mx) log2 e)
+// over the valid keys (0 past L), P_hi = P with its low 13 bits cleared
+// written over S, P_lo = P - P_hi into P_lo slot (c & 3) at tPlo + 32 (c & 3),
+// then arrive(c).  Returns this warp's row sum of P.  wait_lo(c) runs before
+// chunk c's P_lo slot is written.  The exponential is taken for every key
+// and masked afterwards: a select, where a guarded exponential would branch.
+template <class WaitLo, class Arrive>
+__device__ __forceinline__ float p_chunks(uint32_t tS, uint32_t tPlo, int par, int nchunk, int L,
+                                          float mx, WaitLo&& wait_lo, Arrive&& arrive) {
+  const float kLog2e = 1.4426950408889634f;
+  float sum = 0.0f;
+  for (int c = par; c < nchunk; c += 2) {
+    uint32_t hi[32];
+    tmem_ld32(tS + 32u * c, hi);
+    tmem_ld_wait();
+    wait_lo(c);
+    const int nvalid = L - c * 32;  // keys j < nvalid are valid
+#pragma unroll
+    for (int h8 = 0; h8 < 4; ++h8) {
+      uint32_t lo[8];
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) {
+        const int j = h8 * 8 + jj;
+        float pv = ex2_ftz(__fmul_rn(__fsub_rn(__uint_as_float(hi[j]), mx), kLog2e));
+        pv = j < nvalid ? pv : 0.0f;
+        sum = __fadd_rn(sum, pv);
+        const float ph = __uint_as_float(__float_as_uint(pv) & 0xFFFFE000u);
+        hi[j] = __float_as_uint(ph);
+        lo[jj] = __float_as_uint(__fsub_rn(pv, ph));
+      }
+      tmem_st8(tPlo + 32u * (c & 3) + 8u * h8, lo);
+    }
+    tmem_st32(tS + 32u * c, hi);
+    tmem_st_wait();
+    tc_fence_before();
+    __syncwarp();
+    arrive(c);
+  }
+  return sum;
 }
 
 __global__ void __maxnreg__(128)
@@ -340,7 +408,6 @@ __global__ void __maxnreg__(128)
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
     const int stid = sw * 32 + lane;  // 0..255
     const int lrow = stid >> 4, col4 = (stid & 15) * 4;
-    const float kLog2e = 1.4426950408889634f;
     while (true) {
       const int s = n & 1;
       uint8_t* slot = smem + s * kSlotBytes;
@@ -350,17 +417,9 @@ __global__ void __maxnreg__(128)
       const int L = cur.L, nchunk = (L + KC - 1) / KC;
       const bool w0 = ok && mbar_wait_abort(&bar[kSDone + s], (n >> 1) & 1, status, abort_flag);
       tc_fence_after();
-      const uint32_t tS = tmem;
+      const uint32_t tS = tmem + lane_off;
       // ---- row max over the valid keys (each warp over its parity's chunks)
-      float mx = -INFINITY;
-      for (int c = par; c < nchunk; c += 2) {
-        uint32_t r32[32];
-        tmem_ld32(tS + lane_off + 32u * c, r32);
-        tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (c * 32 + j < L) mx = fmaxf(mx, __uint_as_float(r32[j]));
-      }
+      float mx = s_row_max(tS, par, nchunk, L);
       red_max[par][row] = mx;
       if (!soft_all(w0)) {
         ok = false;
@@ -368,32 +427,11 @@ __global__ void __maxnreg__(128)
       }
       mx = fmaxf(red_max[0][row], red_max[1][row]);
       // ---- P chunks into TMEM (P_hi over S, P_lo into its slot)
-      float sum = 0.0f;
-      for (int c = par; c < nchunk; c += 2) {
-        uint32_t hi[32];
-        tmem_ld32(tS + lane_off + 32u * c, hi);
-        tmem_ld_wait();
-#pragma unroll
-        for (int h16 = 0; h16 < 2; ++h16) {
-          uint32_t lo[16];
-#pragma unroll
-          for (int jj = 0; jj < 16; ++jj) {
-            const int j = h16 * 16 + jj;
-            const float sv = __uint_as_float(hi[j]);
-            const float pv = (c * 32 + j < L) ? exp2f(__fmul_rn(__fsub_rn(sv, mx), kLog2e)) : 0.0f;
-            sum = __fadd_rn(sum, pv);
-            const float ph = __uint_as_float(__float_as_uint(pv) & 0xFFFFE000u);
-            hi[j] = __float_as_uint(ph);
-            lo[jj] = __float_as_uint(__fsub_rn(pv, ph));
-          }
-          tmem_st16(tmem + kSColPlo + lane_off + 32u * c + 16u * h16, lo);
-        }
-        tmem_st32(tS + lane_off + 32u * c, hi);
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bar[kChunk + c]);
-      }
+      const float sum = p_chunks(
+          tS, tmem + kSColPlo + lane_off, par, nchunk, L, mx, [](int) {},
+          [&](int c) {
+            if (lane == 0) mbar_arrive(&bar[kChunk + c]);
+          });
       red_sum[par][row] = sum;
       soft_sync();
       const float total = __fadd_rn(red_sum[0][row], red_sum[1][row]);
@@ -466,19 +504,22 @@ __global__ void __maxnreg__(128)
 // kernel.  Prep and softmax warps of both CTAs arrive on CTA 0's ready
 // barriers; CTA 0's MMA completions are committed to both CTAs' barriers.
 // TMEM (each CTA): S [0,256) O [256,320) P_lo [320,448) Q_lo [448,512);
-// chunks 4..7 reuse the P_lo slots of chunks 0..3 once those are consumed.
+// chunk c >= 4 reuses P_lo slot c & 3 once chunk c - 4's P.V is done.
+// Each CTA's V lands in a 32 KB prefetch buffer while S runs and is copied
+// into the slot (with V_lo) once S has consumed K.
 constexpr int LMAX2 = 256;
 enum : int {
   kPFullQK = 0,    // [2] own TMA Q + K landed
-  kPFullV = 2,     // [2] own TMA V landed
+  kPFullVpre = 2,  // own TMA V landed in the prefetch buffer (once per item)
+  kPVpreFree = 3,  // own prep has copied it into the slot (4 prep warps)
   kPQKReady = 4,   // [2] CTA 0: K_lo + Q_lo of both CTAs (8 prep warps)
   kPVReady = 6,    // [2] CTA 0: V_lo of both CTAs (8 prep warps)
   kPSDone = 8,     // S MMAs done (both CTAs, once per item)
   kPODone = 9,     // P.V MMAs done (both CTAs, once per item)
-  kPLoFree = 10,   // chunks 0..3 consumed: P_lo slots free (both CTAs)
-  kPSlotFree = 11, // [2] own epilogue done with the slot (8 softmax warps)
-  kPChunk = 13,    // [8] CTA 0: P chunk c written in both CTAs (8 softmax warps)
-  kPNumBars = 21
+  kPLoFree = 10,   // [4] chunk c's P.V done: P_lo slot c & 3 free for c + 4 (both CTAs)
+  kPSlotFree = 14, // [2] own epilogue done with the slot (8 softmax warps)
+  kPChunk = 16,    // [8] CTA 0: P chunk c written in both CTAs (8 softmax warps)
+  kPNumBars = 24
 };
 
 __device__ __forceinline__ bool decode_long(int it, int H, const int* __restrict__ cu, Item& w) {
@@ -504,10 +545,10 @@ __global__ void __maxnreg__(128)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kBarOff);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kSBarOff);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + kPNumBars);
   volatile uint32_t* abort_flag = tslot + 1;
-  __shared__ float red_max[2][QB], red_sum[2][QB];
+  uint8_t* vpre = smem + kSVpre;
 
   const uint32_t rank = cluster_ctarank();
   const int stride = static_cast<int>(gridDim.x >> 1);
@@ -527,15 +568,16 @@ __global__ void __maxnreg__(128)
   if (tid == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar[kPFullQK + i], 1);
-      mbar_init(&bar[kPFullV + i], 1);
       mbar_init(&bar[kPQKReady + i], 8);
       mbar_init(&bar[kPVReady + i], 8);
       mbar_init(&bar[kPSlotFree + i], 8);
     }
     mbar_init(&bar[kPSDone], 1);
     mbar_init(&bar[kPODone], 1);
-    mbar_init(&bar[kPLoFree], 1);
+    for (int j = 0; j < 4; ++j) mbar_init(&bar[kPLoFree + j], 1);
     for (int c = 0; c < LMAX2 / KC; ++c) mbar_init(&bar[kPChunk + c], 8);
+    mbar_init(&bar[kPFullVpre], 1);
+    mbar_init(&bar[kPVpreFree], 4);
     *abort_flag = 0u;
     fence_barrier_init();
   }
@@ -574,10 +616,12 @@ __global__ void __maxnreg__(128)
           tma_load_2d(slot + kOffKV + blk * 16384, &tmK, &bar[kPFullQK + s], cur.h * DH + 32 * blk,
                       cur.s0 + half * static_cast<int>(rank));
         }
-        if (!(ok = mbar_wait_abort(&bar[kPSDone], n & 1, status, abort_flag))) break;
-        mbar_arrive_expect_tx(&bar[kPFullV + s], 2 * 16384);
+        // V right behind, into the prefetch buffer once prep has moved item
+        // n-1's V out of it.
+        if (n >= 1 && !(ok = mbar_wait_abort(&bar[kPVpreFree], (n - 1) & 1, status, abort_flag))) break;
+        mbar_arrive_expect_tx(&bar[kPFullVpre], 2 * 16384);
         for (int kb = 0; kb < 2; ++kb)
-          tma_load_2d(slot + kOffKV + kb * 16384, &tmV, &bar[kPFullV + s],
+          tma_load_2d(vpre + kb * 16384, &tmV, &bar[kPFullVpre],
                       cur.h * DH + 32 * static_cast<int>(rank), cur.s0 + 128 * kb);
         Item nxt;
         const int itn = next_long(it + stride, stride, n_items, H, cu, nxt);
@@ -632,7 +676,7 @@ __global__ void __maxnreg__(128)
             mma_tf32_ts_pair(tmem + kColO, p_hi, v_lo, idO, 1u);
             mma_tf32_ts_pair(tmem + kColO, p_lo, v_raw, idO, 1u);
           }
-          if (c == 3) commit_both(kPLoFree);
+          if (c + 4 < nchunk) commit_both(kPLoFree + (c & 3));
         }
         if (!ok) break;
         commit_both(kPODone);
@@ -683,22 +727,25 @@ __global__ void __maxnreg__(128)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) arrive_leader(kPQKReady + s);
-      if (!(ok = mbar_wait_abort(&bar[kPFullV + s], (n >> 1) & 1, status, abort_flag))) break;
-      // V_lo over this CTA's 32 dh columns x 256 keys; keys >= L zeroed.
+      // V (prefetched; this CTA's 32 dh columns x 256 keys) into the slot
+      // once S has consumed K, with V_lo; keys >= L zeroed.
+      if (!(ok = mbar_wait_abort(&bar[kPSDone], n & 1, status, abort_flag))) break;
+      if (!(ok = mbar_wait_abort(&bar[kPFullVpre], n & 1, status, abort_flag))) break;
 #pragma unroll 4
       for (int i = 0; i < 16; ++i) {
         const uint32_t o = static_cast<uint32_t>((ptid + i * 128) * 16);
         const int key = static_cast<int>(o >> 7);
-        float4 x = *reinterpret_cast<const float4*>(slot + kOffKV + o);
-        if (key >= L) {
-          x = make_float4(0.f, 0.f, 0.f, 0.f);
-          *reinterpret_cast<float4*>(slot + kOffKV + o) = x;
-        }
+        float4 x = *reinterpret_cast<const float4*>(vpre + o);
+        if (key >= L) x = make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(slot + kOffKV + o) = x;
         *reinterpret_cast<float4*>(slot + kOffLo + o) = tf32_lo4(x);
       }
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) arrive_leader(kPVReady + s);
+      if (lane == 0) {
+        arrive_leader(kPVReady + s);
+        mbar_arrive(&bar[kPVpreFree]);
+      }
       Item nxt;
       const int itn = next_long(it + stride, stride, n_items, H, cu, nxt);
       if (itn >= n_items) break;
@@ -715,60 +762,38 @@ __global__ void __maxnreg__(128)
     const int stid = sw * 32 + lane;
     const int lrow = stid >> 4, col4 = (stid & 15) * 4;
     const int q0 = QB * static_cast<int>(rank);
-    const float kLog2e = 1.4426950408889634f;
+    uint32_t lo_par = 0;  // phase bits of the four P_lo-free barriers
     while (true) {
       const int s = n & 1;
       uint8_t* slot = smem + s * kSlotBytes;
+      // Row max / sum exchange in the slot's Q region (dead once S is done).
+      float (*red_max)[QB] = reinterpret_cast<float (*)[QB]>(slot + kOffQ);
+      float (*red_sum)[QB] = reinterpret_cast<float (*)[QB]>(slot + kOffQ + 1024);
       const int L = cur.L, nchunk = (L + KC - 1) / KC;
       const bool w0 = ok && mbar_wait_abort(&bar[kPSDone], n & 1, status, abort_flag);
       tc_fence_after();
-      float mx = -INFINITY;
-      for (int c = par; c < nchunk; c += 2) {
-        uint32_t r32[32];
-        tmem_ld32(tmem + lane_off + 32u * c, r32);
-        tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (c * 32 + j < L) mx = fmaxf(mx, __uint_as_float(r32[j]));
-      }
+      const uint32_t tS = tmem + lane_off;
+      float mx = s_row_max(tS, par, nchunk, L);
       red_max[par][row] = mx;
       if (!soft_all(w0)) {
         ok = false;
         break;
       }
       mx = fmaxf(red_max[0][row], red_max[1][row]);
-      float sum = 0.0f;
-      bool lo_waited = false;
-      for (int c = par; c < nchunk; c += 2) {
-        if (c >= 4 && !lo_waited) {  // P_lo slots of chunks 0..3 consumed
-          if (ok) ok = mbar_wait_abort(&bar[kPLoFree], n & 1, status, abort_flag);
-          lo_waited = true;
-          tc_fence_after();
-        }
-        uint32_t hi[32];
-        tmem_ld32(tmem + lane_off + 32u * c, hi);
-        tmem_ld_wait();
-#pragma unroll
-        for (int h16 = 0; h16 < 2; ++h16) {
-          uint32_t lo[16];
-#pragma unroll
-          for (int jj = 0; jj < 16; ++jj) {
-            const int j = h16 * 16 + jj;
-            const float sv = __uint_as_float(hi[j]);
-            const float pv = (c * 32 + j < L) ? exp2f(__fmul_rn(__fsub_rn(sv, mx), kLog2e)) : 0.0f;
-            sum = __fadd_rn(sum, pv);
-            const float ph = __uint_as_float(__float_as_uint(pv) & 0xFFFFE000u);
-            hi[j] = __float_as_uint(ph);
-            lo[jj] = __float_as_uint(__fsub_rn(pv, ph));
-          }
-          tmem_st16(tmem + kColPlo + lane_off + 32u * (c & 3) + 16u * h16, lo);
-        }
-        tmem_st32(tmem + lane_off + 32u * c, hi);
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) arrive_leader(kPChunk + c);
-      }
+      // Chunk c >= 4 reuses P_lo slot c & 3 once chunk c - 4's P.V is done.
+      const float sum = p_chunks(
+          tS, tmem + kColPlo + lane_off, par, nchunk, L, mx,
+          [&](int c) {
+            if (c >= 4) {
+              const int j = c & 3;
+              if (ok) ok = mbar_wait_abort(&bar[kPLoFree + j], (lo_par >> j) & 1u, status, abort_flag);
+              lo_par ^= 1u << j;
+              tc_fence_after();
+            }
+          },
+          [&](int c) {
+            if (lane == 0) arrive_leader(kPChunk + c);
+          });
       red_sum[par][row] = sum;
       soft_sync();
       const float total = __fadd_rn(red_sum[0][row], red_sum[1][row]);
@@ -910,7 +935,7 @@ cudaError_t launch_attention_tma_pair(const float* q, const float* k, const floa
   const uint64_t bit = 1ull << (dev & 63);
   if ((attr_set.load() & bit) == 0) {
     cudaError_t e = cudaFuncSetAttribute(attention_tma_pair_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSSmemBytes);
     if (e != cudaSuccess) return e;
     attr_set.fetch_or(bit);
   }
@@ -920,7 +945,7 @@ cudaError_t launch_attention_tma_pair(const float* q, const float* k, const floa
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.dynamicSmemBytes = kSSmemBytes;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
