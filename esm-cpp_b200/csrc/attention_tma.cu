@@ -58,7 +58,13 @@ constexpr uint32_t kOffQ = 0, kOffKV = 32768, kOffLo = 65536;
 constexpr uint32_t kSVpre = 2 * kSlotBytes, kSBarOff = kSVpre + 32768;
 constexpr int kSSmemBytes = static_cast<int>(kSBarOff) + 256 + 1024;
 constexpr uint32_t kSColO = 128, kSColPlo = 256, kSColQlo = 384;
-constexpr uint32_t kColO = 256, kColPlo = 320, kColQlo = 448;  // CTA-pair kernel
+constexpr uint32_t kColO = 256, kColPlo = 384, kColQlo = 448;  // CTA-pair kernel
+// CTA-pair kernel: the V buffer first (it is the raw V operand, and V_lo in
+// a slot's third region sits one positive LBO above it), the two slots, a
+// 1 KB zero block (the B operand's second half in P_lo [V | 0]), barriers.
+constexpr uint32_t kPVbuf = 0, kPSlot0 = 32768;
+constexpr uint32_t kPZero = kPSlot0 + 2 * kSlotBytes, kPBarOff = kPZero + 1024;
+constexpr int kPSmemBytes = static_cast<int>(kPBarOff) + 256 + 1024;
 
 enum : int {
   kFullQK = 0,     // [2] TMA Q + K landed in slot s
@@ -98,6 +104,37 @@ __device__ __forceinline__ float tf32_lo(float x) {
 }
 __device__ __forceinline__ float4 tf32_lo4(float4 x) {
   return make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w));
+}
+
+// 16-byte shared-memory accesses by 32-bit shared address (the kernels'
+// aligned dynamic shared-memory pointer is generic to the compiler).
+__device__ __forceinline__ float4 lds128(uint32_t a) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(a)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void sts128(uint32_t a, float4 v) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(a), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
+}
+
+// lo = x - tf32(x) over a 32 KB tile, 128 threads, 16 bytes per thread per
+// 2 KB step, eight loads in flight.
+__device__ __forceinline__ void tile_lo_32k(uint32_t src, uint32_t dst, int ptid) {
+  src += static_cast<uint32_t>(ptid) * 16u;
+  dst += static_cast<uint32_t>(ptid) * 16u;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    float4 x[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x[i] = lds128(src + (h * 8 + i) * 2048u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sts128(dst + (h * 8 + i) * 2048u, tf32_lo4(x[i]));
+  }
 }
 
 // Named barrier 2 over the softmax warps, with an AND-vote.
@@ -153,37 +190,35 @@ __device__ __forceinline__ float s_row_max(uint32_t tS, int par, int nchunk, int
 
 // One softmax warp's P chunks (c = par, par+2, ...): P = 2^((S - mx) log2 e)
 // over the valid keys (0 past L), P_hi = P with its low 13 bits cleared
-// written over S, P_lo = P - P_hi into P_lo slot (c & 3) at tPlo + 32 (c & 3),
-// then arrive(c).  Returns this warp's row sum of P.  wait_lo(c) runs before
-// chunk c's P_lo slot is written.  The exponential is taken for every key
+// written over S, P_lo = P - P_hi into P_lo slot c & slot_mask (32 columns),
+// then arrive(c).  Returns this warp's row sum of P.  wait_lo(c) runs once P
+// is computed and P_hi stored, before chunk c's P_lo slot is written, so the
+// conversion overlaps the MMAs still reading that slot.  The exponential is
+// taken for every key
 // and masked afterwards: a select, where a guarded exponential would branch.
 template <class WaitLo, class Arrive>
-__device__ __forceinline__ float p_chunks(uint32_t tS, uint32_t tPlo, int par, int nchunk, int L,
-                                          float mx, WaitLo&& wait_lo, Arrive&& arrive) {
+__device__ __forceinline__ float p_chunks(uint32_t tS, uint32_t tPlo, uint32_t slot_mask, int par,
+                                          int nchunk, int L, float mx, WaitLo&& wait_lo,
+                                          Arrive&& arrive) {
   const float kLog2e = 1.4426950408889634f;
   float sum = 0.0f;
   for (int c = par; c < nchunk; c += 2) {
-    uint32_t hi[32];
+    uint32_t hi[32], lo[32];
     tmem_ld32(tS + 32u * c, hi);
     tmem_ld_wait();
-    wait_lo(c);
     const int nvalid = L - c * 32;  // keys j < nvalid are valid
 #pragma unroll
-    for (int h8 = 0; h8 < 4; ++h8) {
-      uint32_t lo[8];
-#pragma unroll
-      for (int jj = 0; jj < 8; ++jj) {
-        const int j = h8 * 8 + jj;
-        float pv = ex2_ftz(__fmul_rn(__fsub_rn(__uint_as_float(hi[j]), mx), kLog2e));
-        pv = j < nvalid ? pv : 0.0f;
-        sum = __fadd_rn(sum, pv);
-        const float ph = __uint_as_float(__float_as_uint(pv) & 0xFFFFE000u);
-        hi[j] = __float_as_uint(ph);
-        lo[jj] = __float_as_uint(__fsub_rn(pv, ph));
-      }
-      tmem_st8(tPlo + 32u * (c & 3) + 8u * h8, lo);
+    for (int j = 0; j < 32; ++j) {
+      float pv = ex2_ftz(__fmul_rn(__fsub_rn(__uint_as_float(hi[j]), mx), kLog2e));
+      pv = j < nvalid ? pv : 0.0f;
+      sum = __fadd_rn(sum, pv);
+      const float ph = __uint_as_float(__float_as_uint(pv) & 0xFFFFE000u);
+      hi[j] = __float_as_uint(ph);
+      lo[j] = __float_as_uint(__fsub_rn(pv, ph));
     }
-    tmem_st32(tS + 32u * c, hi);
+    tmem_st32(tS + 32u * c, hi);  // S chunk c is this warp's alone once read
+    wait_lo(c);
+    tmem_st32(tPlo + 32u * (c & slot_mask), lo);
     tmem_st_wait();
     tc_fence_before();
     __syncwarp();
@@ -343,12 +378,7 @@ __global__ void __maxnreg__(128)
       const int L = cur.L;
       if (!(ok = mbar_wait_abort(&bar[kFullQK + s], (n >> 1) & 1, status, abort_flag))) break;
       // K_lo over the K tile (both 32-column blocks, all 128 rows).
-#pragma unroll 4
-      for (int i = 0; i < 16; ++i) {
-        const uint32_t o = static_cast<uint32_t>((ptid + i * 128) * 16);
-        *reinterpret_cast<float4*>(slot + kOffLo + o) =
-            tf32_lo4(*reinterpret_cast<const float4*>(slot + kOffKV + o));
-      }
+      tile_lo_32k(smem_u32(slot + kOffKV), smem_u32(slot + kOffLo), ptid);
       // Q_lo of this thread's row into TMEM, once S of item n-1 has read the
       // previous Q_lo.
       if (n >= 1 && !(ok = mbar_wait_abort(&bar[kSDone + ((n - 1) & 1)], ((n - 1) >> 1) & 1, status, abort_flag)))
@@ -359,8 +389,8 @@ __global__ void __maxnreg__(128)
         uint32_t lo[32];
 #pragma unroll
         for (int c4 = 0; c4 < 8; ++c4) {
-          const float4 x = *reinterpret_cast<const float4*>(
-              slot + kOffQ + blk * 16384 + row * 128 + ((c4 ^ (row & 7)) << 4));
+          const float4 x = lds128(smem_u32(slot + kOffQ + blk * 16384 + row * 128) +
+                                  static_cast<uint32_t>((c4 ^ (row & 7)) << 4));
           const float4 l = tf32_lo4(x);
           lo[4 * c4] = __float_as_uint(l.x);
           lo[4 * c4 + 1] = __float_as_uint(l.y);
@@ -378,14 +408,22 @@ __global__ void __maxnreg__(128)
       // rows (keys) >= L are zeroed in both parts.
       if (!(ok = mbar_wait_abort(&bar[kSDone + s], (n >> 1) & 1, status, abort_flag))) break;
       if (!(ok = mbar_wait_abort(&bar[kFullVpre], n & 1, status, abort_flag))) break;
-#pragma unroll 4
-      for (int i = 0; i < 16; ++i) {
-        const uint32_t o = static_cast<uint32_t>((ptid + i * 128) * 16);
-        const int key = static_cast<int>((o & 16383u) >> 7);
-        float4 x = *reinterpret_cast<const float4*>(vpre + o);
-        if (key >= L) x = make_float4(0.f, 0.f, 0.f, 0.f);
-        *reinterpret_cast<float4*>(slot + kOffKV + o) = x;
-        *reinterpret_cast<float4*>(slot + kOffLo + o) = tf32_lo4(x);
+      {
+        const uint32_t src = smem_u32(vpre), kv = smem_u32(slot + kOffKV), lo = smem_u32(slot + kOffLo);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          float4 x[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            x[i] = lds128(src + static_cast<uint32_t>((ptid + (h * 8 + i) * 128) * 16));
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const uint32_t o = static_cast<uint32_t>((ptid + (h * 8 + i) * 128) * 16);
+            if (static_cast<int>((o & 16383u) >> 7) >= L) x[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            sts128(kv + o, x[i]);
+            sts128(lo + o, tf32_lo4(x[i]));
+          }
+        }
       }
       fence_proxy_async_smem();
       __syncwarp();
@@ -428,7 +466,7 @@ __global__ void __maxnreg__(128)
       mx = fmaxf(red_max[0][row], red_max[1][row]);
       // ---- P chunks into TMEM (P_hi over S, P_lo into its slot)
       const float sum = p_chunks(
-          tS, tmem + kSColPlo + lane_off, par, nchunk, L, mx, [](int) {},
+          tS, tmem + kSColPlo + lane_off, 3u, par, nchunk, L, mx, [](int) {},
           [&](int c) {
             if (lane == 0) mbar_arrive(&bar[kChunk + c]);
           });
@@ -503,23 +541,26 @@ __global__ void __maxnreg__(128)
 // each CTA keeps the same 96 KB double-buffered slots as the single-CTA
 // kernel.  Prep and softmax warps of both CTAs arrive on CTA 0's ready
 // barriers; CTA 0's MMA completions are committed to both CTAs' barriers.
-// TMEM (each CTA): S [0,256) O [256,320) P_lo [320,448) Q_lo [448,512);
-// chunk c >= 4 reuses P_lo slot c & 3 once chunk c - 4's P.V is done.
-// Each CTA's V lands in a 32 KB prefetch buffer while S runs and is copied
-// into the slot (with V_lo) once S has consumed K.
+// TMEM (each CTA): S [0,256) O [256,384) P_lo [384,448) Q_lo [448,512);
+// chunk c >= 2 reuses P_lo slot c & 1 once chunk c - 2's P.V is done.
+// P.V is two N = 128 MMAs per 8 keys, B in each CTA = its 32 dh columns of
+// V and one LBO further V_lo (P_hi [V | V_lo]) or a zero block (P_lo [V | 0]):
+// pair MMAs of N = 64 run at about 40% of the tensor rate, N = 128 at 66%.
+// Each CTA's V lands in a 32 KB buffer while S runs and is the raw V operand
+// itself; V_lo goes into the slot once S has consumed K_lo, and the next
+// item's V loads once this item's P.V is done.
 constexpr int LMAX2 = 256;
 enum : int {
   kPFullQK = 0,    // [2] own TMA Q + K landed
-  kPFullVpre = 2,  // own TMA V landed in the prefetch buffer (once per item)
-  kPVpreFree = 3,  // own prep has copied it into the slot (4 prep warps)
-  kPQKReady = 4,   // [2] CTA 0: K_lo + Q_lo of both CTAs (8 prep warps)
-  kPVReady = 6,    // [2] CTA 0: V_lo of both CTAs (8 prep warps)
-  kPSDone = 8,     // S MMAs done (both CTAs, once per item)
-  kPODone = 9,     // P.V MMAs done (both CTAs, once per item)
-  kPLoFree = 10,   // [4] chunk c's P.V done: P_lo slot c & 3 free for c + 4 (both CTAs)
-  kPSlotFree = 14, // [2] own epilogue done with the slot (8 softmax warps)
-  kPChunk = 16,    // [8] CTA 0: P chunk c written in both CTAs (8 softmax warps)
-  kPNumBars = 24
+  kPFullV = 2,     // own TMA V landed in the V buffer (once per item)
+  kPQKReady = 3,   // [2] CTA 0: K_lo + Q_lo of both CTAs (8 prep warps)
+  kPVReady = 5,    // [2] CTA 0: V_lo of both CTAs (8 prep warps)
+  kPSDone = 7,     // S MMAs done (both CTAs, once per item)
+  kPODone = 8,     // P.V MMAs done (both CTAs, once per item): V buffer free
+  kPLoFree = 9,    // [2] chunk c's P.V done: P_lo slot c & 1 free for c + 2 (both CTAs)
+  kPSlotFree = 11, // [2] own epilogue done with the slot (8 softmax warps)
+  kPChunk = 13,    // [8] CTA 0: P chunk c written in both CTAs (8 softmax warps)
+  kPNumBars = 21
 };
 
 __device__ __forceinline__ bool decode_long(int it, int H, const int* __restrict__ cu, Item& w) {
@@ -545,10 +586,10 @@ __global__ void __maxnreg__(128)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kSBarOff);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kPBarOff);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + kPNumBars);
   volatile uint32_t* abort_flag = tslot + 1;
-  uint8_t* vpre = smem + kSVpre;
+  uint8_t* vbuf = smem + kPVbuf;
 
   const uint32_t rank = cluster_ctarank();
   const int stride = static_cast<int>(gridDim.x >> 1);
@@ -574,12 +615,15 @@ __global__ void __maxnreg__(128)
     }
     mbar_init(&bar[kPSDone], 1);
     mbar_init(&bar[kPODone], 1);
-    for (int j = 0; j < 4; ++j) mbar_init(&bar[kPLoFree + j], 1);
+    for (int j = 0; j < 2; ++j) mbar_init(&bar[kPLoFree + j], 1);
     for (int c = 0; c < LMAX2 / KC; ++c) mbar_init(&bar[kPChunk + c], 8);
-    mbar_init(&bar[kPFullVpre], 1);
-    mbar_init(&bar[kPVpreFree], 4);
+    mbar_init(&bar[kPFullV], 1);
     *abort_flag = 0u;
     fence_barrier_init();
+  }
+  if (tid < 64) {
+    reinterpret_cast<uint4*>(smem + kPZero)[tid] = make_uint4(0u, 0u, 0u, 0u);
+    fence_proxy_async_smem();
   }
   if (warp == 1) {
     tmem_alloc_pair(tslot, 512);
@@ -605,7 +649,7 @@ __global__ void __maxnreg__(128)
       prefetch_tmap(&tmV);
       while (true) {
         const int s = n & 1;
-        uint8_t* slot = smem + s * kSlotBytes;
+        uint8_t* slot = smem + kPSlot0 + s * kSlotBytes;
         const int half = ((cur.L + 15) & ~15) >> 1;  // this CTA's K rows start at rank * half
         if (n >= 2 && !(ok = mbar_wait_abort(&bar[kPSlotFree + s], ((n >> 1) + 1) & 1, status, abort_flag)))
           break;
@@ -616,12 +660,11 @@ __global__ void __maxnreg__(128)
           tma_load_2d(slot + kOffKV + blk * 16384, &tmK, &bar[kPFullQK + s], cur.h * DH + 32 * blk,
                       cur.s0 + half * static_cast<int>(rank));
         }
-        // V right behind, into the prefetch buffer once prep has moved item
-        // n-1's V out of it.
-        if (n >= 1 && !(ok = mbar_wait_abort(&bar[kPVpreFree], (n - 1) & 1, status, abort_flag))) break;
-        mbar_arrive_expect_tx(&bar[kPFullVpre], 2 * 16384);
+        // V right behind, into the V buffer once item n-1's P.V is done.
+        if (n >= 1 && !(ok = mbar_wait_abort(&bar[kPODone], (n - 1) & 1, status, abort_flag))) break;
+        mbar_arrive_expect_tx(&bar[kPFullV], 2 * 16384);
         for (int kb = 0; kb < 2; ++kb)
-          tma_load_2d(vpre + kb * 16384, &tmV, &bar[kPFullVpre],
+          tma_load_2d(vbuf + kb * 16384, &tmV, &bar[kPFullV],
                       cur.h * DH + 32 * static_cast<int>(rank), cur.s0 + 128 * kb);
         Item nxt;
         const int itn = next_long(it + stride, stride, n_items, H, cu, nxt);
@@ -635,14 +678,15 @@ __global__ void __maxnreg__(128)
     // ============================================ MMA issuer (CTA 0)
     if (lane == 0 && rank == 0) {
       uint32_t cpar = 0;
-      const uint32_t idO = idesc_tf32_bmn(2 * QB, DH);
+      const uint32_t idO2 = idesc_tf32_bmn(2 * QB, 2 * DH);
+      const uint32_t zero = smem_u32(smem + kPZero), vb = smem_u32(vbuf);
       auto commit_both = [&](int i) {
         mma_commit_pair(smem_u32(&bar[i]));
         mma_commit_pair(mapa_shared(smem_u32(&bar[i]), 1));
       };
       while (true) {
         const int s = n & 1;
-        const uint32_t slot = smem_u32(smem + s * kSlotBytes);
+        const uint32_t slot = smem_u32(smem + kPSlot0 + s * kSlotBytes);
         const int L = cur.L, Lk16 = (L + 15) & ~15, nchunk = (L + KC - 1) / KC;
         if (!(ok = mbar_wait_cluster_abort(&bar[kPQKReady + s], (n >> 1) & 1, status, abort_flag))) break;
         // The single S buffer: item n-1's P.V must be done with it.
@@ -667,16 +711,17 @@ __global__ void __maxnreg__(128)
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < KC / 8; ++kk) {
-            const uint32_t vo = static_cast<uint32_t>(c * 4096 + kk * 1024);
-            const uint64_t v_raw = sw128b32_mnmajor_desc(slot + kOffKV + vo, 16384);
-            const uint64_t v_lo = sw128b32_mnmajor_desc(slot + kOffLo + vo, 16384);
+            // Each CTA's B: its 32 dh columns of V (8 keys) and, one LBO
+            // further, of V_lo -- or the zero block for the P_lo term.
+            const uint32_t vs = vb + static_cast<uint32_t>(c * 4096 + kk * 1024);
+            const uint64_t v_all = sw128b32_mnmajor_desc(vs, slot + kOffLo - vb);
+            const uint64_t v_zero = sw128b32_mnmajor_desc(vs, zero - vs);
             const uint32_t p_hi = tmem + 32u * c + 8u * kk;
-            const uint32_t p_lo = tmem + kColPlo + 32u * (c & 3) + 8u * kk;
-            mma_tf32_ts_pair(tmem + kColO, p_hi, v_raw, idO, (c | kk) != 0 ? 1u : 0u);
-            mma_tf32_ts_pair(tmem + kColO, p_hi, v_lo, idO, 1u);
-            mma_tf32_ts_pair(tmem + kColO, p_lo, v_raw, idO, 1u);
+            const uint32_t p_lo = tmem + kColPlo + 32u * (c & 1) + 8u * kk;
+            mma_tf32_ts_pair(tmem + kColO, p_hi, v_all, idO2, (c | kk) != 0 ? 1u : 0u);
+            mma_tf32_ts_pair(tmem + kColO, p_lo, v_zero, idO2, 1u);
           }
-          if (c + 4 < nchunk) commit_both(kPLoFree + (c & 3));
+          if (c + 2 < nchunk) commit_both(kPLoFree + (c & 1));
         }
         if (!ok) break;
         commit_both(kPODone);
@@ -696,15 +741,10 @@ __global__ void __maxnreg__(128)
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
     while (true) {
       const int s = n & 1;
-      uint8_t* slot = smem + s * kSlotBytes;
+      uint8_t* slot = smem + kPSlot0 + s * kSlotBytes;
       const int L = cur.L;
       if (!(ok = mbar_wait_abort(&bar[kPFullQK + s], (n >> 1) & 1, status, abort_flag))) break;
-#pragma unroll 4
-      for (int i = 0; i < 16; ++i) {
-        const uint32_t o = static_cast<uint32_t>((ptid + i * 128) * 16);
-        *reinterpret_cast<float4*>(slot + kOffLo + o) =
-            tf32_lo4(*reinterpret_cast<const float4*>(slot + kOffKV + o));
-      }
+      tile_lo_32k(smem_u32(slot + kOffKV), smem_u32(slot + kOffLo), ptid);
       if (n >= 1 && !(ok = mbar_wait_abort(&bar[kPSDone], (n - 1) & 1, status, abort_flag))) break;
       tc_fence_after();
 #pragma unroll
@@ -712,8 +752,8 @@ __global__ void __maxnreg__(128)
         uint32_t lo[32];
 #pragma unroll
         for (int c4 = 0; c4 < 8; ++c4) {
-          const float4 x = *reinterpret_cast<const float4*>(
-              slot + kOffQ + blk * 16384 + row * 128 + ((c4 ^ (row & 7)) << 4));
+          const float4 x = lds128(smem_u32(slot + kOffQ + blk * 16384 + row * 128) +
+                                  static_cast<uint32_t>((c4 ^ (row & 7)) << 4));
           const float4 l = tf32_lo4(x);
           lo[4 * c4] = __float_as_uint(l.x);
           lo[4 * c4 + 1] = __float_as_uint(l.y);
@@ -727,25 +767,32 @@ __global__ void __maxnreg__(128)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) arrive_leader(kPQKReady + s);
-      // V (prefetched; this CTA's 32 dh columns x 256 keys) into the slot
-      // once S has consumed K, with V_lo; keys >= L zeroed.
+      // V_lo (this CTA's 32 dh columns x 256 keys) into the slot once S has
+      // consumed K_lo; keys >= L zeroed in the V buffer too.
       if (!(ok = mbar_wait_abort(&bar[kPSDone], n & 1, status, abort_flag))) break;
-      if (!(ok = mbar_wait_abort(&bar[kPFullVpre], n & 1, status, abort_flag))) break;
-#pragma unroll 4
-      for (int i = 0; i < 16; ++i) {
-        const uint32_t o = static_cast<uint32_t>((ptid + i * 128) * 16);
-        const int key = static_cast<int>(o >> 7);
-        float4 x = *reinterpret_cast<const float4*>(vpre + o);
-        if (key >= L) x = make_float4(0.f, 0.f, 0.f, 0.f);
-        *reinterpret_cast<float4*>(slot + kOffKV + o) = x;
-        *reinterpret_cast<float4*>(slot + kOffLo + o) = tf32_lo4(x);
+      if (!(ok = mbar_wait_abort(&bar[kPFullV], n & 1, status, abort_flag))) break;
+      {
+        const uint32_t vb = smem_u32(vbuf), lo = smem_u32(slot + kOffLo);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          float4 x[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            x[i] = lds128(vb + static_cast<uint32_t>((ptid + (h * 8 + i) * 128) * 16));
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const uint32_t o = static_cast<uint32_t>((ptid + (h * 8 + i) * 128) * 16);
+            if (static_cast<int>(o >> 7) >= L) {
+              x[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+              sts128(vb + o, x[i]);
+            }
+            sts128(lo + o, tf32_lo4(x[i]));
+          }
+        }
       }
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        arrive_leader(kPVReady + s);
-        mbar_arrive(&bar[kPVpreFree]);
-      }
+      if (lane == 0) arrive_leader(kPVReady + s);
       Item nxt;
       const int itn = next_long(it + stride, stride, n_items, H, cu, nxt);
       if (itn >= n_items) break;
@@ -762,10 +809,10 @@ __global__ void __maxnreg__(128)
     const int stid = sw * 32 + lane;
     const int lrow = stid >> 4, col4 = (stid & 15) * 4;
     const int q0 = QB * static_cast<int>(rank);
-    uint32_t lo_par = 0;  // phase bits of the four P_lo-free barriers
+    uint32_t lo_par = 0;  // phase bits of the two P_lo-free barriers
     while (true) {
       const int s = n & 1;
-      uint8_t* slot = smem + s * kSlotBytes;
+      uint8_t* slot = smem + kPSlot0 + s * kSlotBytes;
       // Row max / sum exchange in the slot's Q region (dead once S is done).
       float (*red_max)[QB] = reinterpret_cast<float (*)[QB]>(slot + kOffQ);
       float (*red_sum)[QB] = reinterpret_cast<float (*)[QB]>(slot + kOffQ + 1024);
@@ -780,12 +827,12 @@ __global__ void __maxnreg__(128)
         break;
       }
       mx = fmaxf(red_max[0][row], red_max[1][row]);
-      // Chunk c >= 4 reuses P_lo slot c & 3 once chunk c - 4's P.V is done.
+      // Chunk c >= 2 reuses P_lo slot c & 1 once chunk c - 2's P.V is done.
       const float sum = p_chunks(
-          tS, tmem + kColPlo + lane_off, par, nchunk, L, mx,
+          tS, tmem + kColPlo + lane_off, 1u, par, nchunk, L, mx,
           [&](int c) {
-            if (c >= 4) {
-              const int j = c & 3;
+            if (c >= 2) {
+              const int j = c & 1;
               if (ok) ok = mbar_wait_abort(&bar[kPLoFree + j], (lo_par >> j) & 1u, status, abort_flag);
               lo_par ^= 1u << j;
               tc_fence_after();
@@ -799,9 +846,14 @@ __global__ void __maxnreg__(128)
       const float total = __fadd_rn(red_sum[0][row], red_sum[1][row]);
       const bool w1 = ok && mbar_wait_abort(&bar[kPODone], n & 1, status, abort_flag);
       tc_fence_after();
-      uint32_t o[32];
-      tmem_ld32(tmem + kColO + lane_off + 32u * par, o);
+      // O columns: [P V | P V_lo] of dh 0-31 (CTA 0's B), then of dh 32-63.
+      uint32_t o[32], ob[32];
+      tmem_ld32(tmem + kColO + lane_off + 64u * par, o);
+      tmem_ld32(tmem + kColO + lane_off + 64u * par + 32u, ob);
       tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        o[j] = __float_as_uint(__fadd_rn(__uint_as_float(o[j]), __uint_as_float(ob[j])));
       {
         const float inv = __fdiv_rn(1.0f, total);
         const bool live = q0 + row < L;
@@ -935,7 +987,7 @@ cudaError_t launch_attention_tma_pair(const float* q, const float* k, const floa
   const uint64_t bit = 1ull << (dev & 63);
   if ((attr_set.load() & bit) == 0) {
     cudaError_t e = cudaFuncSetAttribute(attention_tma_pair_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSSmemBytes);
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytes);
     if (e != cudaSuccess) return e;
     attr_set.fetch_or(bit);
   }
@@ -945,7 +997,7 @@ cudaError_t launch_attention_tma_pair(const float* q, const float* k, const floa
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = kSSmemBytes;
+  cfg.dynamicSmemBytes = kPSmemBytes;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
