@@ -106,22 +106,6 @@ __device__ __forceinline__ float4 tf32_lo4(float4 x) {
   return make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w));
 }
 
-// 16-byte shared-memory accesses by 32-bit shared address (the kernels'
-// aligned dynamic shared-memory pointer is generic to the compiler).
-__device__ __forceinline__ float4 lds128(uint32_t a) {
-  float4 v;
-  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(a)
-               : "memory");
-  return v;
-}
-__device__ __forceinline__ void sts128(uint32_t a, float4 v) {
-  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(a), "f"(v.x), "f"(v.y), "f"(v.z),
-               "f"(v.w)
-               : "memory");
-}
-
 // lo = x - tf32(x) over a 32 KB tile, 128 threads, 16 bytes per thread per
 // 2 KB step, eight loads in flight.
 __device__ __forceinline__ void tile_lo_32k(uint32_t src, uint32_t dst, int ptid) {
@@ -171,21 +155,24 @@ __device__ __forceinline__ float ex2_ftz(float x) {
 // Row max over the valid keys of one softmax warp's chunks (c = par, par+2,
 // ...; 32 keys each, S chunk c at TMEM column tS + 32 c).
 __device__ __forceinline__ float s_row_max(uint32_t tS, int par, int nchunk, int L) {
-  float mx = -INFINITY;
+  float m0 = -INFINITY, m1 = -INFINITY;  // two chains (max is order-free)
   for (int c = par; c < nchunk; c += 2) {
     uint32_t r[32];
     tmem_ld32(tS + 32u * c, r);
     tmem_ld_wait();
     if (c * 32 + 32 <= L) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) mx = fmaxf(mx, __uint_as_float(r[j]));
+      for (int j = 0; j < 32; j += 2) {
+        m0 = fmaxf(m0, __uint_as_float(r[j]));
+        m1 = fmaxf(m1, __uint_as_float(r[j + 1]));
+      }
     } else {
 #pragma unroll
       for (int j = 0; j < 32; ++j)
-        if (c * 32 + j < L) mx = fmaxf(mx, __uint_as_float(r[j]));
+        if (c * 32 + j < L) m0 = fmaxf(m0, __uint_as_float(r[j]));
     }
   }
-  return mx;
+  return fmaxf(m0, m1);
 }
 
 // One softmax warp's P chunks (c = par, par+2, ...): P = 2^((S - mx) log2 e)
@@ -296,14 +283,15 @@ __global__ void __maxnreg__(128)
           tma_load_2d(slot + kOffQ + blk * 16384, &tmQ, &bar[kFullQK + s], cur.h * DH + 32 * blk, cur.s0);
           tma_load_2d(slot + kOffKV + blk * 16384, &tmK, &bar[kFullQK + s], cur.h * DH + 32 * blk, cur.s0);
         }
+        // The next item, looked up while this one's wait is pending.
+        Item nxt;
+        const int itn = next_item(it + stride, stride, n_items, H, cu, nxt);
         // V right behind, into the prefetch buffer once prep has moved item
         // n-1's V out of it.
         if (n >= 1 && !(ok = mbar_wait_abort(&bar[kVpreFree], (n - 1) & 1, status, abort_flag))) break;
         mbar_arrive_expect_tx(&bar[kFullVpre], 2 * 16384);
         for (int blk = 0; blk < 2; ++blk)
           tma_load_2d(vpre + blk * 16384, &tmV, &bar[kFullVpre], cur.h * DH + 32 * blk, cur.s0);
-        Item nxt;
-        const int itn = next_item(it + stride, stride, n_items, H, cu, nxt);
         if (itn >= n_items) break;
         it = itn;
         cur = nxt;
@@ -338,6 +326,9 @@ __global__ void __maxnreg__(128)
           mma_tf32_ts(tS, tmem + kSColQlo + 8u * kk, b_raw, idS, 1u);
         }
         mma_commit(&bar[kSDone + s]);
+        // The next item, looked up while this one's wait is pending.
+        Item nxt;
+        const int itn = next_item(it + stride, stride, n_items, H, cu, nxt);
         if (!(ok = mbar_wait_abort(&bar[kVReady + s], (n >> 1) & 1, status, abort_flag))) break;
         for (int c = 0; c < nchunk; ++c) {
           if (!(ok = mbar_wait_abort(&bar[kChunk + c], (cpar >> c) & 1u, status, abort_flag))) break;
@@ -358,8 +349,6 @@ __global__ void __maxnreg__(128)
         }
         if (!ok) break;
         mma_commit(&bar[kODone + s]);
-        Item nxt;
-        const int itn = next_item(it + stride, stride, n_items, H, cu, nxt);
         if (itn >= n_items) break;
         it = itn;
         cur = nxt;
@@ -404,6 +393,9 @@ __global__ void __maxnreg__(128)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[kQKReady + s]);
+      // The next item, looked up while this one's wait is pending.
+      Item nxt;
+      const int itn = next_item(it + stride, stride, n_items, H, cu, nxt);
       // V (prefetched) into the slot once S has consumed K, with V_lo;
       // rows (keys) >= L are zeroed in both parts.
       if (!(ok = mbar_wait_abort(&bar[kSDone + s], (n >> 1) & 1, status, abort_flag))) break;
@@ -431,8 +423,6 @@ __global__ void __maxnreg__(128)
         mbar_arrive(&bar[kVReady + s]);
         mbar_arrive(&bar[kVpreFree]);
       }
-      Item nxt;
-      const int itn = next_item(it + stride, stride, n_items, H, cu, nxt);
       if (itn >= n_items) break;
       it = itn;
       cur = nxt;
@@ -471,6 +461,9 @@ __global__ void __maxnreg__(128)
             if (lane == 0) mbar_arrive(&bar[kChunk + c]);
           });
       red_sum[par][row] = sum;
+      // The next item, looked up while this one's wait is pending.
+      Item nxt;
+      const int itn = next_item(it + stride, stride, n_items, H, cu, nxt);
       soft_sync();
       const float total = __fadd_rn(red_sum[0][row], red_sum[1][row]);
       // ---- O / sum -> staging (the slot's V region, free once P.V is done)
@@ -513,8 +506,6 @@ __global__ void __maxnreg__(128)
       fence_proxy_async_smem();  // generic writes in the slot precede its next TMA fill
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[kSlotFree + s]);
-      Item nxt;
-      const int itn = next_item(it + stride, stride, n_items, H, cu, nxt);
       if (itn >= n_items) break;
       it = itn;
       cur = nxt;
@@ -554,13 +545,13 @@ enum : int {
   kPFullQK = 0,    // [2] own TMA Q + K landed
   kPFullV = 2,     // own TMA V landed in the V buffer (once per item)
   kPQKReady = 3,   // [2] CTA 0: K_lo + Q_lo of both CTAs (8 prep warps)
-  kPVReady = 5,    // [2] CTA 0: V_lo of both CTAs (8 prep warps)
-  kPSDone = 7,     // S MMAs done (both CTAs, once per item)
-  kPODone = 8,     // P.V MMAs done (both CTAs, once per item): V buffer free
-  kPLoFree = 9,    // [2] chunk c's P.V done: P_lo slot c & 1 free for c + 2 (both CTAs)
-  kPSlotFree = 11, // [2] own epilogue done with the slot (8 softmax warps)
-  kPChunk = 13,    // [8] CTA 0: P chunk c written in both CTAs (8 softmax warps)
-  kPNumBars = 21
+  kPVReady = 5,    // [2][2] CTA 0: V_lo of keys [128 h, 128 h + 128), both CTAs (8 prep warps)
+  kPSDone = 9,     // S MMAs done (both CTAs, once per item)
+  kPODone = 10,    // P.V MMAs done (both CTAs, once per item): V buffer free
+  kPLoFree = 11,   // [2] chunk c's P.V done: P_lo slot c & 1 free for c + 2 (both CTAs)
+  kPSlotFree = 13, // [2] own epilogue done with the slot (8 softmax warps)
+  kPChunk = 15,    // [8] CTA 0: P chunk c written in both CTAs (8 softmax warps)
+  kPNumBars = 23
 };
 
 __device__ __forceinline__ bool decode_long(int it, int H, const int* __restrict__ cu, Item& w) {
@@ -610,7 +601,8 @@ __global__ void __maxnreg__(128)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar[kPFullQK + i], 1);
       mbar_init(&bar[kPQKReady + i], 8);
-      mbar_init(&bar[kPVReady + i], 8);
+      mbar_init(&bar[kPVReady + 2 * i], 8);
+      mbar_init(&bar[kPVReady + 2 * i + 1], 8);
       mbar_init(&bar[kPSlotFree + i], 8);
     }
     mbar_init(&bar[kPSDone], 1);
@@ -660,14 +652,15 @@ __global__ void __maxnreg__(128)
           tma_load_2d(slot + kOffKV + blk * 16384, &tmK, &bar[kPFullQK + s], cur.h * DH + 32 * blk,
                       cur.s0 + half * static_cast<int>(rank));
         }
+        // The next item, looked up while this one's wait is pending.
+        Item nxt;
+        const int itn = next_long(it + stride, stride, n_items, H, cu, nxt);
         // V right behind, into the V buffer once item n-1's P.V is done.
         if (n >= 1 && !(ok = mbar_wait_abort(&bar[kPODone], (n - 1) & 1, status, abort_flag))) break;
         mbar_arrive_expect_tx(&bar[kPFullV], 2 * 16384);
         for (int kb = 0; kb < 2; ++kb)
           tma_load_2d(vbuf + kb * 16384, &tmV, &bar[kPFullV],
                       cur.h * DH + 32 * static_cast<int>(rank), cur.s0 + 128 * kb);
-        Item nxt;
-        const int itn = next_long(it + stride, stride, n_items, H, cu, nxt);
         if (itn >= n_items) break;
         it = itn;
         cur = nxt;
@@ -704,8 +697,13 @@ __global__ void __maxnreg__(128)
           mma_tf32_ts_pair(tmem, tmem + kColQlo + 8u * kk, b_raw, idS, 1u);
         }
         commit_both(kPSDone);
-        if (!(ok = mbar_wait_cluster_abort(&bar[kPVReady + s], (n >> 1) & 1, status, abort_flag))) break;
+        // The next item, looked up while this one's wait is pending.
+        Item nxt;
+        const int itn = next_long(it + stride, stride, n_items, H, cu, nxt);
         for (int c = 0; c < nchunk; ++c) {
+          if ((c & 3) == 0 &&  // V_lo of keys [32 c, 32 c + 128)
+              !(ok = mbar_wait_cluster_abort(&bar[kPVReady + 2 * s + (c >> 2)], (n >> 1) & 1, status, abort_flag)))
+            break;
           if (!(ok = mbar_wait_cluster_abort(&bar[kPChunk + c], (cpar >> c) & 1u, status, abort_flag))) break;
           cpar ^= 1u << c;
           tc_fence_after();
@@ -725,8 +723,6 @@ __global__ void __maxnreg__(128)
         }
         if (!ok) break;
         commit_both(kPODone);
-        Item nxt;
-        const int itn = next_long(it + stride, stride, n_items, H, cu, nxt);
         if (itn >= n_items) break;
         it = itn;
         cur = nxt;
@@ -767,6 +763,9 @@ __global__ void __maxnreg__(128)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) arrive_leader(kPQKReady + s);
+      // The next item, looked up while this one's wait is pending.
+      Item nxt;
+      const int itn = next_long(it + stride, stride, n_items, H, cu, nxt);
       // V_lo (this CTA's 32 dh columns x 256 keys) into the slot once S has
       // consumed K_lo; keys >= L zeroed in the V buffer too.
       if (!(ok = mbar_wait_abort(&bar[kPSDone], n & 1, status, abort_flag))) break;
@@ -788,13 +787,11 @@ __global__ void __maxnreg__(128)
             }
             sts128(lo + o, tf32_lo4(x[i]));
           }
+          fence_proxy_async_smem();  // keys [128 h, 128 h + 128) ready
+          __syncwarp();
+          if (lane == 0) arrive_leader(kPVReady + 2 * s + h);
         }
       }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) arrive_leader(kPVReady + s);
-      Item nxt;
-      const int itn = next_long(it + stride, stride, n_items, H, cu, nxt);
       if (itn >= n_items) break;
       it = itn;
       cur = nxt;
@@ -842,6 +839,9 @@ __global__ void __maxnreg__(128)
             if (lane == 0) arrive_leader(kPChunk + c);
           });
       red_sum[par][row] = sum;
+      // The next item, looked up while this one's wait is pending.
+      Item nxt;
+      const int itn = next_long(it + stride, stride, n_items, H, cu, nxt);
       soft_sync();
       const float total = __fadd_rn(red_sum[0][row], red_sum[1][row]);
       const bool w1 = ok && mbar_wait_abort(&bar[kPODone], n & 1, status, abort_flag);
@@ -884,8 +884,6 @@ __global__ void __maxnreg__(128)
       fence_proxy_async_smem();  // generic writes in the slot precede its next TMA fill
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[kPSlotFree + s]);
-      Item nxt;
-      const int itn = next_long(it + stride, stride, n_items, H, cu, nxt);
       if (itn >= n_items) break;
       it = itn;
       cur = nxt;
