@@ -294,28 +294,36 @@ __global__ void __maxnreg__(EW == 16 ? 96 : 168)
           prefetch_l1(p.epi.sin_t + static_cast<long>(pos_m) * 64);
         }
       }
-      if (!epi_all<EW>(mbar_wait(&tfull[acc], acc_phase, p.status))) break;
-      tc_fence_after();
+      // The tile's scales and bias are loaded before the accumulator wait so
+      // their latency overlaps it: the activation scale, and this thread's
+      // column (at most one) of the w_scale / bias vectors.
+      static_assert(BN <= EW * 32, "one vector column per epilogue thread");
       const long m = static_cast<long>(m_base) + row_in_tile;
       const bool row_ok = m < p.M;
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
-                             static_cast<uint32_t>(acc * BN);
       float as = 1.0f;  // the raw-accumulator mode carries no activation scale
       if (row_ok && p.acc_out == nullptr) as = p.per_token ? __ldg(p.a_scale + m) : __ldg(p.a_scale);
-
-      // This tile's w_scale / bias columns, copied once into shared memory by
-      // the epilogue warps (tail columns read the last valid column).
-      float* wsv = colvec;
-      float* bsv = colvec + BN;
       // Per-tensor scale: ws[n]*as is the same for every row, so the rounded
       // product (the reference rounds it before the fma) is formed once.
       const float as_col = p.per_token ? 1.0f : (p.acc_out ? 1.0f : __ldg(p.a_scale));
-      if (p.acc_out == nullptr) {
-        for (int j = etid; j < BN; j += EW * 32) {
-          const int n = min(n_blk * BN + j, p.N - 1);
-          wsv[j] = p.per_token ? __ldg(p.w_scale + n) : __fmul_rn(__ldg(p.w_scale + n), as_col);
-          bsv[j] = p.bias ? __ldg(p.bias + n) : 0.0f;
-        }
+      const bool has_col = p.acc_out == nullptr && etid < BN;
+      float ws_col = 0.0f, b_col = 0.0f;
+      if (has_col) {  // tail columns read the last valid column
+        const int n = min(n_blk * BN + etid, p.N - 1);
+        ws_col = __ldg(p.w_scale + n);
+        b_col = p.bias ? __ldg(p.bias + n) : 0.0f;
+      }
+      if (!epi_all<EW>(mbar_wait(&tfull[acc], acc_phase, p.status))) break;
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                             static_cast<uint32_t>(acc * BN);
+
+      // This tile's w_scale / bias columns in shared memory for all epilogue
+      // warps.
+      float* wsv = colvec;
+      float* bsv = colvec + BN;
+      if (has_col) {
+        wsv[etid] = p.per_token ? ws_col : __fmul_rn(ws_col, as_col);
+        bsv[etid] = b_col;
       }
       epi_barrier<EW>();  // vectors filled
       // Dequant of 32 accumulators at tile columns jc0.. (jc0 a multiple of
