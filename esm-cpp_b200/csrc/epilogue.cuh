@@ -58,19 +58,20 @@ __device__ __forceinline__ float epi_row_run(const EpiParams& e, long m, int c0,
 }
 
 // The q-scale and RoPE of epi_qkv_rope_head on the values only (the caller
-// stores them); which = 0 (q), 1 (k), 2 (v); p = the row's position.
-__device__ __forceinline__ void epi_qkv_rope_values(const EpiParams& e, int p, int which,
-                                                    float (&y)[64]) {
+// stores them); which = 0 (q), 1 (k), 2 (v).  The row's cos / sin table
+// entries 0..31 are in shared memory at cs_row (cos) and cs_row + 128 (sin),
+// 16-byte chunk i4 at position i4 ^ swz.
+__device__ __forceinline__ void epi_qkv_rope_values(const EpiParams& e, uint32_t cs_row,
+                                                    int swz, int which, float (&y)[64]) {
   if (which == 0) {
 #pragma unroll
     for (int j = 0; j < 64; ++j) y[j] = __fmul_rn(y[j], e.q_scale);
   }
   if (which <= 1) {
-    const float4* c4 = reinterpret_cast<const float4*>(e.cos_t + static_cast<long>(p) * 64);
-    const float4* s4 = reinterpret_cast<const float4*>(e.sin_t + static_cast<long>(p) * 64);
 #pragma unroll
     for (int i4 = 0; i4 < 8; ++i4) {
-      const float4 cv = __ldg(c4 + i4), sv = __ldg(s4 + i4);
+      const uint32_t o = static_cast<uint32_t>((i4 ^ swz) << 4);
+      const float4 cv = lds128(cs_row + o), sv = lds128(cs_row + 128u + o);
       const float cc[4] = {cv.x, cv.y, cv.z, cv.w}, ss[4] = {sv.x, sv.y, sv.z, sv.w};
 #pragma unroll
       for (int k = 0; k < 4; ++k) {

@@ -42,7 +42,7 @@ constexpr int BK = 128;  // bytes of K per stage = one 128-byte swizzle row
 constexpr int threads_for(int ew) { return 64 + 32 * ew; }  // + producer, MMA issuer
 constexpr int kSmemLimit = 232448;                            // opt-in maximum per CTA
 
-template <int BN, bool PAIR, int EW>
+template <int BN, bool PAIR, int EW, int ROPE = 0>
 struct Cfg {
   static constexpr int A_BYTES = BM * BK;
   static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * BK;  // this CTA's rows of W
@@ -53,11 +53,15 @@ struct Cfg {
   // tile's (w_scale * a_scale) and bias columns shared by the epilogue warps.
   static constexpr int STAGING_BYTES = EW * 4096;
   static constexpr int COLVEC_BYTES = 2 * BN * 4;
+  // RoPE epilogue: the tile rows' cos / sin table entries 0..31 (128 rows x
+  // 256 bytes), staged once per tile.
+  static constexpr int ROPE_BYTES = ROPE ? BM * 256 : 0;
   // As many stages as the rest of shared memory holds (at most 8).
-  static constexpr int FIT = (kSmemLimit - 1024 - 256 - STAGING_BYTES - COLVEC_BYTES) / STAGE_BYTES;
+  static constexpr int FIT =
+      (kSmemLimit - 1024 - 256 - STAGING_BYTES - COLVEC_BYTES - ROPE_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = FIT < 8 ? FIT : 8;
-  static constexpr int SMEM =
-      STAGES * STAGE_BYTES + STAGING_BYTES + COLVEC_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + STAGING_BYTES + COLVEC_BYTES + ROPE_BYTES +
+                              1024 /*align*/ + 256 /*barriers*/;
 };
 
 struct Params {
@@ -103,7 +107,7 @@ __global__ void __maxnreg__(EW == 16 ? 96 : 168)
                    const __grid_constant__ CUtensorMap tmC0,
                    const __grid_constant__ CUtensorMap tmC1,
                    const __grid_constant__ CUtensorMap tmC2, const Params p) {
-  using C = Cfg<BN, PAIR, EW>;
+  using C = Cfg<BN, PAIR, EW, EPI == kEpiQkvRope>;
   constexpr int kEpiPerQuad = EW / 4;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -112,7 +116,9 @@ __global__ void __maxnreg__(EW == 16 ? 96 : 168)
   uint8_t* sB = smem + C::STAGES * C::A_BYTES;
   uint8_t* staging = smem + C::STAGES * C::STAGE_BYTES;
   float* colvec = reinterpret_cast<float*>(staging + C::STAGING_BYTES);
-  uint64_t* full = reinterpret_cast<uint64_t*>(staging + C::STAGING_BYTES + C::COLVEC_BYTES);
+  uint8_t* rope_cs = staging + C::STAGING_BYTES + C::COLVEC_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + C::STAGING_BYTES + C::COLVEC_BYTES +
+                                               C::ROPE_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
@@ -283,15 +289,26 @@ __global__ void __maxnreg__(EW == 16 ? 96 : 168)
     for (int tile = first_tile; tile < num_tiles; tile += tile_stride) {
       const int m_base = tile_m_base(tile);
       const int n_blk = tile / m_units;
-      // RoPE: this row's position, and its cos / sin table rows prefetched
-      // into L1 while the accumulator is still being computed.
-      int pos_m = 0;
-      if (EPI == kEpiQkvRope && p.tma) {
-        const long mm = static_cast<long>(m_base) + row_in_tile;
-        if (mm < p.M) {
-          pos_m = __ldg(p.epi.pos + mm);
-          prefetch_l1(p.epi.cos_t + static_cast<long>(pos_m) * 64);
-          prefetch_l1(p.epi.sin_t + static_cast<long>(pos_m) * 64);
+      // RoPE: the quadrant's 32 rows' cos (warp sub 0) or sin (sub 1) table
+      // entries 0..31 into shared memory while the accumulator is still being
+      // computed, 8 lanes per 128-byte row (coalesced); row r's 16-byte chunk
+      // k goes to position k ^ (r & 7) so the per-row reads are conflict-free.
+      // The previous tile's readers are past the tile-end barrier; this
+      // tile's read after the vectors-filled barrier.
+      if constexpr (EPI == kEpiQkvRope) {
+        static_assert(EW / 4 == 2, "two epilogue warps per TMEM lane quadrant");
+        if (p.tma) {
+          const long mm = static_cast<long>(m_base) + row_in_tile;
+          const int pos_m = mm < p.M ? __ldg(p.epi.pos + mm) : 0;
+          const float* tab = sub == 0 ? p.epi.cos_t : p.epi.sin_t;
+          uint8_t* qreg = rope_cs + quad * 32 * 256 + sub * 128;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int r = i * 4 + (lane >> 3), k = lane & 7;
+            const int pr = __shfl_sync(0xffffffffu, pos_m, r);
+            const float4 v = __ldg(reinterpret_cast<const float4*>(tab + static_cast<long>(pr) * 64) + k);
+            sts128(smem_u32(qreg + r * 256 + ((k ^ (r & 7)) << 4)), v);
+          }
         }
       }
       // The tile's scales and bias are loaded before the accumulator wait so
@@ -418,7 +435,7 @@ __global__ void __maxnreg__(EW == 16 ? 96 : 168)
             if (p.tma) {
               const int which = n_base / p.epi.d;
               const int col = n_base - which * p.epi.d;
-              epi_qkv_rope_values(p.epi, pos_m, which, y);
+              epi_qkv_rope_values(p.epi, smem_u32(rope_cs + row_in_tile * 256), lane & 7, which, y);
               const CUtensorMap* mp = which == 0 ? &tmC0 : (which == 1 ? &tmC1 : &tmC2);
 #pragma unroll
               for (int half = 0; half < 2; ++half) {
@@ -520,7 +537,7 @@ bool make_tmap_f32(CUtensorMap* map, const float* base, long rows, long cols, lo
 
 template <int BN, int EPI, bool PAIR, int EW>
 cudaError_t launch_bn(const GemmI8Args& a, cudaStream_t s) {
-  using C = Cfg<BN, PAIR, EW>;
+  using C = Cfg<BN, PAIR, EW, EPI == kEpiQkvRope>;
   constexpr int kThreads = threads_for(EW);
   CUtensorMap tmA, tmB, tmC[3];
   if (!make_tmap_i8(&tmA, a.A, a.M, a.K, a.lda, BM)) return cudaErrorInvalidValue;
