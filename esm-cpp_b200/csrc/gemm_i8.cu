@@ -346,12 +346,12 @@ __global__ void __maxnreg__(EW == 16 ? 96 : 168)
       // Dequant of 32 accumulators at tile columns jc0.. (jc0 a multiple of
       // 4): fma(float(acc), ws[n]*as, bias[n]) (gemm_int8.cpp:109-126), the
       // column vectors read as float4.
+      const uint32_t wsv_s = smem_u32(wsv), bsv_s = smem_u32(bsv);
       auto deq32 = [&](const uint32_t(&r)[32], int jc0, float* y) {
-        const float4* w4 = reinterpret_cast<const float4*>(wsv + jc0);
-        const float4* b4 = reinterpret_cast<const float4*>(bsv + jc0);
 #pragma unroll
         for (int j4 = 0; j4 < 8; ++j4) {
-          const float4 w = w4[j4], b = b4[j4];
+          const uint32_t o = static_cast<uint32_t>((jc0 + 4 * j4) * 4);
+          const float4 w = lds128(wsv_s + o), b = lds128(bsv_s + o);
           const float ws[4] = {w.x, w.y, w.z, w.w}, bs[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
@@ -371,10 +371,11 @@ __global__ void __maxnreg__(EW == 16 ? 96 : 168)
       // Stage y[0..32) of this thread's row (lane) with the 128-byte swizzle
       // the tensor map expects.
       auto stage32 = [&](uint8_t* buf, const float* y) {
+        const uint32_t b = smem_u32(buf) + static_cast<uint32_t>(lane * 128);
 #pragma unroll
         for (int j = 0; j < 8; ++j)
-          *reinterpret_cast<float4*>(buf + lane * 128 + ((j ^ (lane & 7)) * 16)) =
-              make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
+          sts128(b + static_cast<uint32_t>((j ^ (lane & 7)) * 16),
+                 make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]));
       };
 
       // One 32-column chunk of the plain epilogues (store / residual / GELU /
