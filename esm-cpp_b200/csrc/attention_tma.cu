@@ -143,15 +143,6 @@ __device__ __forceinline__ uint32_t stage_off(int j, int c4) {
   return static_cast<uint32_t>(j * 256 + ((c4 ^ (j & 15)) << 4));
 }
 
-// 2^x by the PTX ex2.approx.ftz.f32 instruction (relative error about
-// 2^-22; results below 2^-126 flush to zero, which the softmax sum of at
-// least 1 cannot see).
-__device__ __forceinline__ float ex2_ftz(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
 // Row max over the valid keys of one softmax warp's chunks (c = par, par+2,
 // ...; 32 keys each, S chunk c at TMEM column tS + 32 c).
 __device__ __forceinline__ float s_row_max(uint32_t tS, int par, int nchunk, int L) {

@@ -340,6 +340,14 @@ __device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
+// 2^x by the PTX ex2.approx.ftz.f32 instruction (relative error about
+// 2^-22; results below 2^-126 flush to zero).
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // 16-byte shared-memory accesses by 32-bit shared address (an aligned
 // dynamic shared-memory pointer is generic to the compiler).
 __device__ __forceinline__ float4 lds128(uint32_t a) {

@@ -9,9 +9,28 @@
 namespace esmb200 {
 
 // gelu.cpp:30-35: x * 0.5 * (1 + erf(x / sqrt(2))), each step rounded.
+// erf(z) = sign(z) (1 - erfc|z|) with erfc(a) = 2^(a R(a)): R is a degree-9
+// least-squares polynomial fit of log2(erfc(a)) / a on (0, 4] (fitted in
+// double precision against erfc, coefficients rounded to float, evaluated by
+// Horner FMAs); past |z| = 4 the exponent is driven down so erfc = 0 there
+// (erf = +-1, as erf rounds in float).  One ex2 and eleven FMAs in place of
+// a general erf: erfc is within about 4e-6 relative (log2 error < 5e-6,
+// < 8e-7 for |z| < 1.5), which keeps the GELU within 5% of the 1e-6
+// (1 + |gelu|) op tolerance.
 __device__ __forceinline__ float gelu_erf(float x) {
+  constexpr float kR[10] = {-0x1.a0bf78p+0f,  -0x1.d629d6p-1f,  -0x1.30f734p-3f, 0x1.d920dep-6f,
+                            -0x1.2cd446p-10f, -0x1.8d0dbcp-10f, 0x1.3426e2p-11f, -0x1.d6149ap-14f,
+                            0x1.81f4eap-17f,  -0x1.0f5acep-21f};
   const float kInvSqrt2 = 0.70710678118654752440f;
-  return __fmul_rn(__fmul_rn(x, 0.5f), __fadd_rn(1.0f, erff(__fmul_rn(x, kInvSqrt2))));
+  const float z = __fmul_rn(x, kInvSqrt2);
+  const float az = fabsf(z);
+  const float a = fminf(az, 4.0f);
+  float r = kR[9];
+#pragma unroll
+  for (int i = 8; i >= 0; --i) r = __fmaf_rn(r, a, kR[i]);
+  const float q = __fmaf_rn(fmaxf(__fsub_rn(az, 4.0f), 0.0f), -1.0e4f, __fmul_rn(r, a));
+  const float erf_z = copysignf(__fsub_rn(1.0f, ex2_ftz(q)), z);
+  return __fmul_rn(__fmul_rn(x, 0.5f), __fadd_rn(1.0f, erf_z));
 }
 
 // Applies kEpiStore / kEpiResidual / kEpiGelu to y[0..NV) = columns
