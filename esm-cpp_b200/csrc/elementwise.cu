@@ -26,6 +26,16 @@ __global__ void residual_kernel(float* __restrict__ y, const float* __restrict__
     y[i] = __fadd_rn(y[i], x[i]);
 }
 
+// lo = x - tf32(x): the part of an fp32 operand a tf32 MMA drops (it reads
+// the fp32 word with its low 13 mantissa bits cleared).
+__global__ void tf32_lo_kernel(const float* __restrict__ x, float* __restrict__ lo, long n) {
+  for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const float v = x[i];
+    lo[i] = __fsub_rn(v, __uint_as_float(__float_as_uint(v) & 0xFFFFE000u));
+  }
+}
+
 __global__ void scale_kernel(float* __restrict__ x, long n, float s) {
   for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<long>(gridDim.x) * blockDim.x)
@@ -155,6 +165,12 @@ cudaError_t launch_gelu(const float* x, float* out, long n, cudaStream_t s) {
 cudaError_t launch_residual_add(float* y, const float* x, long n, cudaStream_t s) {
   if (n <= 0) return cudaSuccess;
   residual_kernel<<<grid_for(n, 256), 256, 0, s>>>(y, x, n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tf32_lo(const float* x, float* lo, long n, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  tf32_lo_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, lo, n);
   return cudaGetLastError();
 }
 

@@ -42,17 +42,22 @@ constexpr int BK = 128;  // bytes of K per stage = one 128-byte swizzle row
 constexpr int threads_for(int ew) { return 64 + 32 * ew; }  // + producer, MMA issuer
 constexpr int kSmemLimit = 232448;                            // opt-in maximum per CTA
 
-template <int BN, bool PAIR, int EW, int ROPE = 0>
+// F32: the tf32x3 mode -- fp32 operands, a stage holds 32 K-elements of A
+// and W (raw) and of their lo parts, 128-byte rows each.
+template <int BN, bool PAIR, int EW, int ROPE = 0, bool F32 = false>
 struct Cfg {
-  static constexpr int A_BYTES = BM * BK;
-  static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * BK;  // this CTA's rows of W
+  static constexpr int A_RAW = BM * BK;
+  static constexpr int B_RAW = (PAIR ? BN / 2 : BN) * BK;  // this CTA's rows of W
+  static constexpr int A_BYTES = (F32 ? 2 : 1) * A_RAW;     // [raw | lo] in F32 mode
+  static constexpr int B_BYTES = (F32 ? 2 : 1) * B_RAW;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 
   static constexpr int TMEM_COLS = 2 * BN;
   // Epilogue staging for TMA stores: one [32 rows x 128 B] per warp, then the
   // tile's (w_scale * a_scale) and bias columns shared by the epilogue warps.
   static constexpr int STAGING_BYTES = EW * 4096;
-  static constexpr int COLVEC_BYTES = 2 * BN * 4;
+  // (F32: the bias columns only)
+  static constexpr int COLVEC_BYTES = (F32 ? 1 : 2) * BN * 4;
   // RoPE epilogue: the tile rows' cos / sin table entries 0..31 (128 rows x
   // 256 bytes), staged once per tile.
   static constexpr int ROPE_BYTES = ROPE ? BM * 256 : 0;
@@ -100,14 +105,16 @@ __device__ __forceinline__ bool epi_all(bool v) {
 
 // Register cap: with EW = 16, 18 warps put five on one SM sub-partition (16K
 // registers each) -> 96; with EW = 8, three -> 168.
-template <int BN, int EPI, bool PAIR, int EW>
+template <int BN, int EPI, bool PAIR, int EW, bool F32 = false>
 __global__ void __maxnreg__(EW == 16 ? 96 : 168)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA,
                    const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC0,
                    const __grid_constant__ CUtensorMap tmC1,
-                   const __grid_constant__ CUtensorMap tmC2, const Params p) {
-  using C = Cfg<BN, PAIR, EW, EPI == kEpiQkvRope>;
+                   const __grid_constant__ CUtensorMap tmC2,
+                   const __grid_constant__ CUtensorMap tmAlo,
+                   const __grid_constant__ CUtensorMap tmBlo, const Params p) {
+  using C = Cfg<BN, PAIR, EW, EPI == kEpiQkvRope, F32>;
   constexpr int kEpiPerQuad = EW / 4;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -142,6 +149,10 @@ __global__ void __maxnreg__(EW == 16 ? 96 : 168)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    if (F32) {
+      prefetch_tmap(&tmAlo);
+      prefetch_tmap(&tmBlo);
+    }
     if (p.tma) {
       prefetch_tmap(&tmC0);
       if (EPI == kEpiQkvRope) {
@@ -173,7 +184,8 @@ __global__ void __maxnreg__(EW == 16 ? 96 : 168)
   const int m_units = PAIR ? (p.M + 2 * BM - 1) / (2 * BM) : (p.M + BM - 1) / BM;
   const int n_blocks = (p.N + BN - 1) / BN;
   const int num_tiles = m_units * n_blocks;
-  const int num_kb = (p.K + BK - 1) / BK;
+  const int kpb = F32 ? BK / 4 : BK;  // K elements per stage
+  const int num_kb = (p.K + kpb - 1) / kpb;
   auto tile_m_base = [&](int tile) {
     const int mu = tile % m_units;
     return PAIR ? mu * 2 * BM + static_cast<int>(rank) * BM : mu * BM;
@@ -193,18 +205,29 @@ __global__ void __maxnreg__(EW == 16 ? 96 : 168)
             ok = false;
             break;
           }
+          const int kx = F32 ? kb * (BK / 4) : kb * BK;  // K coordinate in elements
+          const int nrow = n_blk * BN + (PAIR ? static_cast<int>(rank) * (BN / 2) : 0);
+          uint8_t* a_dst = sA + stage * C::A_BYTES;
+          uint8_t* b_dst = sB + stage * C::B_BYTES;
           if (PAIR) {
             // Both CTAs' bytes complete on CTA 0's full barrier, which CTA 0
             // arms for the pair.
             if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
             const uint32_t bar0 = mapa_shared(smem_u32(&full[stage]), 0);
-            tma_load_2d_pair(sA + stage * C::A_BYTES, &tmA, bar0, kb * BK, m_base);
-            tma_load_2d_pair(sB + stage * C::B_BYTES, &tmB, bar0, kb * BK,
-                             n_blk * BN + static_cast<int>(rank) * (BN / 2));
+            tma_load_2d_pair(a_dst, &tmA, bar0, kx, m_base);
+            tma_load_2d_pair(b_dst, &tmB, bar0, kx, nrow);
+            if (F32) {
+              tma_load_2d_pair(a_dst + C::A_RAW, &tmAlo, bar0, kx, m_base);
+              tma_load_2d_pair(b_dst + C::B_RAW, &tmBlo, bar0, kx, nrow);
+            }
           } else {
             mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-            tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * BK, m_base);
-            tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * BK, n_blk * BN);
+            tma_load_2d(a_dst, &tmA, &full[stage], kx, m_base);
+            tma_load_2d(b_dst, &tmB, &full[stage], kx, nrow);
+            if (F32) {
+              tma_load_2d(a_dst + C::A_RAW, &tmAlo, &full[stage], kx, m_base);
+              tma_load_2d(b_dst + C::B_RAW, &tmBlo, &full[stage], kx, nrow);
+            }
           }
           if (++stage == C::STAGES) {
             stage = 0;
@@ -225,7 +248,7 @@ __global__ void __maxnreg__(EW == 16 ? 96 : 168)
   } else if (warp == 1) {
     // ------------------------------------------------------- MMA issuer
     if (lane == 0 && rank == 0) {
-      constexpr uint32_t idesc = idesc_i8(PAIR ? 2 * BM : BM, BN);
+      constexpr uint32_t idesc = F32 ? idesc_tf32(PAIR ? 2 * BM : BM, BN) : idesc_i8(PAIR ? 2 * BM : BM, BN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -245,12 +268,27 @@ __global__ void __maxnreg__(EW == 16 ? 96 : 168)
           const uint32_t b0 = smem_u32(sB + stage * C::B_BYTES);
 #pragma unroll
           for (int k = 0; k < BK / 32; ++k) {
-            if (PAIR)
-              mma_i8_pair(d_tmem, sw128_kmajor_desc(a0 + k * 32), sw128_kmajor_desc(b0 + k * 32),
-                          idesc, (kb | k) != 0 ? 1u : 0u);
-            else
-              mma_i8(d_tmem, sw128_kmajor_desc(a0 + k * 32), sw128_kmajor_desc(b0 + k * 32), idesc,
-                     (kb | k) != 0 ? 1u : 0u);
+            const uint64_t ad = sw128_kmajor_desc(a0 + k * 32), bd = sw128_kmajor_desc(b0 + k * 32);
+            const uint32_t acc_in = (kb | k) != 0 ? 1u : 0u;
+            if constexpr (F32) {
+              // 3xTF32: A W + A W_lo + A_lo W (the tensor core reads an fp32
+              // word as tf32 by dropping its low 13 bits, so raw = hi).
+              const uint64_t alo = sw128_kmajor_desc(a0 + C::A_RAW + k * 32);
+              const uint64_t blo = sw128_kmajor_desc(b0 + C::B_RAW + k * 32);
+              if (PAIR) {
+                mma_tf32_pair(d_tmem, ad, bd, idesc, acc_in);
+                mma_tf32_pair(d_tmem, ad, blo, idesc, 1u);
+                mma_tf32_pair(d_tmem, alo, bd, idesc, 1u);
+              } else {
+                mma_tf32(d_tmem, ad, bd, idesc, acc_in);
+                mma_tf32(d_tmem, ad, blo, idesc, 1u);
+                mma_tf32(d_tmem, alo, bd, idesc, 1u);
+              }
+            } else if (PAIR) {
+              mma_i8_pair(d_tmem, ad, bd, idesc, acc_in);
+            } else {
+              mma_i8(d_tmem, ad, bd, idesc, acc_in);
+            }
           }
           if (PAIR) {  // the stage is free in both CTAs
             mma_commit_pair(smem_u32(&empty[stage]));
@@ -318,15 +356,16 @@ __global__ void __maxnreg__(EW == 16 ? 96 : 168)
       const long m = static_cast<long>(m_base) + row_in_tile;
       const bool row_ok = m < p.M;
       float as = 1.0f;  // the raw-accumulator mode carries no activation scale
-      if (row_ok && p.acc_out == nullptr) as = p.per_token ? __ldg(p.a_scale + m) : __ldg(p.a_scale);
+      if (!F32 && row_ok && p.acc_out == nullptr)
+        as = p.per_token ? __ldg(p.a_scale + m) : __ldg(p.a_scale);
       // Per-tensor scale: ws[n]*as is the same for every row, so the rounded
       // product (the reference rounds it before the fma) is formed once.
-      const float as_col = p.per_token ? 1.0f : (p.acc_out ? 1.0f : __ldg(p.a_scale));
+      const float as_col = (F32 || p.per_token || p.acc_out) ? 1.0f : __ldg(p.a_scale);
       const bool has_col = p.acc_out == nullptr && etid < BN;
       float ws_col = 0.0f, b_col = 0.0f;
       if (has_col) {  // tail columns read the last valid column
         const int n = min(n_blk * BN + etid, p.N - 1);
-        ws_col = __ldg(p.w_scale + n);
+        if (!F32) ws_col = __ldg(p.w_scale + n);
         b_col = p.bias ? __ldg(p.bias + n) : 0.0f;
       }
       if (!epi_all<EW>(mbar_wait(&tfull[acc], acc_phase, p.status))) break;
@@ -337,9 +376,9 @@ __global__ void __maxnreg__(EW == 16 ? 96 : 168)
       // This tile's w_scale / bias columns in shared memory for all epilogue
       // warps.
       float* wsv = colvec;
-      float* bsv = colvec + BN;
+      float* bsv = F32 ? colvec : colvec + BN;
       if (has_col) {
-        wsv[etid] = p.per_token ? ws_col : __fmul_rn(ws_col, as_col);
+        if (!F32) wsv[etid] = p.per_token ? ws_col : __fmul_rn(ws_col, as_col);
         bsv[etid] = b_col;
       }
       epi_barrier<EW>();  // vectors filled
@@ -348,15 +387,26 @@ __global__ void __maxnreg__(EW == 16 ? 96 : 168)
       // column vectors read as float4.
       const uint32_t wsv_s = smem_u32(wsv), bsv_s = smem_u32(bsv);
       auto deq32 = [&](const uint32_t(&r)[32], int jc0, float* y) {
+        if constexpr (F32) {  // fp32 accumulator + bias (gemm_fp32.cpp's Linear)
 #pragma unroll
-        for (int j4 = 0; j4 < 8; ++j4) {
-          const uint32_t o = static_cast<uint32_t>((jc0 + 4 * j4) * 4);
-          const float4 w = lds128(wsv_s + o), b = lds128(bsv_s + o);
-          const float ws[4] = {w.x, w.y, w.z, w.w}, bs[4] = {b.x, b.y, b.z, b.w};
+          for (int j4 = 0; j4 < 8; ++j4) {
+            const float4 b = lds128(bsv_s + static_cast<uint32_t>((jc0 + 4 * j4) * 4));
+            const float bs[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const float sc = p.per_token ? __fmul_rn(ws[u], as) : ws[u];
-            y[4 * j4 + u] = __fmaf_rn(__int2float_rn(static_cast<int>(r[4 * j4 + u])), sc, bs[u]);
+            for (int u = 0; u < 4; ++u)
+              y[4 * j4 + u] = __fadd_rn(__uint_as_float(r[4 * j4 + u]), bs[u]);
+          }
+        } else {
+#pragma unroll
+          for (int j4 = 0; j4 < 8; ++j4) {
+            const uint32_t o = static_cast<uint32_t>((jc0 + 4 * j4) * 4);
+            const float4 w = lds128(wsv_s + o), b = lds128(bsv_s + o);
+            const float ws[4] = {w.x, w.y, w.z, w.w}, bs[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const float sc = p.per_token ? __fmul_rn(ws[u], as) : ws[u];
+              y[4 * j4 + u] = __fmaf_rn(__int2float_rn(static_cast<int>(r[4 * j4 + u])), sc, bs[u]);
+            }
           }
         }
       };
@@ -521,15 +571,17 @@ bool make_tmap_i8(CUtensorMap* map, const int8_t* base, int rows, int cols, long
   return r == CUDA_SUCCESS;
 }
 
-// 2-D fp32 tensor [rows, cols] with row stride `ld` floats; box = 32 x 32
-// (128-byte rows, 128-byte swizzle) for the epilogue's TMA stores.
-bool make_tmap_f32(CUtensorMap* map, const float* base, long rows, long cols, long ld) {
+// 2-D fp32 tensor [rows, cols] with row stride `ld` floats; box = 32 columns
+// x box_rows (128-byte rows, 128-byte swizzle): 32 x 32 for the epilogue's
+// TMA stores, BM or BN rows for the tf32x3 operand loads.
+bool make_tmap_f32(CUtensorMap* map, const float* base, long rows, long cols, long ld,
+                   int box_rows = 32) {
   auto fn = get_encode_fn();
   if (fn == nullptr || base == nullptr || (ld & 3) || (reinterpret_cast<uintptr_t>(base) & 15))
     return false;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 4)};
-  cuuint32_t box[2] = {32, 32};
+  cuuint32_t box[2] = {32, static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box,
             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -560,7 +612,7 @@ cudaError_t launch_bn(const GemmI8Args& a, cudaStream_t s) {
   cudaGetDevice(&dev);
   const uint64_t bit = 1ull << (dev & 63);
   if ((attr_set.load() & bit) == 0) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_i8_kernel<BN, EPI, PAIR, EW>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_i8_kernel<BN, EPI, PAIR, EW, false>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
     attr_set.fetch_or(bit);
@@ -580,8 +632,8 @@ cudaError_t launch_bn(const GemmI8Args& a, cudaStream_t s) {
   if constexpr (!PAIR) {
     const int tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
     const int grid = tiles < a.num_sms ? tiles : a.num_sms;
-    gemm_i8_kernel<BN, EPI, false, EW><<<grid, kThreads, C::SMEM, s>>>(tmA, tmB, tmC[0], tmC[1],
-                                                                    tmC[2], p);
+    gemm_i8_kernel<BN, EPI, false, EW, false><<<grid, kThreads, C::SMEM, s>>>(
+        tmA, tmB, tmC[0], tmC[1], tmC[2], tmC[1], tmC[2], p);
     return cudaGetLastError();
   } else {
   // CTA pairs: one 2-CTA cluster per pair tile, at most num_sms / 2 pairs.
@@ -599,8 +651,73 @@ cudaError_t launch_bn(const GemmI8Args& a, cudaStream_t s) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemm_i8_kernel<BN, EPI, true, EW>, tmA, tmB, tmC[0], tmC[1], tmC[2],
-                            p);
+  return cudaLaunchKernelEx(&cfg, gemm_i8_kernel<BN, EPI, true, EW, false>, tmA, tmB, tmC[0],
+                            tmC[1], tmC[2], tmC[1], tmC[2], p);
+  }
+}
+
+// The tf32x3 mode (fp32 operands with their lo parts): BN = 256 on CTA pairs
+// or BN = 128 on single CTAs, 8 epilogue warps, 3 stages of 64 KB.
+template <int BN, bool PAIR>
+cudaError_t launch_f32(const GemmTf32Args& a, cudaStream_t s) {
+  constexpr int EW = 8;
+  using C = Cfg<BN, PAIR, EW, 0, true>;
+  static_assert(C::STAGES >= 2, "the tf32x3 ring needs two stages");
+  constexpr int kThreads = threads_for(EW);
+  constexpr int brow = PAIR ? BN / 2 : BN;
+  CUtensorMap tmA, tmAlo, tmB, tmBlo, tmC[3];
+  if (!make_tmap_f32(&tmA, a.A, a.M, a.K, a.lda, BM) ||
+      !make_tmap_f32(&tmAlo, a.A_lo, a.M, a.K, a.lda, BM) ||
+      !make_tmap_f32(&tmB, a.W, a.N, a.K, a.ldw, brow) ||
+      !make_tmap_f32(&tmBlo, a.W_lo, a.N, a.K, a.ldw, brow))
+    return cudaErrorInvalidValue;
+  std::memset(tmC, 0, sizeof(tmC));
+  const bool tma = make_tmap_f32(&tmC[0], a.epi.C, a.M, a.N, a.epi.ldc);
+  static std::atomic<uint64_t> attr_set{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if ((attr_set.load() & bit) == 0) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_i8_kernel<BN, kEpiStore, PAIR, EW, true>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return e;
+    attr_set.fetch_or(bit);
+  }
+  Params p;
+  p.M = a.M;
+  p.N = a.N;
+  p.K = a.K;
+  p.w_scale = nullptr;
+  p.a_scale = nullptr;
+  p.per_token = 0;
+  p.bias = a.bias;
+  p.epi = a.epi;
+  p.status = a.status;
+  p.acc_out = nullptr;
+  p.tma = tma ? 1 : 0;
+  if constexpr (!PAIR) {
+    const int tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
+    const int grid = tiles < a.num_sms ? tiles : a.num_sms;
+    gemm_i8_kernel<BN, kEpiStore, false, EW, true><<<grid, kThreads, C::SMEM, s>>>(
+        tmA, tmB, tmC[0], tmC[1], tmC[2], tmAlo, tmBlo, p);
+    return cudaGetLastError();
+  } else {
+    const int tiles = ((a.M + 2 * BM - 1) / (2 * BM)) * ((a.N + BN - 1) / BN);
+    const int pairs = std::max(1, std::min(tiles, a.num_sms / 2));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemm_i8_kernel<BN, kEpiStore, true, EW, true>, tmA, tmB,
+                              tmC[0], tmC[1], tmC[2], tmAlo, tmBlo, p);
   }
 }
 
@@ -632,6 +749,20 @@ cudaError_t launch_gemm_i8(const GemmI8Args& a, cudaStream_t s) {
   if (wide) return gelu ? launch_bn<256, kEpiStore, false, 16>(a, s)
                         : launch_bn<256, kEpiStore, false, 8>(a, s);
   return gelu ? launch_bn<128, kEpiStore, false, 16>(a, s) : launch_bn<128, kEpiStore, false, 8>(a, s);
+}
+
+cudaError_t launch_gemm_tf32x3(const GemmTf32Args& a, cudaStream_t s) {
+  if (a.M <= 0 || a.N <= 0) return cudaSuccess;
+  if (a.K <= 0 || (a.K & 3) || (a.lda & 3) || (a.ldw & 3) || a.A_lo == nullptr ||
+      a.W_lo == nullptr || a.status == nullptr || a.epi.kind == kEpiQkvRope ||
+      ((reinterpret_cast<uintptr_t>(a.A) | reinterpret_cast<uintptr_t>(a.A_lo) |
+        reinterpret_cast<uintptr_t>(a.W) | reinterpret_cast<uintptr_t>(a.W_lo)) & 15))
+    return cudaErrorNotSupported;
+  // CTA pairs (M = 256, N = 256) when there are tiles for every pair: each
+  // CTA then streams 64 KB per 32 K-elements for 12 full-rate MMAs.
+  const long pair_tiles = static_cast<long>((a.M + 255) / 256) * ((a.N + 255) / 256);
+  if (a.N >= 256 && pair_tiles >= a.num_sms / 2) return launch_f32<256, true>(a, s);
+  return launch_f32<128, false>(a, s);
 }
 
 }  // namespace esmb200

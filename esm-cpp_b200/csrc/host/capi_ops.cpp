@@ -188,6 +188,40 @@ int esmcu_linear(esmcu_context* ctx, const float* A, const float* W, const float
   ESMCU_TRY(check_ptr(A, "A"));
   ESMCU_TRY(check_ptr(W, "W"));
   ESMCU_TRY(check_ptr(C, "C"));
+  EpiParams epi;
+  epi.kind = kEpiStore;
+  epi.C = C;
+  epi.ldc = N;
+  // 3xTF32 on the tensor cores when K and the operands allow 16-byte TMA
+  // rows (the lo parts of A and W go to the context scratch); FP32 SIMT
+  // otherwise.
+  const bool tc = (K % 4 == 0) &&
+                  ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(W)) & 15) == 0;
+  if (tc) {
+    const size_t na = static_cast<size_t>(M) * K, nw = static_cast<size_t>(N) * K;
+    const size_t off_w = align_up(na * sizeof(float), 256);
+    ESMCU_TRY(ensure_scratch(ctx, off_w + nw * sizeof(float)));
+    float* a_lo = static_cast<float*>(ctx->scratch);
+    float* w_lo = reinterpret_cast<float*>(static_cast<char*>(ctx->scratch) + off_w);
+    ESMCU_CUDA(launch_tf32_lo(A, a_lo, static_cast<long>(na), ctx->stream));
+    ESMCU_CUDA(launch_tf32_lo(W, w_lo, static_cast<long>(nw), ctx->stream));
+    GemmTf32Args g;
+    g.A = A;
+    g.A_lo = a_lo;
+    g.lda = K;
+    g.W = W;
+    g.W_lo = w_lo;
+    g.ldw = K;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.bias = bias;
+    g.epi = epi;
+    g.status = ctx->d_status;
+    g.num_sms = ctx->num_sms;
+    ESMCU_CUDA(launch_gemm_tf32x3(g, ctx->stream));
+    return ESMCU_OK;
+  }
   GemmF32Args a;
   a.A = A;
   a.lda = K;
@@ -197,9 +231,7 @@ int esmcu_linear(esmcu_context* ctx, const float* A, const float* W, const float
   a.N = N;
   a.K = K;
   a.bias = bias;
-  a.epi.kind = kEpiStore;
-  a.epi.C = C;
-  a.epi.ldc = N;
+  a.epi = epi;
   ESMCU_CUDA(launch_gemm_f32(a, ctx->stream));
   return ESMCU_OK;
 }

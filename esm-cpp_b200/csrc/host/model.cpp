@@ -60,6 +60,7 @@ struct esmcu_model {
   float *embed = nullptr, *final_ln_w = nullptr, *final_ln_b = nullptr;
   float *lm_w = nullptr, *lm_b = nullptr, *lm_ln_w = nullptr, *lm_ln_b = nullptr,
         *lm_bias = nullptr;
+  float* lm_w_lo = nullptr;  // lm_w - tf32(lm_w), for the 3xTF32 dense GEMM
   bool embed_set = false, head_set = false;
   float *cos_t = nullptr, *sin_t = nullptr;
   int rope_len = 0;
@@ -513,7 +514,28 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
     e.kind = kEpiGelu;  // dense -> GELU (model.cpp:1192-1223)
     e.C = attn;
     e.ldc = d;
-    TRY(gemm_f32(ln, d, m->lm_w, d, m->lm_b, e));
+    if (d % 4 == 0) {
+      // 3xTF32 on the tensor cores; the lo part of `ln` goes to `k` (free
+      // once the layers are done).
+      LAUNCH(m, launch_tf32_lo(ln, k, static_cast<long>(T) * d, s));
+      GemmTf32Args g;
+      g.A = ln;
+      g.A_lo = k;
+      g.lda = d;
+      g.W = m->lm_w;
+      g.W_lo = m->lm_w_lo;
+      g.ldw = d;
+      g.M = T;
+      g.N = d;
+      g.K = d;
+      g.bias = m->lm_b;
+      g.epi = e;
+      g.status = ctx->d_status;
+      g.num_sms = ctx->num_sms;
+      LAUNCH(m, launch_gemm_tf32x3(g, s));
+    } else {
+      TRY(gemm_f32(ln, d, m->lm_w, d, m->lm_b, e));
+    }
   }
   sec.end();
   sec.begin("lm_ln");
@@ -710,6 +732,19 @@ int esmcu_model_set_head(esmcu_model* m, const float* final_ln_w, const float* f
   TRY(upload_vec(m, &m->final_ln_w, final_ln_w, d, "final_ln_w"));
   TRY(upload_vec(m, &m->final_ln_b, final_ln_b, d, "final_ln_b"));
   TRY(upload_vec(m, &m->lm_w, lm_dense_w, d * d, "lm_dense_w"));
+  // Its lo part for the 3xTF32 GEMM, formed once on the device.
+  if (m->lm_w_lo == nullptr) {
+    void* p = nullptr;
+    if (cudaMalloc(&p, d * d * sizeof(float)) != cudaSuccess)
+      return fail(ESMCU_ERR_CUDA, "cudaMalloc(lm_w_lo) failed");
+    m->owned.push_back(p);
+    m->lm_w_lo = static_cast<float*>(p);
+  }
+  {
+    cudaError_t e = launch_tf32_lo(m->lm_w, m->lm_w_lo, static_cast<long>(d * d), m->ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "lm_w_lo");
+  }
   TRY(upload_vec(m, &m->lm_b, lm_dense_b, d, "lm_dense_b"));
   TRY(upload_vec(m, &m->lm_ln_w, lm_ln_w, d, "lm_ln_w"));
   TRY(upload_vec(m, &m->lm_ln_b, lm_ln_b, d, "lm_ln_b"));

@@ -78,6 +78,28 @@ struct GemmF32Args {
 };
 cudaError_t launch_gemm_f32(const GemmF32Args& a, cudaStream_t s);
 
+// The same product on the tensor cores, 3xTF32 (tcgen05 kind::tf32):
+// C = epilogue( A W^T + A W_lo^T + A_lo W^T + bias ), where x_lo = x - tf32(x)
+// (launch_tf32_lo) is given for both operands.  FP32-accurate to about 2^-21
+// relative per product.  K, lda, ldw multiples of 4, operands 16-byte
+// aligned; cudaErrorNotSupported otherwise (and for the QKV epilogue).
+struct GemmTf32Args {
+  const float* A = nullptr;
+  const float* A_lo = nullptr;
+  long lda = 0;
+  const float* W = nullptr;
+  const float* W_lo = nullptr;
+  long ldw = 0;
+  int M = 0, N = 0, K = 0;
+  const float* bias = nullptr;
+  EpiParams epi;
+  uint32_t* status = nullptr;
+  int num_sms = 148;
+};
+cudaError_t launch_gemm_tf32x3(const GemmTf32Args& a, cudaStream_t s);
+// lo[i] = x[i] - (x[i] with its low 13 mantissa bits cleared), i < n.
+cudaError_t launch_tf32_lo(const float* x, float* lo, long n, cudaStream_t s);
+
 // ------------------------------------------------------------ quantisation
 // Per-tensor: scale = amax>0 ? amax/127 : 1 (amax = max over the kAmaxSlots
 // slots at amax_bits);

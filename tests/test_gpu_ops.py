@@ -170,7 +170,11 @@ def test_attention_large_scores_finite(cuda):
     np.testing.assert_allclose(o[0, 0], v.mean(axis=0)[0], rtol=1e-4, atol=1e-5)
 
 
-@pytest.mark.parametrize("M,N,K", [(1, 33, 320), (130, 1280, 1280), (77, 33, 1280), (9, 11, 40)])
+# K % 4 == 0 takes the 3xTF32 tensor-core path (BN = 128 tiles, or CTA pairs
+# when there are >= 74 pair tiles: the 1200 x 4096 case), else FP32 SIMT
+# (K = 37).
+@pytest.mark.parametrize("M,N,K", [(1, 33, 320), (130, 1280, 1280), (77, 33, 1280), (9, 11, 40),
+                                   (1200, 4096, 500), (300, 1000, 1284), (50, 70, 37)])
 def test_linear_f32_matches_oracle(cuda, O, M, N, K):
     from esm_b200 import ops
 
