@@ -22,6 +22,13 @@
 // drains its own 128 TMEM rows.
 // The epilogue of tile i overlaps the mainloop of tile i+1.  Every barrier
 // wait is bounded; a timeout sets a status bit and the CTA unwinds.
+//
+// The same kernel in its F32 mode is the 3xTF32 FP32 GEMM (launch_gemm_tf32x3,
+// the reference's FP32 Linear, gemm_fp32.cpp:272-292, for the LM head): a
+// stage holds 32 K-elements of A, W and their lo parts (x - tf32(x), formed
+// by launch_tf32_lo), three kind::tf32 MMAs per 8 K-elements (A W + A W_lo +
+// A_lo W; the tensor core reads the raw fp32 word as its tf32 hi part), and
+// the epilogue adds the bias to the fp32 accumulator.
 #include <cudaTypedefs.h>
 
 #include <algorithm>

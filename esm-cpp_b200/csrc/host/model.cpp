@@ -60,7 +60,8 @@ struct esmcu_model {
   float *embed = nullptr, *final_ln_w = nullptr, *final_ln_b = nullptr;
   float *lm_w = nullptr, *lm_b = nullptr, *lm_ln_w = nullptr, *lm_ln_b = nullptr,
         *lm_bias = nullptr;
-  float* lm_w_lo = nullptr;  // lm_w - tf32(lm_w), for the 3xTF32 dense GEMM
+  float* lm_w_lo = nullptr;   // lm_w - tf32(lm_w), for the 3xTF32 dense GEMM
+  float* embed_lo = nullptr;  // the same for the tied decoder (embed^T)
   bool embed_set = false, head_set = false;
   float *cos_t = nullptr, *sin_t = nullptr;
   int rope_len = 0;
@@ -548,7 +549,26 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
     e.kind = kEpiStore;  // tied decoder: lm_ln . embed^T + bias (model.cpp:1234-1239)
     e.C = logits;
     e.ldc = c.vocab_size;
-    TRY(gemm_f32(q, d, m->embed, c.vocab_size, m->lm_bias, e));
+    if (d % 4 == 0) {  // 3xTF32, the lo part of `q` into `v`
+      LAUNCH(m, launch_tf32_lo(q, v, static_cast<long>(T) * d, s));
+      GemmTf32Args g;
+      g.A = q;
+      g.A_lo = v;
+      g.lda = d;
+      g.W = m->embed;
+      g.W_lo = m->embed_lo;
+      g.ldw = d;
+      g.M = T;
+      g.N = c.vocab_size;
+      g.K = d;
+      g.bias = m->lm_bias;
+      g.epi = e;
+      g.status = ctx->d_status;
+      g.num_sms = ctx->num_sms;
+      LAUNCH(m, launch_gemm_tf32x3(g, s));
+    } else {
+      TRY(gemm_f32(q, d, m->embed, c.vocab_size, m->lm_bias, e));
+    }
   }
   sec.end();
   for (auto& e : sec.ev) m->pending.push_back(std::move(e));
@@ -714,11 +734,26 @@ int esmcu_model_config(const esmcu_model* m, esmcu_config* out) {
   return ESMCU_OK;
 }
 
+// *lo (allocated once) = x - tf32(x) over n floats of device data x.
+static int make_lo(esmcu_model* m, float** lo, const float* x, size_t n, const char* name) {
+  if (*lo == nullptr) {
+    void* p = nullptr;
+    if (cudaMalloc(&p, (n == 0 ? 1 : n) * sizeof(float)) != cudaSuccess)
+      return fail(ESMCU_ERR_CUDA, std::string("cudaMalloc(") + name + ") failed");
+    m->owned.push_back(p);
+    *lo = static_cast<float*>(p);
+  }
+  cudaError_t e = launch_tf32_lo(x, *lo, static_cast<long>(n), m->ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(m->ctx->stream);
+  return e == cudaSuccess ? ESMCU_OK : cuda_fail(e, name);
+}
+
 int esmcu_model_set_embeddings(esmcu_model* m, const float* embed) {
   if (m == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "null model");
   TRY(use_device(m->ctx));
-  TRY(upload_vec(m, &m->embed, embed,
-                 static_cast<size_t>(m->cfg.vocab_size) * m->cfg.hidden_size, "embed"));
+  const size_t n = static_cast<size_t>(m->cfg.vocab_size) * m->cfg.hidden_size;
+  TRY(upload_vec(m, &m->embed, embed, n, "embed"));
+  TRY(make_lo(m, &m->embed_lo, m->embed, n, "embed_lo"));  // the decoder's W_lo
   m->embed_set = true;
   return ESMCU_OK;
 }
@@ -733,18 +768,7 @@ int esmcu_model_set_head(esmcu_model* m, const float* final_ln_w, const float* f
   TRY(upload_vec(m, &m->final_ln_b, final_ln_b, d, "final_ln_b"));
   TRY(upload_vec(m, &m->lm_w, lm_dense_w, d * d, "lm_dense_w"));
   // Its lo part for the 3xTF32 GEMM, formed once on the device.
-  if (m->lm_w_lo == nullptr) {
-    void* p = nullptr;
-    if (cudaMalloc(&p, d * d * sizeof(float)) != cudaSuccess)
-      return fail(ESMCU_ERR_CUDA, "cudaMalloc(lm_w_lo) failed");
-    m->owned.push_back(p);
-    m->lm_w_lo = static_cast<float*>(p);
-  }
-  {
-    cudaError_t e = launch_tf32_lo(m->lm_w, m->lm_w_lo, static_cast<long>(d * d), m->ctx->stream);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(m->ctx->stream);
-    if (e != cudaSuccess) return cuda_fail(e, "lm_w_lo");
-  }
+  TRY(make_lo(m, &m->lm_w_lo, m->lm_w, d * d, "lm_w_lo"));
   TRY(upload_vec(m, &m->lm_b, lm_dense_b, d, "lm_dense_b"));
   TRY(upload_vec(m, &m->lm_ln_w, lm_ln_w, d, "lm_ln_w"));
   TRY(upload_vec(m, &m->lm_ln_b, lm_ln_b, d, "lm_ln_b"));
