@@ -200,7 +200,10 @@ __device__ __forceinline__ uint32_t quant4(float4 y, float inv) {
          ((static_cast<uint32_t>(a2) & 0xffu) << 16) | ((static_cast<uint32_t>(a3) & 0xffu) << 24);
 }
 
-constexpr int kLqThreads = 384;  // 12 warps: one block per SM at up to 168 registers
+// 12 warps, one block per SM (up to 168 registers).  Each warp keeps two
+// rows in registers: the next row's loads are in flight while the current
+// one is reduced or quantised.  Gamma and beta are read from shared memory.
+constexpr int kLqThreads = 384;
 
 template <int NV>
 __global__ void __launch_bounds__(kLqThreads, 1)
@@ -211,39 +214,68 @@ __global__ void __launch_bounds__(kLqThreads, 1)
   const int lane = threadIdx.x & 31;
   const long warp_g = static_cast<long>(blockIdx.x) * (kLqThreads / 32) + (threadIdx.x >> 5);
   const long nwarps = static_cast<long>(gridDim.x) * (kLqThreads / 32);
+  __shared__ __align__(16) float s_gb[2 * 128 * NV];  // gamma | beta
+  for (int i = threadIdx.x; i < d; i += kLqThreads) {
+    s_gb[i] = __ldg(g + i);
+    s_gb[128 * NV + i] = __ldg(b + i);
+  }
+  __syncthreads();
+  const uint32_t sg = smem_u32(s_gb), sb = sg + 128u * NV * 4u;
+  auto load_row = [&](long r, float4 (&v)[NV]) {
+    const float* xr = x + r * d;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) v[i] = __ldg(reinterpret_cast<const float4*>(xr + 4 * lane + 128 * i));
+  };
   // ---- phase 1: statistics and absmax of y
   float tmax = 0.0f;
-  for (long r = warp_g; r < rows; r += nwarps) {
-    const float* xr = x + r * d;
-    float4 v[NV];
-    double sum = 0.0;
+  // Mean and variance in double in one pass (sum and sum of squares, two
+  // partial chains each, one combined warp reduction): var = E[x^2] - mean^2
+  // differs from the two-pass double variance by ~1e-12 relative, far below
+  // the float rounding of var that follows.
+  auto stats_row = [&](long r, const float4 (&v)[NV]) {
+    double s0 = 0.0, s1 = 0.0, q0 = 0.0, q1 = 0.0;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      v[i] = __ldg(reinterpret_cast<const float4*>(xr + 4 * lane + 128 * i));
-      sum += static_cast<double>(v[i].x) + static_cast<double>(v[i].y) +
-             (static_cast<double>(v[i].z) + static_cast<double>(v[i].w));
+      const double a = v[i].x, bb = v[i].y, cc = v[i].z, dd = v[i].w;
+      s0 += a + bb;
+      s1 += cc + dd;
+      q0 = fma(a, a, fma(bb, bb, q0));
+      q1 = fma(cc, cc, fma(dd, dd, q1));
     }
-    const double mean = warp_sum_d(sum) / d;
-    double var = 0.0;
+    double sum = s0 + s1, sq = q0 + q1;
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const double a = static_cast<double>(v[i].x) - mean, bb = static_cast<double>(v[i].y) - mean;
-      const double cc = static_cast<double>(v[i].z) - mean, dd = static_cast<double>(v[i].w) - mean;
-      var += a * a + bb * bb + (cc * cc + dd * dd);
+    for (int o = 16; o > 0; o >>= 1) {
+      sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      sq += __shfl_xor_sync(0xffffffffu, sq, o);
     }
-    var = warp_sum_d(var) / d;
+    const double mean = sum / d;
+    const double var = fmax(sq / d - mean * mean, 0.0);
     const float inv_std = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(var), eps)));
     const float meanf = static_cast<float>(mean);
     float mx = 0.0f;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int c = 4 * lane + 128 * i;
-      const float4 y = ln_y4(v[i], meanf, inv_std, __ldg(reinterpret_cast<const float4*>(g + c)),
-                             __ldg(reinterpret_cast<const float4*>(b + c)));
+      const float4 y = ln_y4(v[i], meanf, inv_std, lds128(sg + c * 4u), lds128(sb + c * 4u));
       mx = fmaxf(mx, fmaxf(fmaxf(fabsf(y.x), fabsf(y.y)), fmaxf(fabsf(y.z), fabsf(y.w))));
     }
     if (lane == 0) stats[r] = make_float2(meanf, inv_std);
     tmax = fmaxf(tmax, mx);
+  };
+  {
+    float4 va[NV], vb[NV];
+    long r = warp_g;
+    if (r < rows) load_row(r, va);
+    while (r < rows) {
+      const long r1 = r + nwarps;
+      if (r1 < rows) load_row(r1, vb);
+      stats_row(r, va);
+      if (r1 >= rows) break;
+      const long r2 = r1 + nwarps;
+      if (r2 < rows) load_row(r2, va);
+      stats_row(r1, vb);
+      r = r2;
+    }
   }
   amax_publish(amax, tmax);
   grid_barrier_once(counter, status);
@@ -262,19 +294,31 @@ __global__ void __launch_bounds__(kLqThreads, 1)
   }
   __syncthreads();
   const float inv = s_inv;
-  for (long r = warp_g; r < rows; r += nwarps) {
-    const float* xr = x + r * d;
+  auto quant_row = [&](long r, const float4 (&v)[NV]) {
     const float2 st = __ldcg(stats + r);
     int8_t* qr = q + r * ldq;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int c = 4 * lane + 128 * i;
-      const float4 y = ln_y4(__ldg(reinterpret_cast<const float4*>(xr + c)), st.x, st.y,
-                             __ldg(reinterpret_cast<const float4*>(g + c)),
-                             __ldg(reinterpret_cast<const float4*>(b + c)));
+      const float4 y = ln_y4(v[i], st.x, st.y, lds128(sg + c * 4u), lds128(sb + c * 4u));
       *reinterpret_cast<uint32_t*>(qr + c) = quant4(y, inv);
     }
     for (long c = d + lane; c < ldq; c += 32) qr[c] = 0;
+  };
+  {
+    float4 va[NV], vb[NV];
+    long r = warp_g;
+    if (r < rows) load_row(r, va);
+    while (r < rows) {
+      const long r1 = r + nwarps;
+      if (r1 < rows) load_row(r1, vb);
+      quant_row(r, va);
+      if (r1 >= rows) break;
+      const long r2 = r1 + nwarps;
+      if (r2 < rows) load_row(r2, va);
+      quant_row(r1, vb);
+      r = r2;
+    }
   }
 }
 
