@@ -14,10 +14,18 @@ inline int grid_for(long work, int block) {
   return static_cast<int>(g < 1 ? 1 : g);
 }
 
+// Two elements per thread and step through gelu_erf2 (the GEMM epilogue's
+// form), the odd tail through gelu_erf.
 __global__ void gelu_kernel(const float* __restrict__ x, float* __restrict__ out, long n) {
-  for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n;
-       i += static_cast<long>(gridDim.x) * blockDim.x)
-    out[i] = gelu_erf(x[i]);
+  const long np = n / 2;
+  for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < np;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    float a = x[2 * i], b = x[2 * i + 1];
+    gelu_erf2(a, b);
+    out[2 * i] = a;
+    out[2 * i + 1] = b;
+  }
+  if ((n & 1) && blockIdx.x == 0 && threadIdx.x == 0) out[n - 1] = gelu_erf(x[n - 1]);
 }
 
 __global__ void residual_kernel(float* __restrict__ y, const float* __restrict__ x, long n) {

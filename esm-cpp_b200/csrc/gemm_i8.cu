@@ -454,7 +454,7 @@ __global__ void __maxnreg__(EW == 16 ? 96 : 168)
         }
         if (p.epi.kind == kEpiGelu) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) y[j] = gelu_erf(y[j]);
+          for (int j = 0; j < 32; j += 2) gelu_erf2(y[j], y[j + 1]);
         }
         if (row_ok && p.epi.amax != nullptr) {
           if (n0 + 32 <= p.N) {  // warp-uniform: the whole chunk is in range
