@@ -179,20 +179,33 @@ __device__ __forceinline__ float p_chunks(uint32_t tS, uint32_t tPlo, uint32_t s
                                           int nchunk, int L, float mx, WaitLo&& wait_lo,
                                           Arrive&& arrive) {
   const float kLog2e = 1.4426950408889634f;
-  float sum = 0.0f;
+  // Two keys per packed f32x2 instruction (each rounded as its scalar form);
+  // the row sum is kept as two interleaved partial sums.
+  const unsigned long long mx2 = f2_pack(mx, mx), l2e2 = f2_pack(kLog2e, kLog2e);
+  unsigned long long sum2 = f2_pack(0.0f, 0.0f);
   for (int c = par; c < nchunk; c += 2) {
     uint32_t hi[32], lo[32];
     tmem_ld32(tS + 32u * c, hi);
     tmem_ld_wait();
     const int nvalid = L - c * 32;  // keys j < nvalid are valid
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      float pv = ex2_ftz(__fmul_rn(__fsub_rn(__uint_as_float(hi[j]), mx), kLog2e));
-      pv = j < nvalid ? pv : 0.0f;
-      sum = __fadd_rn(sum, pv);
-      const float ph = __uint_as_float(__float_as_uint(pv) & 0xFFFFE000u);
-      hi[j] = __float_as_uint(ph);
-      lo[j] = __float_as_uint(__fsub_rn(pv, ph));
+    for (int j = 0; j < 32; j += 2) {
+      float t0, t1;
+      f2_unpack(f2_mul(f2_sub(f2_pack(__uint_as_float(hi[j]), __uint_as_float(hi[j + 1])), mx2), l2e2),
+                t0, t1);
+      float p0 = ex2_ftz(t0), p1 = ex2_ftz(t1);  // masked after, not guarded
+      p0 = j < nvalid ? p0 : 0.0f;
+      p1 = j + 1 < nvalid ? p1 : 0.0f;
+      const unsigned long long pv = f2_pack(p0, p1);
+      sum2 = f2_add(sum2, pv);
+      const float h0 = __uint_as_float(__float_as_uint(p0) & 0xFFFFE000u);
+      const float h1 = __uint_as_float(__float_as_uint(p1) & 0xFFFFE000u);
+      hi[j] = __float_as_uint(h0);
+      hi[j + 1] = __float_as_uint(h1);
+      float l0, l1;
+      f2_unpack(f2_sub(pv, f2_pack(h0, h1)), l0, l1);
+      lo[j] = __float_as_uint(l0);
+      lo[j + 1] = __float_as_uint(l1);
     }
     tmem_st32(tS + 32u * c, hi);  // S chunk c is this warp's alone once read
     wait_lo(c);
@@ -202,7 +215,9 @@ __device__ __forceinline__ float p_chunks(uint32_t tS, uint32_t tPlo, uint32_t s
     __syncwarp();
     arrive(c);
   }
-  return sum;
+  float s0, s1;
+  f2_unpack(sum2, s0, s1);
+  return __fadd_rn(s0, s1);
 }
 
 __global__ void __maxnreg__(128)
@@ -300,9 +315,10 @@ __global__ void __maxnreg__(128)
         const uint32_t slot = smem_u32(smem + s * kSlotBytes);
         const int L = cur.L, Lk16 = (L + 15) & ~15, nchunk = (L + KC - 1) / KC;
         if (!(ok = mbar_wait_abort(&bar[kQKReady + s], (n >> 1) & 1, status, abort_flag))) break;
-        // The single S buffer holds item n-1's P_hi until its P.V is done.
-        if (n >= 1 && !(ok = mbar_wait_abort(&bar[kODone + ((n - 1) & 1)], ((n - 1) >> 1) & 1, status, abort_flag)))
-          break;
+        // The single S buffer still holds item n-1's P_hi, read by the P.V
+        // MMAs this thread issued before: tcgen05.mma from one thread execute
+        // in issue order, so S(n) is issued without waiting for them to finish
+        // (the same reuse of P's TMEM by the next S as in CUTLASS's sm100 FMHA).
         tc_fence_after();
         const uint32_t tS = tmem;
         const uint32_t idS = idesc_tf32(QB, Lk16);
@@ -673,8 +689,9 @@ __global__ void __maxnreg__(128)
         const uint32_t slot = smem_u32(smem + kPSlot0 + s * kSlotBytes);
         const int L = cur.L, Lk16 = (L + 15) & ~15, nchunk = (L + KC - 1) / KC;
         if (!(ok = mbar_wait_cluster_abort(&bar[kPQKReady + s], (n >> 1) & 1, status, abort_flag))) break;
-        // The single S buffer: item n-1's P.V must be done with it.
-        if (n >= 1 && !(ok = mbar_wait_abort(&bar[kPODone], (n - 1) & 1, status, abort_flag))) break;
+        // The single S buffer still holds item n-1's P_hi: issued after that
+        // item's P.V MMAs by this thread, S(n) executes after them (in-order
+        // tcgen05.mma), so no wait on their completion.
         tc_fence_after();
         const uint32_t idS = idesc_tf32(2 * QB, Lk16);
 #pragma unroll
