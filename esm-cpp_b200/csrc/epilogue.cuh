@@ -111,22 +111,27 @@ __device__ __forceinline__ float epi_row_run(const EpiParams& e, long m, int c0,
 // 16-byte chunk i4 at position i4 ^ swz.
 __device__ __forceinline__ void epi_qkv_rope_values(const EpiParams& e, uint32_t cs_row,
                                                     int swz, int which, float (&y)[64]) {
+  // Two columns per packed f32x2 instruction, the scalar rounding per column.
   if (which == 0) {
+    const unsigned long long qs = f2_pack(e.q_scale, e.q_scale);
 #pragma unroll
-    for (int j = 0; j < 64; ++j) y[j] = __fmul_rn(y[j], e.q_scale);
+    for (int j = 0; j < 64; j += 2) f2_unpack(f2_mul(f2_pack(y[j], y[j + 1]), qs), y[j], y[j + 1]);
   }
   if (which <= 1) {
 #pragma unroll
     for (int i4 = 0; i4 < 8; ++i4) {
       const uint32_t o = static_cast<uint32_t>((i4 ^ swz) << 4);
       const float4 cv = lds128(cs_row + o), sv = lds128(cs_row + 128u + o);
-      const float cc[4] = {cv.x, cv.y, cv.z, cv.w}, ss[4] = {sv.x, sv.y, sv.z, sv.w};
+      const unsigned long long c2[2] = {f2_pack(cv.x, cv.y), f2_pack(cv.z, cv.w)};
+      const unsigned long long s2[2] = {f2_pack(sv.x, sv.y), f2_pack(sv.z, sv.w)};
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int i = 4 * i4 + k;
-        const float lo = y[i], hi = y[i + 32];
-        y[i] = __fmaf_rn(-hi, ss[k], __fmul_rn(lo, cc[k]));
-        y[i + 32] = __fmaf_rn(hi, cc[k], __fmul_rn(lo, ss[k]));
+      for (int k = 0; k < 2; ++k) {
+        const int i = 4 * i4 + 2 * k;
+        const unsigned long long lo = f2_pack(y[i], y[i + 1]), hi = f2_pack(y[i + 32], y[i + 33]);
+        const unsigned long long nhi = f2_pack(-y[i + 32], -y[i + 33]);
+        // lo' = fma(-hi, s, lo * c), hi' = fma(hi, c, lo * s)
+        f2_unpack(f2_fma(nhi, s2[k], f2_mul(lo, c2[k])), y[i], y[i + 1]);
+        f2_unpack(f2_fma(hi, c2[k], f2_mul(lo, s2[k])), y[i + 32], y[i + 33]);
       }
     }
   }

@@ -408,12 +408,20 @@ __global__ void __maxnreg__(EW == 16 ? 96 : 168)
           for (int j4 = 0; j4 < 8; ++j4) {
             const uint32_t o = static_cast<uint32_t>((jc0 + 4 * j4) * 4);
             const float4 w = lds128(wsv_s + o), b = lds128(bsv_s + o);
-            const float ws[4] = {w.x, w.y, w.z, w.w}, bs[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const float sc = p.per_token ? __fmul_rn(ws[u], as) : ws[u];
-              y[4 * j4 + u] = __fmaf_rn(__int2float_rn(static_cast<int>(r[4 * j4 + u])), sc, bs[u]);
+            unsigned long long w01 = f2_pack(w.x, w.y), w23 = f2_pack(w.z, w.w);
+            if (p.per_token) {
+              const unsigned long long as2 = f2_pack(as, as);
+              w01 = f2_mul(w01, as2);
+              w23 = f2_mul(w23, as2);
             }
+            const int* ri = reinterpret_cast<const int*>(r) + 4 * j4;
+            // fma(float(acc), scale, bias) two columns per instruction
+            f2_unpack(f2_fma(f2_pack(__int2float_rn(ri[0]), __int2float_rn(ri[1])), w01,
+                             f2_pack(b.x, b.y)),
+                      y[4 * j4], y[4 * j4 + 1]);
+            f2_unpack(f2_fma(f2_pack(__int2float_rn(ri[2]), __int2float_rn(ri[3])), w23,
+                             f2_pack(b.z, b.w)),
+                      y[4 * j4 + 2], y[4 * j4 + 3]);
           }
         }
       };
