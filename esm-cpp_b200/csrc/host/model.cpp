@@ -644,31 +644,107 @@ int forward_packed_host(esmcu_model* m, const int32_t* ids, const int32_t* masks
   return check_device_status(m->ctx);
 }
 
-// One scheduled group: pack, forward, scatter into caller order.
-int run_group(esmcu_model* m, const std::vector<int>& group, const int32_t* ids_concat,
-              const std::vector<long>& offsets, const int32_t* lens, const int32_t* masks_concat,
-              float* logits) {
-  const int V = m->cfg.vocab_size;
-  std::vector<int32_t> ids, masks, cu(group.size() + 1, 0);
-  for (size_t gi = 0; gi < group.size(); ++gi) {
-    const int idx = group[gi];
-    ids.insert(ids.end(), ids_concat + offsets[static_cast<size_t>(idx)],
-               ids_concat + offsets[static_cast<size_t>(idx)] + lens[idx]);
+// Several scheduled groups on one device, enqueued back to back: every
+// group's ids / masks / cu go through its own region of the pinned staging
+// buffer, its forward runs in the (shared, stream-ordered) arena and its
+// logits come back into its own pinned region; one synchronisation at the
+// end, then the logits are scattered into caller order.  The host packing of
+// group g+1 and the scatter no longer sit between the GPU's groups.
+int run_groups(esmcu_model* m, const std::vector<std::vector<int>>& groups, const int32_t* ids_concat,
+               const std::vector<long>& offsets, const int32_t* lens, const int32_t* masks_concat,
+               float* logits) {
+  if (m == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "null model");
+  TRY(use_device(m->ctx));
+  if (!model_ready(m)) return fail(ESMCU_ERR_INVALID_ARGUMENT, "model weights are not fully set");
+  const size_t V = static_cast<size_t>(m->cfg.vocab_size);
+  struct Packed {
+    const std::vector<int>* group;
+    std::vector<int32_t> ids, masks, cu;
+    int T = 0, B = 0, max_len = 0;
+    Arena a{};
+    size_t off_ids = 0, off_masks = 0, off_cu = 0, off_logits = 0;
+  };
+  std::vector<Packed> ps;
+  size_t arena_need = 0, pin = 0;
+  int max_len_all = 0;
+  for (const auto& g : groups) {
+    if (g.empty()) continue;
+    Packed p;
+    p.group = &g;
+    p.cu.assign(g.size() + 1, 0);
+    for (size_t gi = 0; gi < g.size(); ++gi) {
+      const int idx = g[gi];
+      const int32_t* src = ids_concat + offsets[static_cast<size_t>(idx)];
+      p.ids.insert(p.ids.end(), src, src + lens[idx]);
+      if (masks_concat) {
+        const int32_t* ms = masks_concat + offsets[static_cast<size_t>(idx)];
+        p.masks.insert(p.masks.end(), ms, ms + lens[idx]);
+      }
+      p.cu[gi + 1] = p.cu[gi] + lens[idx];
+    }
+    p.T = p.cu.back();
+    p.B = static_cast<int>(g.size());
+    if (p.T == 0) continue;
+    std::string msg = ValidateBatchView(p.T, masks_concat ? p.T : 0, p.cu.data(), p.B + 1, p.B);
+    if (!msg.empty()) return fail(ESMCU_ERR_INVALID_ARGUMENT, msg);
+    for (int32_t id : p.ids)
+      if (id < 0 || id >= m->cfg.vocab_size)
+        return fail(ESMCU_ERR_OUT_OF_RANGE, "token id " + std::to_string(id) + " out of range");
+    int min_len = p.cu[1] - p.cu[0];
+    for (int b = 0; b < p.B; ++b) {
+      p.max_len = std::max(p.max_len, p.cu[b + 1] - p.cu[b]);
+      min_len = std::min(min_len, p.cu[b + 1] - p.cu[b]);
+    }
+    max_len_all = std::max(max_len_all, p.max_len);
+    p.a = plan_arena(m, p.T, p.B);
+    p.a.min_len = min_len;
+    arena_need = std::max(arena_need, p.a.total);
+    const size_t n_ids = static_cast<size_t>(p.T) * 4;
+    p.off_ids = pin;
+    pin += align_up(n_ids, 256);
+    p.off_masks = pin;
+    if (masks_concat) pin += align_up(n_ids, 256);
+    p.off_cu = pin;
+    pin += align_up(static_cast<size_t>(p.B + 1) * 4, 256);
+    p.off_logits = pin;
+    pin += align_up(static_cast<size_t>(p.T) * V * 4, 256);
+    ps.push_back(std::move(p));
+  }
+  if (ps.empty()) return ESMCU_OK;
+  TRY(ensure_rope(m, max_len_all));
+  TRY(ensure_arena(m, arena_need));
+  TRY(ensure_pinned(m, pin));
+  m->launches = 0;
+  cudaStream_t s = m->ctx->stream;
+  char* base = m->arena;
+  char* hp = m->pinned;
+  for (auto& p : ps) {
+    const size_t n_ids = static_cast<size_t>(p.T) * 4, n_cu = static_cast<size_t>(p.B + 1) * 4;
+    std::memcpy(hp + p.off_ids, p.ids.data(), n_ids);
+    if (masks_concat) std::memcpy(hp + p.off_masks, p.masks.data(), n_ids);
+    std::memcpy(hp + p.off_cu, p.cu.data(), n_cu);
+    ESMCU_CUDA(cudaMemcpyAsync(base + p.a.ids, hp + p.off_ids, n_ids, cudaMemcpyHostToDevice, s));
     if (masks_concat)
-      masks.insert(masks.end(), masks_concat + offsets[static_cast<size_t>(idx)],
-                   masks_concat + offsets[static_cast<size_t>(idx)] + lens[idx]);
-    cu[gi + 1] = cu[gi] + lens[idx];
+      ESMCU_CUDA(cudaMemcpyAsync(base + p.a.masks, hp + p.off_masks, n_ids, cudaMemcpyHostToDevice, s));
+    ESMCU_CUDA(cudaMemcpyAsync(base + p.a.cu, hp + p.off_cu, n_cu, cudaMemcpyHostToDevice, s));
+    float* d_logits = reinterpret_cast<float*>(base + p.a.logits);
+    TRY(forward_device(m, p.a, reinterpret_cast<const int*>(base + p.a.ids),
+                       masks_concat ? reinterpret_cast<const int*>(base + p.a.masks) : nullptr,
+                       d_logits, p.T, p.B, p.max_len, 0.0f, nullptr));
+    ESMCU_CUDA(cudaMemcpyAsync(hp + p.off_logits, d_logits, static_cast<size_t>(p.T) * V * 4,
+                               cudaMemcpyDeviceToHost, s));
   }
-  const int T = cu.back();
-  std::vector<float> out(static_cast<size_t>(T) * V);
-  TRY(forward_packed_host(m, ids.data(), masks_concat ? masks.data() : nullptr, T, cu.data(),
-                          static_cast<int>(group.size()), out.data(), 0.0f, nullptr));
-  for (size_t gi = 0; gi < group.size(); ++gi) {
-    const int idx = group[gi];
-    std::memcpy(logits + offsets[static_cast<size_t>(idx)] * V, out.data() + static_cast<size_t>(cu[gi]) * V,
-                static_cast<size_t>(lens[idx]) * V * sizeof(float));
+  ESMCU_CUDA(cudaStreamSynchronize(s));
+  for (const auto& p : ps) {
+    const float* src = reinterpret_cast<const float*>(hp + p.off_logits);
+    for (size_t gi = 0; gi < p.group->size(); ++gi) {
+      const int idx = (*p.group)[gi];
+      std::memcpy(logits + offsets[static_cast<size_t>(idx)] * static_cast<long>(V),
+                  src + static_cast<size_t>(p.cu[gi]) * V, static_cast<size_t>(lens[idx]) * V * sizeof(float));
+    }
   }
-  return ESMCU_OK;
+  if (m->profiling) collect_profile(m, true);
+  return check_device_status(m->ctx);
 }
 
 int check_sched_args(const int32_t* ids_concat, const int32_t* lens, int n, float* logits) {
@@ -874,11 +950,7 @@ int esmcu_model_forward_scheduled(esmcu_model* m, const int32_t* ids_concat, con
   std::vector<long> offsets(static_cast<size_t>(n) + 1, 0);
   for (int i = 0; i < n; ++i) offsets[static_cast<size_t>(i) + 1] = offsets[static_cast<size_t>(i)] + lens[i];
   auto plan = PlanBatches(lengths, threshold, max_batch);
-  for (const auto& g : plan) {
-    if (g.empty()) continue;
-    TRY(run_group(m, g, ids_concat, offsets, lens, masks_concat, logits));
-  }
-  return ESMCU_OK;
+  return run_groups(m, plan, ids_concat, offsets, lens, masks_concat, logits);
 }
 
 int esmcu_forward_scheduled_multi(esmcu_model** models, int n_models, const int32_t* ids_concat,
@@ -915,14 +987,12 @@ int esmcu_forward_scheduled_multi(esmcu_model** models, int n_models, const int3
   std::vector<std::thread> threads;
   for (int w = 0; w < n_models; ++w) {
     threads.emplace_back([&, w]() {
-      for (int g : assign[static_cast<size_t>(w)]) {
-        int r = run_group(models[w], plan[static_cast<size_t>(g)], ids_concat, offsets, lens,
-                          masks_concat, logits);
-        if (r != ESMCU_OK) {
-          rc[static_cast<size_t>(w)] = r;
-          err[static_cast<size_t>(w)] = esmcu_last_error();
-          return;
-        }
+      std::vector<std::vector<int>> mine;
+      for (int g : assign[static_cast<size_t>(w)]) mine.push_back(plan[static_cast<size_t>(g)]);
+      int r = run_groups(models[w], mine, ids_concat, offsets, lens, masks_concat, logits);
+      if (r != ESMCU_OK) {
+        rc[static_cast<size_t>(w)] = r;
+        err[static_cast<size_t>(w)] = esmcu_last_error();
       }
     });
   }
