@@ -152,13 +152,31 @@ __global__ void embed_kernel(const float* __restrict__ embed_w, int d, const int
       src_len > 0 ? __fdiv_rn(static_cast<float>(observed), static_cast<float>(src_len)) : 0.0f;
   const float denom = fmaxf(__fsub_rn(1.0f, obs_ratio), 1e-12f);
   const float scale = __fdiv_rn(__fsub_rn(1.0f, ratio_train), denom);
-  const long n = static_cast<long>(s1 - s0) * d;
-  for (long w = threadIdx.x; w < n; w += blockDim.x) {
-    const int t = s0 + static_cast<int>(w / d);
-    const int c = static_cast<int>(w % d);
+  // Rows: one warp per token, blockIdx.y splitting the sequence's tokens over
+  // gridDim.y blocks (each recomputes the sequence's counts above), float4
+  // columns when d % 4 == 0 and the tables are 16-byte aligned.
+  const int nw = static_cast<int>(blockDim.x >> 5), warp = static_cast<int>(threadIdx.x >> 5);
+  const int lane = static_cast<int>(threadIdx.x & 31);
+  const int step = nw * static_cast<int>(gridDim.y);
+  const bool vec = (d % 4 == 0) && ((reinterpret_cast<uintptr_t>(embed_w) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+  for (int t = s0 + static_cast<int>(blockIdx.y) * nw + warp; t < s1; t += step) {
     const int id = ids[t];
     const bool zero = (id == mask_id) || (masks != nullptr && masks[t] == 0);
-    out[static_cast<long>(t) * d + c] = zero ? 0.0f : __fmul_rn(__ldg(embed_w + static_cast<long>(id) * d + c), scale);
+    const float* src = embed_w + static_cast<long>(id) * d;
+    float* dst = out + static_cast<long>(t) * d;
+    if (vec) {
+      for (int c4 = lane; c4 < d / 4; c4 += 32) {
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (!zero) {
+          const float4 w = __ldg(reinterpret_cast<const float4*>(src) + c4);
+          v = make_float4(__fmul_rn(w.x, scale), __fmul_rn(w.y, scale), __fmul_rn(w.z, scale),
+                          __fmul_rn(w.w, scale));
+        }
+        reinterpret_cast<float4*>(dst)[c4] = v;
+      }
+    } else {
+      for (int c = lane; c < d; c += 32) dst[c] = zero ? 0.0f : __fmul_rn(__ldg(src + c), scale);
+    }
   }
 }
 
@@ -215,7 +233,7 @@ cudaError_t launch_positions(const int* cu, int B, int* pos, cudaStream_t s) {
 cudaError_t launch_embed(const float* embed_w, int d, const int* ids, const int* masks,
                          const int* cu, int B, int mask_id, float* out, cudaStream_t s) {
   if (B <= 0) return cudaSuccess;
-  embed_kernel<<<B, 256, 0, s>>>(embed_w, d, ids, masks, cu, B, mask_id, out);
+  embed_kernel<<<dim3(B, 4), 256, 0, s>>>(embed_w, d, ids, masks, cu, B, mask_id, out);
   return cudaGetLastError();
 }
 
