@@ -200,13 +200,12 @@ __device__ __forceinline__ uint32_t quant4(float4 y, float inv) {
          ((static_cast<uint32_t>(a2) & 0xffu) << 16) | ((static_cast<uint32_t>(a3) & 0xffu) << 24);
 }
 
-// 12 warps, one block per SM (up to 168 registers).  Each warp keeps two
-// rows in registers: the next row's loads are in flight while the current
-// one is reduced or quantised.  Gamma and beta are read from shared memory.
+// 12 warps per block, two blocks per SM (at most 80 registers: gamma and beta
+// come from shared memory and the statistics take one pass), a row per warp.
 constexpr int kLqThreads = 384;
 
 template <int NV>
-__global__ void __launch_bounds__(kLqThreads, 1)
+__global__ void __launch_bounds__(kLqThreads, 2)
     ln_quant_kernel(const float* __restrict__ x, const float* __restrict__ g,
                     const float* __restrict__ b, float eps, int rows, int d, uint32_t* amax,
                     float2* stats, uint32_t* counter, int8_t* __restrict__ q, long ldq,
@@ -262,20 +261,10 @@ __global__ void __launch_bounds__(kLqThreads, 1)
     if (lane == 0) stats[r] = make_float2(meanf, inv_std);
     tmax = fmaxf(tmax, mx);
   };
-  {
-    float4 va[NV], vb[NV];
-    long r = warp_g;
-    if (r < rows) load_row(r, va);
-    while (r < rows) {
-      const long r1 = r + nwarps;
-      if (r1 < rows) load_row(r1, vb);
-      stats_row(r, va);
-      if (r1 >= rows) break;
-      const long r2 = r1 + nwarps;
-      if (r2 < rows) load_row(r2, va);
-      stats_row(r1, vb);
-      r = r2;
-    }
+  for (long r = warp_g; r < rows; r += nwarps) {
+    float4 va[NV];
+    load_row(r, va);
+    stats_row(r, va);
   }
   amax_publish(amax, tmax);
   grid_barrier_once(counter, status);
@@ -305,20 +294,10 @@ __global__ void __launch_bounds__(kLqThreads, 1)
     }
     for (long c = d + lane; c < ldq; c += 32) qr[c] = 0;
   };
-  {
-    float4 va[NV], vb[NV];
-    long r = warp_g;
-    if (r < rows) load_row(r, va);
-    while (r < rows) {
-      const long r1 = r + nwarps;
-      if (r1 < rows) load_row(r1, vb);
-      quant_row(r, va);
-      if (r1 >= rows) break;
-      const long r2 = r1 + nwarps;
-      if (r2 < rows) load_row(r2, va);
-      quant_row(r1, vb);
-      r = r2;
-    }
+  for (long r = warp_g; r < rows; r += nwarps) {
+    float4 va[NV];
+    load_row(r, va);
+    quant_row(r, va);
   }
 }
 
