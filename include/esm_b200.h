@@ -78,7 +78,10 @@ int esmcu_memcpy_d2h(esmcu_context* ctx, void* dst, const void* src, size_t byte
 /* ---- kernel facade (device pointers) ------------------------------------
  * Each replaces the esm::kernels function named in its comment. */
 
-/* kernels.h:19-20 Linear: C[M,N] = A[M,K] . W[N,K]^T + bias (bias nullable). */
+/* kernels.h:19-20 Linear: C[M,N] = A[M,K] . W[N,K]^T + bias (bias nullable).
+ * FP32-accurate: 3xTF32 on the tensor cores when K % 4 == 0 and A, W are
+ * 16-byte aligned (the lo parts of A and W, 4*(M+N)*K bytes, go to the
+ * context's scratch, which grows on demand), FP32 SIMT otherwise. */
 int esmcu_linear(esmcu_context* ctx, const float* A, const float* W, const float* bias,
                  float* C, int M, int N, int K);
 
