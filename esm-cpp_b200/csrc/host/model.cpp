@@ -62,6 +62,9 @@ struct esmcu_model {
         *lm_bias = nullptr;
   float* lm_w_lo = nullptr;   // lm_w - tf32(lm_w), for the 3xTF32 dense GEMM
   float* embed_lo = nullptr;  // the same for the tied decoder (embed^T)
+  // Device staging of the hidden states for ForwardWithHiddenStates.
+  float* hs_dev = nullptr;
+  size_t hs_bytes = 0;
   bool embed_set = false, head_set = false;
   float *cos_t = nullptr, *sin_t = nullptr;
   int rope_len = 0;
@@ -289,8 +292,12 @@ float host_percentile(const float* dev, size_t n, float pctile, cudaStream_t s) 
 
 // The packed forward on device buffers already in the arena.  When stats
 // is non-null (calibration), writes the four per-layer site percentiles.
+// hidden (device, nullable): [num_layers + 1, T, d] receives the hidden
+// states of ForwardPackedInto's hidden_packed_out (model.cpp:1142-1189): the
+// embedding output, each layer's output, and in the last entry the final
+// LayerNorm's output in place of the last layer's.
 int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk, float* logits,
-                   int T, int B, int max_len, float pctile, float* stats) {
+                   int T, int B, int max_len, float pctile, float* stats, float* hidden_out = nullptr) {
   const auto& c = m->cfg;
   esmcu_context* ctx = m->ctx;
   cudaStream_t s = ctx->stream;
@@ -323,6 +330,8 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
   sec.begin("embed");
   LAUNCH(m, launch_embed(m->embed, d, ids, mk, cu, B, c.mask_token_id, hidden, s));
   sec.end();
+  const size_t Tdh = static_cast<size_t>(T) * c.hidden_size;
+  if (hidden_out) ESMCU_CUDA(cudaMemcpyAsync(hidden_out, hidden, Tdh * 4, cudaMemcpyDeviceToDevice, s));
 
   // INT8 GEMM helper: A = quantised activations in q8 (row stride lda).
   auto gemm_i8 = [&](const int8_t* W, long ldk, int N, const float* ws, const float* bias,
@@ -502,6 +511,9 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
       }
     }
     sec.end();
+    if (hidden_out && li + 1 < c.num_layers)
+      ESMCU_CUDA(cudaMemcpyAsync(hidden_out + (li + 1) * Tdh, hidden, Tdh * 4,
+                                 cudaMemcpyDeviceToDevice, s));
   }
 
   // ---- final LN + LM head (model.cpp:1181-1239), FP32
@@ -509,6 +521,9 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
   LAUNCH(m, launch_layernorm(hidden, m->final_ln_w, m->final_ln_b, c.layer_norm_eps, ln, T, d,
                              nullptr, nullptr, 0, nullptr, s));
   sec.end();
+  if (hidden_out)  // the last entry is the final LayerNorm's output
+    ESMCU_CUDA(cudaMemcpyAsync(hidden_out + static_cast<size_t>(c.num_layers) * Tdh, ln, Tdh * 4,
+                               cudaMemcpyDeviceToDevice, s));
   sec.begin("lm_dense");
   {
     EpiParams e;
@@ -607,12 +622,13 @@ int prepare(esmcu_model* m, int T, bool has_masks, const int32_t* cu, int B, Are
 
 // Packed forward from host buffers; logits (host) [T, V].
 int forward_packed_host(esmcu_model* m, const int32_t* ids, const int32_t* masks, int T,
-                        const int32_t* cu, int B, float* logits, float pctile, float* stats) {
+                        const int32_t* cu, int B, float* logits, float pctile, float* stats,
+                        float* hidden = nullptr) {
   Arena a;
   int max_len = 0;
   TRY(prepare(m, T, masks != nullptr, cu, B, &a, &max_len));
   if (T == 0) return ESMCU_OK;  // model.cpp:1105-1108
-  if (ids == nullptr || (logits == nullptr && stats == nullptr))
+  if (ids == nullptr || (logits == nullptr && stats == nullptr && hidden == nullptr))
     return fail(ESMCU_ERR_INVALID_ARGUMENT, "ids/logits is null");
   for (int t = 0; t < T; ++t)
     if (ids[t] < 0 || ids[t] >= m->cfg.vocab_size)
@@ -634,12 +650,22 @@ int forward_packed_host(esmcu_model* m, const int32_t* ids, const int32_t* masks
   if (masks) ESMCU_CUDA(cudaMemcpyAsync(base + a.masks, pin + off_masks, n_ids, cudaMemcpyHostToDevice, s));
   ESMCU_CUDA(cudaMemcpyAsync(base + a.cu, pin + off_cu, n_cu, cudaMemcpyHostToDevice, s));
   float* d_logits = reinterpret_cast<float*>(base + a.logits);
+  const size_t n_hidden = hidden ? static_cast<size_t>(m->cfg.num_layers + 1) * T * m->cfg.hidden_size * 4 : 0;
+  if (n_hidden > m->hs_bytes) {
+    ESMCU_CUDA(cudaStreamSynchronize(s));
+    if (m->hs_dev) ESMCU_CUDA(cudaFree(m->hs_dev));
+    m->hs_dev = nullptr;
+    m->hs_bytes = 0;
+    ESMCU_CUDA(cudaMalloc(&m->hs_dev, n_hidden));
+    m->hs_bytes = n_hidden;
+  }
   TRY(forward_device(m, a, reinterpret_cast<const int*>(base + a.ids),
                      masks ? reinterpret_cast<const int*>(base + a.masks) : nullptr, d_logits, T, B,
-                     max_len, pctile, stats));
+                     max_len, pctile, stats, hidden ? m->hs_dev : nullptr));
   if (logits) ESMCU_CUDA(cudaMemcpyAsync(pin + off_logits, d_logits, n_logits, cudaMemcpyDeviceToHost, s));
   ESMCU_CUDA(cudaStreamSynchronize(s));
   if (logits) std::memcpy(logits, pin + off_logits, n_logits);
+  if (hidden) ESMCU_CUDA(cudaMemcpy(hidden, m->hs_dev, n_hidden, cudaMemcpyDeviceToHost));
   if (m->profiling) collect_profile(m, true);
   return check_device_status(m->ctx);
 }
@@ -800,6 +826,7 @@ int esmcu_model_destroy(esmcu_model* m) {
   for (auto e : m->event_pool) cudaEventDestroy(e);
   if (m->cos_t) cudaFree(m->cos_t);
   if (m->sin_t) cudaFree(m->sin_t);
+  if (m->hs_dev) cudaFree(m->hs_dev);
   delete m;
   return ESMCU_OK;
 }
@@ -915,6 +942,13 @@ int esmcu_model_set_layer(esmcu_model* m, int layer, const esmcu_layer_weights* 
 int esmcu_model_forward_packed(esmcu_model* m, const int32_t* ids, const int32_t* masks, int T,
                                const int32_t* cu, int B, float* logits) {
   return forward_packed_host(m, ids, masks, T, cu, B, logits, 0.0f, nullptr);
+}
+
+int esmcu_model_forward_hidden_states(esmcu_model* m, const int32_t* ids, const int32_t* masks,
+                                      int T, const int32_t* cu, int B, float* logits,
+                                      float* hidden_out) {
+  if (hidden_out == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "hidden_out is null");
+  return forward_packed_host(m, ids, masks, T, cu, B, logits, 0.0f, nullptr, hidden_out);
 }
 
 int esmcu_model_forward_packed_device(esmcu_model* m, const int32_t* d_ids,

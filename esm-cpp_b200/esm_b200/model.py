@@ -378,6 +378,44 @@ class Model:
             return np.empty((0, self._cfg.vocab_size), F32)
         return self.forward_packed(ids, np.array([0, ids.shape[0]], np.int32), attention_mask)[0]
 
+    def forward_packed_hidden_states(self, packed_ids, cu_seqlens, packed_masks=None):
+        """ForwardPackedInto with hidden_packed_out (model.cpp:1142-1189) on a
+        packed batch: (logits [T, V], hidden [num_layers + 1, T, d]) with
+        hidden[0] the embedding output, hidden[i] layer i-1's output and
+        hidden[num_layers] the final LayerNorm's output."""
+        self._ensure_device()
+        ids = np.ascontiguousarray(packed_ids, np.int32)
+        cu = np.ascontiguousarray(cu_seqlens, np.int32)
+        if ids.ndim != 1:
+            raise ValueError("packed_ids must be a 1-D int32 array")
+        if cu.ndim != 1 or cu.shape[0] < 2:
+            raise ValueError("cu_seqlens must be a 1-D int32 array of size batch + 1")
+        masks = None if packed_masks is None else np.ascontiguousarray(packed_masks, np.int32)
+        if masks is not None and masks.shape != ids.shape:
+            raise ValueError("packed_masks must be a 1-D int32 array of the same length as packed_ids")
+        c = self._cfg
+        T, B = ids.shape[0], cu.shape[0] - 1
+        logits = np.empty((T, c.vocab_size), F32)
+        hidden = np.empty((c.num_hidden_layers + 1, T, c.hidden_size), F32)
+        if T == 0:
+            return logits, hidden
+        _lib.call("esmcu_model_forward_hidden_states", self._dev, ids.ctypes.data,
+                  None if masks is None else masks.ctypes.data, T, cu.ctypes.data, B,
+                  logits.ctypes.data, hidden.ctypes.data)
+        return logits, hidden
+
+    def forward_with_hidden_states(self, input_ids, attention_mask=None):
+        """Model::ForwardWithHiddenStates (model.h:185-191; the Python binding
+        forward_with_hidden_states, _core.cpp:511-524): (logits [L, V],
+        [hidden_state_0, ..., hidden_state_N]), N = num_hidden_layers,
+        hidden_state_0 post-embed, hidden_state_N post-final-LN, each [L, d]."""
+        ids = np.ascontiguousarray(input_ids, np.int32)
+        if ids.ndim != 1:
+            raise ValueError("input_ids must be a 1-D int32 array")
+        logits, hidden = self.forward_packed_hidden_states(
+            ids, np.array([0, ids.shape[0]], np.int32), attention_mask)
+        return logits, [hidden[i] for i in range(hidden.shape[0])]
+
     def forward_scheduled(self, input_ids, attention_masks=None, imbalance_threshold: float = 1.2,
                           max_batch_size: int = 256):
         """Model::ForwardScheduled: logits in input order."""

@@ -196,6 +196,15 @@ int esmcu_model_set_head(esmcu_model* m, const float* final_ln_w, const float* f
  * writes nothing. */
 int esmcu_model_forward_packed(esmcu_model* m, const int32_t* ids, const int32_t* masks, int T,
                                const int32_t* cu_seqlens, int batch_size, float* logits);
+
+/* Model::ForwardWithHiddenStates (model.h:185-191) on a packed batch, the
+ * hidden_packed_out of ForwardPackedInto (model.cpp:1142-1189): host
+ * hidden_out [num_layers + 1, T, hidden_size] receives the embedding output,
+ * each layer's output and, last, the final LayerNorm's output (in place of
+ * the last layer's); logits [T, V] as esmcu_model_forward_packed, or NULL. */
+int esmcu_model_forward_hidden_states(esmcu_model* m, const int32_t* ids, const int32_t* masks,
+                                      int T, const int32_t* cu, int B, float* logits,
+                                      float* hidden_out);
 /* Model::ForwardScheduled (model.cpp:1298-1421): n sequences concatenated in
  * ids_concat with lengths lens[n] (masks_concat NULL = all real) -> logits
  * concatenated in caller order [sum(lens), V]. */

@@ -280,16 +280,22 @@ def plan_batches(lengths, threshold=1.2, max_batch=256):
     return out
 
 
-def forward_packed(model, ids, cu, masks=None, per_token: bool = False):
+def forward_packed(model, ids, cu, masks=None, per_token: bool = False, hidden=None):
     """ForwardPackedInto (model.cpp:1093-1255) + TransformerBlock
     (model.cpp:932-1066) composed from the restated ops; `model` is an
-    esm_b200.Model (host numpy weights).  Returns packed logits [T, V]."""
+    esm_b200.Model (host numpy weights).  Returns packed logits [T, V].
+    With a list as `hidden`, it receives hidden_packed_out (model.cpp:
+    1142-1189): the embedding output, each layer's output, and the final
+    LayerNorm's output in place of the last layer's (num_layers + 1 [T, d])."""
     c = model.config
     d, H, dh = c.hidden_size, c.num_attention_heads, c.head_dim
     ids, cu = _a(ids, np.int32), _a(cu, np.int32)
     T = ids.size
     maxL = int(np.max(np.diff(cu))) if cu.size > 1 else 0
     h = embed(model.embed, ids, cu, masks, c.mask_token_id)
+    if hidden is not None:
+        hidden.clear()
+        hidden.append(h.copy())
     cos_t, sin_t = rope_build_tables(max(maxL, 1), dh)
     qs = F32(1.0) / F32(np.sqrt(F32(dh)))
 
@@ -311,8 +317,12 @@ def forward_packed(model, ids, cu, masks=None, per_token: bool = False):
         ln = layernorm(h, lw["ffn_ln_w"], lw["ffn_ln_b"], c.layer_norm_eps)
         inter = gelu(lin(ln, lw, "fc1"))
         h = (h + lin(inter, lw, "fc2")).astype(F32)
+        if hidden is not None:
+            hidden.append(h.copy())
     hd = model.head
     fl = layernorm(h, hd["final_ln_w"], hd["final_ln_b"], c.layer_norm_eps)
+    if hidden is not None:
+        hidden[-1] = fl.copy()
     g = gelu(linear_f32(fl, hd["lm_dense_w"], hd["lm_dense_b"]))
     lm = layernorm(g, hd["lm_ln_w"], hd["lm_ln_b"], c.layer_norm_eps)
     return linear_f32(lm, model.embed, hd["lm_bias"])
@@ -344,6 +354,18 @@ class RefModel:
                                                  C.c_int(ids.size), cu.ctypes.data,
                                                  C.c_int(cu.size - 1), out.ctypes.data), "forward_packed")
         return out
+
+    def forward_hidden(self, ids):
+        """Model::ForwardWithHiddenStates for one sequence: (logits [L, V],
+        hidden [num_layers + 1, L, d])."""
+        ids = _a(ids, np.int32)
+        L = ids.size
+        logits = np.zeros((L, self.vocab), F32)
+        hidden = np.zeros((self.layers + 1, L, self.d), F32)
+        ref_check(ref().ref_model_forward_hidden(C.c_void_p(self.h), ids.ctypes.data, C.c_int(L),
+                                                 logits.ctypes.data, hidden.ctypes.data),
+                  "forward_hidden")
+        return logits, hidden
 
     def forward_scheduled(self, seqs, threshold=1.2, max_batch=256):
         lens = np.array([len(s) for s in seqs], np.int32)

@@ -14,6 +14,8 @@ Every array is produced by a reference entry point named in the key:
   plan_*     PlanBatches.
   model_*    Model::ForwardPacked of a tiny W8A8 model (its Q8_ESM GGUF
              tensors are stored alongside) and of the same model in FP32.
+  hidden_*   Model::ForwardWithHiddenStates of that model, FP32 and W8A8
+             (hidden_golden.npz), one sequence at a time, concatenated.
 """
 from __future__ import annotations
 
@@ -137,9 +139,37 @@ def model_fixture(path):
                         logits_q8_default=logits_default)
 
 
+def hidden_fixture(path, model_path):
+    """Model::ForwardWithHiddenStates (model.h:185-191) of the reference on
+    the tiny model of `model_fixture`, one sequence at a time: the embedding
+    output, each block's output but the last, and the final-LN output, for the
+    FP32 model and the W8A8 model (VNNI ISA)."""
+    M = np.load(model_path)
+    ids, cu = M["ids"], M["cu"]
+    out = {}
+    with tempfile.TemporaryDirectory() as td:
+        st = Path(td) / "m.safetensors"
+        st.write_bytes(M["safetensors"].tobytes())
+        gg = Path(td) / "m_q8.gguf"
+        gg.write_bytes(M["gguf_q8"].tobytes())
+        O.ref_force_isa("avx512vnni")
+        for tag, p in (("fp32", st), ("q8", gg)):
+            ref = O.RefModel(p)
+            hs, lg = [], []
+            for b in range(len(cu) - 1):
+                logits, hidden = ref.forward_hidden(ids[cu[b]:cu[b + 1]])
+                hs.append(hidden)
+                lg.append(logits)
+            out[f"hidden_{tag}"] = np.concatenate(hs, axis=1)
+            out[f"logits_{tag}"] = np.concatenate(lg, axis=0)
+        O.ref_force_isa(None)
+    np.savez_compressed(path, **out)
+
+
 if __name__ == "__main__":
     O.build()
     ops_fixture(HERE / "ops_golden.npz")
     model_fixture(HERE / "model_golden.npz")
+    hidden_fixture(HERE / "hidden_golden.npz", HERE / "model_golden.npz")
     for p in sorted(HERE.glob("*.npz")):
         print(p.name, p.stat().st_size, "bytes")

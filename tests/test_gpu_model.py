@@ -109,6 +109,52 @@ def test_w8a8_packed_matches_reference_via_gguf(tiny_q8, O, R, tmp_path):
     np.testing.assert_allclose(got, want, rtol=1e-3, atol=W8A8_ATOL)
 
 
+def test_fp32_hidden_states_match_reference(tiny_fp32, O, R, tmp_path):
+    """forward_with_hidden_states (the reference's binding, _core.cpp:511-524;
+    test_against_hf.py:100-125 checks the same N+1 states against HF): every
+    hidden state and the logits within the FP32 class of the reference's own
+    ForwardWithHiddenStates."""
+    p = tmp_path / "tiny_h.safetensors"
+    tiny_fp32.save_to_safetensors(p)
+    ref = O.RefModel(p)
+    ids = _batch([57], 11)[0][0]
+    logits, hidden = tiny_fp32.forward_with_hidden_states(ids)
+    want_logits, want_hidden = ref.forward_hidden(ids)
+    assert len(hidden) == TINY["num_hidden_layers"] + 1
+    for j in range(len(hidden)):
+        assert hidden[j].shape == (ids.size, TINY["hidden_size"])
+        _close(hidden[j], want_hidden[j])
+    _close(logits, want_logits)
+
+
+def test_hidden_states_packed_match_oracle_and_single(tiny_fp32, tiny_q8, O):
+    """The packed form (hidden_packed_out of ForwardPackedInto): the FP32
+    model matches the oracle's packed forward to the FP32 class and each
+    sequence's rows match its single-sequence call (1e-5); the W8A8
+    model matches the oracle under the whole-forward W8A8 gate."""
+    seqs, ids, cu = _batch([20, 64, 5], 12)
+    L1 = TINY["num_hidden_layers"] + 1
+    logits, hidden = tiny_fp32.forward_packed_hidden_states(ids, cu)
+    want = []
+    want_logits = O.forward_packed(tiny_fp32, ids, cu, hidden=want)
+    assert hidden.shape == (L1, ids.size, TINY["hidden_size"]) and len(want) == L1
+    for j in range(L1):
+        _close(hidden[j], want[j])
+    _close(logits, want_logits)
+    for b, s in enumerate(seqs):
+        _, hs = tiny_fp32.forward_with_hidden_states(s)
+        for j in range(L1):
+            _close(hidden[j][cu[b]:cu[b + 1]], hs[j], tol=1e-5)
+    lq, hq = tiny_q8.forward_packed_hidden_states(ids, cu)
+    wq = []
+    O.forward_packed(tiny_q8, ids, cu, hidden=wq)
+    assert np.array_equal(hq[0], wq[0])  # the embedding is exact
+    for j in range(1, L1):
+        np.testing.assert_allclose(hq[j], wq[j], rtol=1e-3, atol=W8A8_ATOL)
+        r = np.corrcoef(hq[j].ravel(), wq[j].ravel())[0, 1]
+        assert r >= W8A8_PEARSON, f"hidden state {j}: Pearson {r:.7f}"
+
+
 def test_gguf_round_trip_of_reference_artefact(tiny_fp32, O, R, tmp_path):
     """The reference calibrates, migrates, quantises and saves a Q8_ESM GGUF
     (quantize.py:35-91); this package loads it and matches the reference's
