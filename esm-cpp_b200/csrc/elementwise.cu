@@ -180,6 +180,33 @@ __global__ void embed_kernel(const float* __restrict__ embed_w, int d, const int
   }
 }
 
+// out[r] = x[rows[r]] for rows of d floats: the masked positions that the
+// masked-marginal head scores (eval/proteingym.py:84-88 reads logits[p + 1]
+// of each masked copy).  One block per selected row.
+__global__ void gather_rows_kernel(const float* __restrict__ x, const int* __restrict__ rows, int d,
+                                   float* __restrict__ out) {
+  const float* src = x + static_cast<long>(__ldg(rows + blockIdx.x)) * d;
+  float* dst = out + static_cast<long>(blockIdx.x) * d;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) dst[i] = src[i];
+}
+
+// In place, each row of x [R, V]: (x - max) - log(sum(exp(x - max))), the
+// order of eval/proteingym.py:48-50.  One warp per row.
+__global__ void log_softmax_rows_kernel(float* __restrict__ x, int R, int V) {
+  const long row = (blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= R) return;
+  float* xr = x + row * V;
+  float mx = -INFINITY;
+  for (int j = lane; j < V; j += 32) mx = fmaxf(mx, xr[j]);
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float sum = 0.0f;
+  for (int j = lane; j < V; j += 32) sum = __fadd_rn(sum, expf(__fsub_rn(xr[j], mx)));
+  for (int o = 16; o; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+  const float lse = logf(sum);
+  for (int j = lane; j < V; j += 32) xr[j] = __fsub_rn(__fsub_rn(xr[j], mx), lse);
+}
+
 }  // namespace
 
 cudaError_t launch_gelu(const float* x, float* out, long n, cudaStream_t s) {
@@ -234,6 +261,20 @@ cudaError_t launch_embed(const float* embed_w, int d, const int* ids, const int*
                          const int* cu, int B, int mask_id, float* out, cudaStream_t s) {
   if (B <= 0) return cudaSuccess;
   embed_kernel<<<dim3(B, 4), 256, 0, s>>>(embed_w, d, ids, masks, cu, B, mask_id, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gather_rows(const float* x, const int* rows, int R, int d, float* out,
+                               cudaStream_t s) {
+  if (R <= 0) return cudaSuccess;
+  gather_rows_kernel<<<R, 128, 0, s>>>(x, rows, d, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_log_softmax_rows(float* x, int R, int V, cudaStream_t s) {
+  if (R <= 0) return cudaSuccess;
+  const long threads = static_cast<long>(R) * 32;  // one warp per row
+  log_softmax_rows_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, s>>>(x, R, V);
   return cudaGetLastError();
 }
 

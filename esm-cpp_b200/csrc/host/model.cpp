@@ -45,6 +45,7 @@ struct DevLayer {
 // Byte offsets of the per-forward buffers inside the arena.
 struct Arena {
   size_t ids, masks, cu, pos, hidden, ln, q8, ascale, q, k, v, attn, inter, qkv, logits, amax;
+  size_t rows;  // packed row indices scored by the masked-marginal head
   size_t lnstat;  // per-row LayerNorm statistics of the fused LN + quantise kernel
   size_t total;
   int min_len = 0;  // shortest sequence of the batch (kernel choice)
@@ -181,6 +182,7 @@ Arena plan_arena(const esmcu_model* m, int T, int B) {
   a.logits = take(Tz * static_cast<size_t>(c.vocab_size) * 4);
   a.amax = take(amax_region_bytes(c.num_layers));
   a.lnstat = take(Tz * 8);
+  a.rows = take((static_cast<size_t>(B) + 1) * 4);
   a.total = cur;
   return a;
 }
@@ -296,8 +298,12 @@ float host_percentile(const float* dev, size_t n, float pctile, cudaStream_t s) 
 // states of ForwardPackedInto's hidden_packed_out (model.cpp:1142-1189): the
 // embedding output, each layer's output, and in the last entry the final
 // LayerNorm's output in place of the last layer's.
+// rows (device, nullable): the LM head runs on the R packed rows rows[0..R)
+// only, and logits [R, V] receive their log-softmax (the masked-marginal
+// head of eval/proteingym.py:84-98).
 int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk, float* logits,
-                   int T, int B, int max_len, float pctile, float* stats, float* hidden_out = nullptr) {
+                   int T, int B, int max_len, float pctile, float* stats, float* hidden_out = nullptr,
+                   const int* rows = nullptr, int R = 0) {
   const auto& c = m->cfg;
   esmcu_context* ctx = m->ctx;
   cudaStream_t s = ctx->stream;
@@ -355,13 +361,13 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
     return ESMCU_OK;
   };
   auto gemm_f32 = [&](const float* A, int K, const float* W, int N, const float* bias,
-                      EpiParams epi) -> int {
+                      EpiParams epi, int M = -1) -> int {
     GemmF32Args g;
     g.A = A;
     g.lda = K;
     g.W = W;
     g.ldw = K;
-    g.M = T;
+    g.M = M < 0 ? T : M;
     g.N = N;
     g.K = K;
     g.bias = bias;
@@ -524,6 +530,15 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
   if (hidden_out)  // the last entry is the final LayerNorm's output
     ESMCU_CUDA(cudaMemcpyAsync(hidden_out + static_cast<size_t>(c.num_layers) * Tdh, ln, Tdh * 4,
                                cudaMemcpyDeviceToDevice, s));
+  // The LM head is row-wise: with `rows` it runs on the selected rows only,
+  // gathered into `hidden` (free after the final LayerNorm).
+  const float* head_in = ln;
+  int TH = T;
+  if (rows) {
+    LAUNCH(m, launch_gather_rows(ln, rows, R, d, hidden, s));
+    head_in = hidden;
+    TH = R;
+  }
   sec.begin("lm_dense");
   {
     EpiParams e;
@@ -533,15 +548,15 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
     if (d % 4 == 0) {
       // 3xTF32 on the tensor cores; the lo part of `ln` goes to `k` (free
       // once the layers are done).
-      LAUNCH(m, launch_tf32_lo(ln, k, static_cast<long>(T) * d, s));
+      LAUNCH(m, launch_tf32_lo(head_in, k, static_cast<long>(TH) * d, s));
       GemmTf32Args g;
-      g.A = ln;
+      g.A = head_in;
       g.A_lo = k;
       g.lda = d;
       g.W = m->lm_w;
       g.W_lo = m->lm_w_lo;
       g.ldw = d;
-      g.M = T;
+      g.M = TH;
       g.N = d;
       g.K = d;
       g.bias = m->lm_b;
@@ -550,12 +565,12 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
       g.num_sms = ctx->num_sms;
       LAUNCH(m, launch_gemm_tf32x3(g, s));
     } else {
-      TRY(gemm_f32(ln, d, m->lm_w, d, m->lm_b, e));
+      TRY(gemm_f32(head_in, d, m->lm_w, d, m->lm_b, e, TH));
     }
   }
   sec.end();
   sec.begin("lm_ln");
-  LAUNCH(m, launch_layernorm(attn, m->lm_ln_w, m->lm_ln_b, c.layer_norm_eps, q, T, d, nullptr,
+  LAUNCH(m, launch_layernorm(attn, m->lm_ln_w, m->lm_ln_b, c.layer_norm_eps, q, TH, d, nullptr,
                              nullptr, 0, nullptr, s));
   sec.end();
   sec.begin("lm_decoder");
@@ -565,7 +580,7 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
     e.C = logits;
     e.ldc = c.vocab_size;
     if (d % 4 == 0) {  // 3xTF32, the lo part of `q` into `v`
-      LAUNCH(m, launch_tf32_lo(q, v, static_cast<long>(T) * d, s));
+      LAUNCH(m, launch_tf32_lo(q, v, static_cast<long>(TH) * d, s));
       GemmTf32Args g;
       g.A = q;
       g.A_lo = v;
@@ -573,7 +588,7 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
       g.W = m->embed;
       g.W_lo = m->embed_lo;
       g.ldw = d;
-      g.M = T;
+      g.M = TH;
       g.N = c.vocab_size;
       g.K = d;
       g.bias = m->lm_bias;
@@ -582,10 +597,11 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
       g.num_sms = ctx->num_sms;
       LAUNCH(m, launch_gemm_tf32x3(g, s));
     } else {
-      TRY(gemm_f32(q, d, m->embed, c.vocab_size, m->lm_bias, e));
+      TRY(gemm_f32(q, d, m->embed, c.vocab_size, m->lm_bias, e, TH));
     }
   }
   sec.end();
+  if (rows) LAUNCH(m, launch_log_softmax_rows(logits, R, c.vocab_size, s));
   for (auto& e : sec.ev) m->pending.push_back(std::move(e));
   return ESMCU_OK;
 }
@@ -676,19 +692,21 @@ int forward_packed_host(esmcu_model* m, const int32_t* ids, const int32_t* masks
 // logits come back into its own pinned region; one synchronisation at the
 // end, then the logits are scattered into caller order.  The host packing of
 // group g+1 and the scatter no longer sit between the GPU's groups.
+// score_rows (host, nullable): one row per sequence; the output is then
+// [n, V], the log-softmax of sequence i's logits at row score_rows[i].
 int run_groups(esmcu_model* m, const std::vector<std::vector<int>>& groups, const int32_t* ids_concat,
                const std::vector<long>& offsets, const int32_t* lens, const int32_t* masks_concat,
-               float* logits) {
+               float* logits, const int32_t* score_rows = nullptr) {
   if (m == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "null model");
   TRY(use_device(m->ctx));
   if (!model_ready(m)) return fail(ESMCU_ERR_INVALID_ARGUMENT, "model weights are not fully set");
   const size_t V = static_cast<size_t>(m->cfg.vocab_size);
   struct Packed {
     const std::vector<int>* group;
-    std::vector<int32_t> ids, masks, cu;
+    std::vector<int32_t> ids, masks, cu, rows;
     int T = 0, B = 0, max_len = 0;
     Arena a{};
-    size_t off_ids = 0, off_masks = 0, off_cu = 0, off_logits = 0;
+    size_t off_ids = 0, off_masks = 0, off_cu = 0, off_rows = 0, off_logits = 0;
   };
   std::vector<Packed> ps;
   size_t arena_need = 0, pin = 0;
@@ -710,6 +728,16 @@ int run_groups(esmcu_model* m, const std::vector<std::vector<int>>& groups, cons
     }
     p.T = p.cu.back();
     p.B = static_cast<int>(g.size());
+    if (score_rows) {
+      for (size_t gi = 0; gi < g.size(); ++gi) {
+        const int idx = g[gi];
+        if (score_rows[idx] < 0 || score_rows[idx] >= lens[idx])
+          return fail(ESMCU_ERR_OUT_OF_RANGE, "row " + std::to_string(score_rows[idx]) +
+                                                  " of sequence " + std::to_string(idx) + " (length " +
+                                                  std::to_string(lens[idx]) + ")");
+        p.rows.push_back(p.cu[gi] + score_rows[idx]);
+      }
+    }
     if (p.T == 0) continue;
     std::string msg = ValidateBatchView(p.T, masks_concat ? p.T : 0, p.cu.data(), p.B + 1, p.B);
     if (!msg.empty()) return fail(ESMCU_ERR_INVALID_ARGUMENT, msg);
@@ -732,8 +760,10 @@ int run_groups(esmcu_model* m, const std::vector<std::vector<int>>& groups, cons
     if (masks_concat) pin += align_up(n_ids, 256);
     p.off_cu = pin;
     pin += align_up(static_cast<size_t>(p.B + 1) * 4, 256);
+    p.off_rows = pin;
+    if (score_rows) pin += align_up(static_cast<size_t>(p.B) * 4, 256);
     p.off_logits = pin;
-    pin += align_up(static_cast<size_t>(p.T) * V * 4, 256);
+    pin += align_up(static_cast<size_t>(score_rows ? p.B : p.T) * V * 4, 256);
     ps.push_back(std::move(p));
   }
   if (ps.empty()) return ESMCU_OK;
@@ -753,11 +783,19 @@ int run_groups(esmcu_model* m, const std::vector<std::vector<int>>& groups, cons
     if (masks_concat)
       ESMCU_CUDA(cudaMemcpyAsync(base + p.a.masks, hp + p.off_masks, n_ids, cudaMemcpyHostToDevice, s));
     ESMCU_CUDA(cudaMemcpyAsync(base + p.a.cu, hp + p.off_cu, n_cu, cudaMemcpyHostToDevice, s));
+    const int* d_rows = nullptr;
+    if (score_rows) {
+      const size_t n_rows = static_cast<size_t>(p.B) * 4;
+      std::memcpy(hp + p.off_rows, p.rows.data(), n_rows);
+      ESMCU_CUDA(cudaMemcpyAsync(base + p.a.rows, hp + p.off_rows, n_rows, cudaMemcpyHostToDevice, s));
+      d_rows = reinterpret_cast<const int*>(base + p.a.rows);
+    }
     float* d_logits = reinterpret_cast<float*>(base + p.a.logits);
     TRY(forward_device(m, p.a, reinterpret_cast<const int*>(base + p.a.ids),
                        masks_concat ? reinterpret_cast<const int*>(base + p.a.masks) : nullptr,
-                       d_logits, p.T, p.B, p.max_len, 0.0f, nullptr));
-    ESMCU_CUDA(cudaMemcpyAsync(hp + p.off_logits, d_logits, static_cast<size_t>(p.T) * V * 4,
+                       d_logits, p.T, p.B, p.max_len, 0.0f, nullptr, nullptr, d_rows, p.B));
+    ESMCU_CUDA(cudaMemcpyAsync(hp + p.off_logits, d_logits,
+                               static_cast<size_t>(score_rows ? p.B : p.T) * V * 4,
                                cudaMemcpyDeviceToHost, s));
   }
   ESMCU_CUDA(cudaStreamSynchronize(s));
@@ -765,8 +803,12 @@ int run_groups(esmcu_model* m, const std::vector<std::vector<int>>& groups, cons
     const float* src = reinterpret_cast<const float*>(hp + p.off_logits);
     for (size_t gi = 0; gi < p.group->size(); ++gi) {
       const int idx = (*p.group)[gi];
-      std::memcpy(logits + offsets[static_cast<size_t>(idx)] * static_cast<long>(V),
-                  src + static_cast<size_t>(p.cu[gi]) * V, static_cast<size_t>(lens[idx]) * V * sizeof(float));
+      if (score_rows)
+        std::memcpy(logits + static_cast<size_t>(idx) * V, src + gi * V, V * sizeof(float));
+      else
+        std::memcpy(logits + offsets[static_cast<size_t>(idx)] * static_cast<long>(V),
+                    src + static_cast<size_t>(p.cu[gi]) * V,
+                    static_cast<size_t>(lens[idx]) * V * sizeof(float));
     }
   }
   if (m->profiling) collect_profile(m, true);
@@ -985,6 +1027,20 @@ int esmcu_model_forward_scheduled(esmcu_model* m, const int32_t* ids_concat, con
   for (int i = 0; i < n; ++i) offsets[static_cast<size_t>(i) + 1] = offsets[static_cast<size_t>(i)] + lens[i];
   auto plan = PlanBatches(lengths, threshold, max_batch);
   return run_groups(m, plan, ids_concat, offsets, lens, masks_concat, logits);
+}
+
+int esmcu_model_masked_marginals(esmcu_model* m, const int32_t* ids_concat, const int32_t* lens,
+                                 const int32_t* masks_concat, const int32_t* rows, int n,
+                                 float threshold, int max_batch, float* log_probs) {
+  if (m == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "null model");
+  TRY(check_sched_args(ids_concat, lens, n, log_probs));
+  if (n == 0) return ESMCU_OK;
+  if (rows == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "rows is null");
+  std::vector<int> lengths(lens, lens + n);
+  std::vector<long> offsets(static_cast<size_t>(n) + 1, 0);
+  for (int i = 0; i < n; ++i) offsets[static_cast<size_t>(i) + 1] = offsets[static_cast<size_t>(i)] + lens[i];
+  auto plan = PlanBatches(lengths, threshold, max_batch);
+  return run_groups(m, plan, ids_concat, offsets, lens, masks_concat, log_probs, rows);
 }
 
 int esmcu_forward_scheduled_multi(esmcu_model** models, int n_models, const int32_t* ids_concat,

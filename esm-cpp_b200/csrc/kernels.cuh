@@ -158,6 +158,11 @@ cudaError_t launch_split_qkv_rope(const float* qkv, float* q, float* k, float* v
                                   const float* sin_t, float q_scale, cudaStream_t s);
 // Token -> position inside its sequence, from cu_seqlens.
 cudaError_t launch_positions(const int* cu, int B, int* pos, cudaStream_t s);
+// out [R, d] = x[rows[r]] (rows must index rows of x).
+cudaError_t launch_gather_rows(const float* x, const int* rows, int R, int d, float* out,
+                               cudaStream_t s);
+// In-place log-softmax of each row of x [R, V].
+cudaError_t launch_log_softmax_rows(float* x, int R, int V, cudaStream_t s);
 // model.cpp:737-778 Embed.
 cudaError_t launch_embed(const float* embed_w, int d, const int* ids, const int* masks,
                          const int* cu, int B, int mask_id, float* out, cudaStream_t s);

@@ -100,6 +100,8 @@ _SIGS = {
                                                 _VP]),
     "esmcu_model_forward_packed_device": (C.c_int, [_VP, _VP, _VP, C.c_int, _VP, C.c_int, _VP]),
     "esmcu_model_forward_hidden_states": (C.c_int, [_VP, _VP, _VP, C.c_int, _VP, C.c_int, _VP, _VP]),
+    "esmcu_model_masked_marginals": (C.c_int, [_VP, _VP, _VP, _VP, _VP, C.c_int, C.c_float, C.c_int,
+                                               _VP]),
     "esmcu_forward_scheduled_multi": (C.c_int, [_VP, C.c_int, _VP, _VP, _VP, C.c_int, C.c_float,
                                                 C.c_int, _VP]),
     "esmcu_model_observe_packed": (C.c_int, [_VP, _VP, C.c_int, _VP, C.c_int, C.c_float, _VP]),

@@ -416,19 +416,16 @@ class Model:
             ids, np.array([0, ids.shape[0]], np.int32), attention_mask)
         return logits, [hidden[i] for i in range(hidden.shape[0])]
 
-    def forward_scheduled(self, input_ids, attention_masks=None, imbalance_threshold: float = 1.2,
-                          max_batch_size: int = 256):
-        """Model::ForwardScheduled: logits in input order."""
-        self._ensure_device()
+    @staticmethod
+    def _concat_sequences(input_ids, attention_masks):
+        """(lens [n], ids_concat, masks_concat or None) of a list of sequences."""
         seqs = [np.ascontiguousarray(a, np.int32) for a in input_ids]
         for a in seqs:
             if a.ndim != 1:
                 raise ValueError("each input_ids entry must be a 1-D int32 array")
         n = len(seqs)
-        if n == 0:
-            return []
         lens = np.array([a.shape[0] for a in seqs], np.int32)
-        ids = np.concatenate(seqs) if lens.sum() else np.zeros(0, np.int32)
+        ids = np.concatenate(seqs) if n and lens.sum() else np.zeros(0, np.int32)
         masks = None
         if attention_masks is not None:
             if len(attention_masks) != n:
@@ -438,6 +435,16 @@ class Model:
                 if m.shape != a.shape:
                     raise ValueError("attention_mask[i] must be a 1-D int32 array of the same length as input_ids[i]")
             masks = np.concatenate(ms)
+        return lens, ids, masks
+
+    def forward_scheduled(self, input_ids, attention_masks=None, imbalance_threshold: float = 1.2,
+                          max_batch_size: int = 256):
+        """Model::ForwardScheduled: logits in input order."""
+        self._ensure_device()
+        lens, ids, masks = self._concat_sequences(input_ids, attention_masks)
+        n = lens.shape[0]
+        if n == 0:
+            return []
         V = self._cfg.vocab_size
         logits = np.empty((int(lens.sum()), V), F32)
         _lib.call("esmcu_model_forward_scheduled", self._dev, ids.ctypes.data, lens.ctypes.data,
@@ -445,6 +452,28 @@ class Model:
                   int(max_batch_size), logits.ctypes.data)
         off = np.concatenate([[0], np.cumsum(lens)])
         return [logits[off[i]:off[i + 1]] for i in range(n)]
+
+    def masked_marginals(self, input_ids, rows, attention_masks=None,
+                         imbalance_threshold: float = 1.2, max_batch_size: int = 256):
+        """log_softmax(forward_scheduled(input_ids)[i][rows[i]]) for every i, as
+        one [n, V] array, without the full logits: the LM head runs on the n
+        scored rows only and the log-softmax on the device
+        (esmcu_model_masked_marginals; eval/proteingym.py:84-98 takes these
+        rows of the masked copies' logits)."""
+        self._ensure_device()
+        lens, ids, masks = self._concat_sequences(input_ids, attention_masks)
+        n = lens.shape[0]
+        r = np.ascontiguousarray(rows, np.int32)
+        if r.shape != (n,):
+            raise ValueError("rows must hold one row index per sequence")
+        V = self._cfg.vocab_size
+        out = np.empty((n, V), F32)
+        if n == 0:
+            return out
+        _lib.call("esmcu_model_masked_marginals", self._dev, ids.ctypes.data, lens.ctypes.data,
+                  None if masks is None else masks.ctypes.data, r.ctypes.data, n,
+                  float(imbalance_threshold), int(max_batch_size), out.ctypes.data)
+        return out
 
     def _observe(self, seqs, pctile) -> dict:
         if self._cfg.weights_quantized:

@@ -211,6 +211,14 @@ int esmcu_model_forward_hidden_states(esmcu_model* m, const int32_t* ids, const 
 int esmcu_model_forward_scheduled(esmcu_model* m, const int32_t* ids_concat,
                                   const int32_t* lens, const int32_t* masks_concat, int n,
                                   float imbalance_threshold, int max_batch_size, float* logits);
+/* The masked-marginal head of score_assay (python/esm_cpp/eval/proteingym.py:
+ * 75-98): the scheduled forward of n sequences (as esmcu_model_forward_scheduled)
+ * with the LM head run only on row rows[i] of sequence i (0 <= rows[i] <
+ * lens[i], else ESMCU_ERR_OUT_OF_RANGE); log_probs [n, V] receives the
+ * log-softmax of those rows, (x - max) - log(sum(exp(x - max))). */
+int esmcu_model_masked_marginals(esmcu_model* m, const int32_t* ids_concat, const int32_t* lens,
+                                 const int32_t* masks_concat, const int32_t* rows, int n,
+                                 float imbalance_threshold, int max_batch_size, float* log_probs);
 /* The same forward on device buffers, asynchronous on the context stream:
  * d_ids [T] (and d_masks [T] or NULL) already on the device, host cu_seqlens
  * [B+1] (validated on the host), d_logits [T, V] on the device.  Call

@@ -328,6 +328,36 @@ def forward_packed(model, ids, cu, masks=None, per_token: bool = False, hidden=N
     return linear_f32(lm, model.embed, hd["lm_bias"])
 
 
+def forward_scheduled(model, seqs, threshold=1.2, max_batch=256, per_token: bool = False):
+    """Model::ForwardScheduled (model.cpp:1298-1421): PlanBatches groups,
+    each packed and run through forward_packed; logits per sequence in
+    caller order.  (The W8A8 per-tensor activation scale is an absmax over
+    a group's rows, so the grouping is part of the result.)"""
+    out = [None] * len(seqs)
+    for g in plan_batches([len(s) for s in seqs], threshold, max_batch):
+        ids = np.concatenate([_a(seqs[i], np.int32) for i in g])
+        cu = np.concatenate([[0], np.cumsum([len(seqs[i]) for i in g])]).astype(np.int32)
+        lg = forward_packed(model, ids, cu, per_token=per_token)
+        for j, i in enumerate(g):
+            out[i] = lg[cu[j]:cu[j + 1]]
+    return out
+
+
+def log_softmax_at(row, token: int) -> float:
+    """eval/proteingym.py:48-50, numpy float32 as there."""
+    m = float(row.max())
+    return float(row[token] - m - np.log(np.exp(row - m).sum()))
+
+
+def masked_marginals(model, seqs, rows, threshold=1.2, max_batch=256):
+    """[n, V]: log-softmax of sequence i's logits at row rows[i], from the
+    scheduled forward (eval/proteingym.py:84-98)."""
+    lg = forward_scheduled(model, seqs, threshold, max_batch)
+    V = model.config.vocab_size
+    return np.array([[log_softmax_at(lg[i][r], t) for t in range(V)]
+                     for i, r in enumerate(rows)], F32)
+
+
 # ------------------------------------------------- the compiled reference
 class RefModel:
     """esm::Model from the reference compiled in oracle/_ref."""
