@@ -134,6 +134,10 @@ cudaError_t launch_attention_tma_pair(const float* q, const float* k, const floa
                                       const int* cu, int B, int H, long T, float* out,
                                       uint32_t* amax, uint32_t* status, int num_sms,
                                       cudaStream_t s);
+cudaError_t launch_attention_tma_long(const float* q, const float* k, const float* v,
+                                      const int* cu, int B, int H, long T, int max_len, float* out,
+                                      uint32_t* amax, uint32_t* status, int num_sms,
+                                      cudaStream_t s);
 
 cudaError_t launch_attention_varlen(const float* q, const float* k, const float* v,
                                     const int* cu, int B, int H, int dh, long T, int min_len,
@@ -141,9 +145,9 @@ cudaError_t launch_attention_varlen(const float* q, const float* k, const float*
                                     int num_sms, cudaStream_t s) {
   if (B <= 0 || H <= 0 || max_len <= 0) return cudaSuccess;
   if (dh <= 0 || dh > 128 || (dh & 3)) return cudaErrorInvalidValue;
-  // head_dim 64: tensor cores (3xTF32) up to 256 tokens -- one CTA per
-  // (sequence, head) for L <= 128, a CTA pair above; the rest: FP32 SIMT.
-  int simt_min = 0;
+  // head_dim 64: tensor cores (3xTF32) -- one CTA per (sequence, head) for
+  // L <= 128, a CTA pair for 129..256, one CTA per (sequence, head, 128-row
+  // query tile) above; other head dims: FP32 SIMT.
   if (dh == 64 && status != nullptr) {
     if (min_len <= 128) {
       cudaError_t e = launch_attention_tma(q, k, v, cu, B, H, T, out, amax, status, num_sms, s);
@@ -153,10 +157,14 @@ cudaError_t launch_attention_varlen(const float* q, const float* k, const float*
       cudaError_t e = launch_attention_tma_pair(q, k, v, cu, B, H, T, out, amax, status, num_sms, s);
       if (e != cudaSuccess) return e;
     }
-    if (max_len <= 256) return cudaSuccess;
-    simt_min = 256;
+    if (max_len > 256) {
+      cudaError_t e = launch_attention_tma_long(q, k, v, cu, B, H, T, max_len, out, amax, status,
+                                                num_sms, s);
+      if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
   }
-  const int min_len_simt = simt_min;
+  const int min_len_simt = 0;
   dim3 grid(H, B);
   if (dh <= 16) attention_varlen_kernel<16><<<grid, QT, 0, s>>>(q, k, v, cu, H, dh, out, amax, min_len_simt);
   else if (dh <= 32) attention_varlen_kernel<32><<<grid, QT, 0, s>>>(q, k, v, cu, H, dh, out, amax, min_len_simt);

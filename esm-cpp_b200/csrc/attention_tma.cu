@@ -913,6 +913,398 @@ __global__ void __maxnreg__(128)
   }
 }
 
+// ============================================================ long sequences
+// Sequences of more than 256 tokens: items = (sequence, head, 128-row query
+// tile), one CTA each on a persistent grid, keys in blocks of 128.  The
+// softmax keeps the exact form -- the row max over all keys first, then
+// exponentials, sum and P.V -- in two passes over the key blocks:
+//   pass 1  S_j = Q K_j^T (3xTF32) for the row max m;
+//   pass 2  the same S_j again (the same MMAs, so the same values), P =
+//           2^((S - m) log2 e) chunk by chunk into TMEM as in the short
+//           kernel, O += P V_j (3xTF32), row sums summed over the blocks.
+// O is never rescaled; the price is S computed twice.
+// Tiles flow through a ring of two 64 KB stages (raw | lo, the short
+// kernel's slot layout): the producer loads pass 1's K_j, then pass 2's
+// K_0, V_0, K_1, V_1, ...; the prep warps form each tile's lo part and zero
+// V rows past L.  Within pass 2, S_{j+1} is issued right behind P.V_j
+// (in-order MMAs, as across items in the short kernel); in pass 1 the
+// softmax warps release S explicitly.
+// TMEM: S [0,128) O [128,256) P_lo [256,384) Q_lo [384,448).
+constexpr uint32_t kLQ = 0, kLRing = 32768, kLStage = 65536;
+constexpr uint32_t kLRed = kLRing + 2 * kLStage;  // red_max [2][128] | red_sum [2][128]
+constexpr uint32_t kLBarOff = kLRed + 2048;
+constexpr int kLSmemBytes = static_cast<int>(kLBarOff) + 256 + 1024;
+enum : int {
+  kLFull = 0,    // [2] TMA tile landed in stage s
+  kLReady = 2,   // [2] prep done with stage s (4 prep warps)
+  kLFree = 4,    // [2] MMAs done with stage s
+  kLQFull = 6,   // TMA Q landed
+  kLQReady = 7,  // Q_lo in TMEM (4 prep warps)
+  kLQFree = 8,   // the item's last S done: Q and Q_lo free
+  kLSDone = 9,   // an S is in TMEM
+  kLSFree = 10,  // pass 1: S read (8 softmax warps)
+  kLODone = 11,  // the item's P.V done
+  kLChunk = 12,  // [4] P chunk c written (4 softmax warps)
+  kLNumBars = 16
+};
+
+struct LItem {
+  int h, s0, L, q0;
+};
+
+// Item it = (b * H + h) * qtiles + qt; valid when L > 256 and q0 < L.
+__device__ __forceinline__ bool decode_long(int it, int H, int qtiles, const int* __restrict__ cu,
+                                            LItem& w) {
+  const int per_seq = H * qtiles;
+  const int b = it / per_seq;
+  const int r = it - b * per_seq;
+  w.h = r / qtiles;
+  w.q0 = (r - w.h * qtiles) * QB;
+  w.s0 = __ldg(cu + b);
+  w.L = __ldg(cu + b + 1) - w.s0;
+  return w.L > LMAX2 && w.q0 < w.L;
+}
+
+__device__ __forceinline__ int next_long(int it, int stride, int n_items, int H, int qtiles,
+                                         const int* __restrict__ cu, LItem& w) {
+  for (; it < n_items; it += stride)
+    if (decode_long(it, H, qtiles, cu, w)) return it;
+  return n_items;
+}
+
+__global__ void __maxnreg__(128)
+    attention_tma_long_kernel(const __grid_constant__ CUtensorMap tmQ,
+                              const __grid_constant__ CUtensorMap tmK,
+                              const __grid_constant__ CUtensorMap tmV, const int* __restrict__ cu,
+                              int H, int qtiles, int n_items, float* __restrict__ out,
+                              uint32_t* amax, uint32_t* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kLBarOff);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + kLNumBars);
+  volatile uint32_t* abort_flag = tslot + 1;
+
+  const int stride = gridDim.x;
+  LItem first;
+  const int it0 = next_long(blockIdx.x, stride, n_items, H, qtiles, cu, first);
+  if (it0 >= n_items) return;  // CTA-uniform, before any barrier
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const long rs = static_cast<long>(H) * DH;  // token row stride (floats)
+
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar[kLFull + i], 1);
+      mbar_init(&bar[kLReady + i], 4);
+      mbar_init(&bar[kLFree + i], 1);
+    }
+    mbar_init(&bar[kLQFull], 1);
+    mbar_init(&bar[kLQReady], 4);
+    mbar_init(&bar[kLQFree], 1);
+    mbar_init(&bar[kLSDone], 1);
+    mbar_init(&bar[kLSFree], 8);
+    mbar_init(&bar[kLODone], 1);
+    for (int c = 0; c < 4; ++c) mbar_init(&bar[kLChunk + c], 4);
+    *abort_flag = 0u;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tslot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  bool ok = true;
+  float mx_out = 0.0f;
+  LItem cur = first;
+  int it = it0;
+  int n = 0;       // this CTA's item counter
+  uint32_t t = 0;  // ring tile counter (producer, prep and MMA count alike)
+
+  if (warp == 0) {
+    // ================================================== TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmV);
+      while (ok) {
+        const int nkb = (cur.L + QB - 1) / QB;
+        if (n >= 1 && !(ok = mbar_wait_abort(&bar[kLQFree], (n - 1) & 1, status, abort_flag))) break;
+        mbar_arrive_expect_tx(&bar[kLQFull], 2 * 16384);
+        for (int blk = 0; blk < 2; ++blk)
+          tma_load_2d(smem + kLQ + blk * 16384, &tmQ, &bar[kLQFull], cur.h * DH + 32 * blk,
+                      cur.s0 + cur.q0);
+        for (int i = 0; i < 3 * nkb; ++i, ++t) {
+          const int s = static_cast<int>(t & 1);
+          if (t >= 2 && !(ok = mbar_wait_abort(&bar[kLFree + s], ((t >> 1) + 1) & 1, status, abort_flag)))
+            break;
+          // Tiles 0..nkb-1: pass 1's K_j; then K_j, V_j alternately.
+          const bool is_v = i >= nkb && ((i - nkb) & 1);
+          const int j = i < nkb ? i : (i - nkb) >> 1;
+          uint8_t* st = smem + kLRing + s * kLStage;
+          mbar_arrive_expect_tx(&bar[kLFull + s], 2 * 16384);
+          for (int blk = 0; blk < 2; ++blk)
+            tma_load_2d(st + blk * 16384, is_v ? &tmV : &tmK, &bar[kLFull + s], cur.h * DH + 32 * blk,
+                        cur.s0 + QB * j);
+        }
+        if (!ok) break;
+        LItem nxt;
+        const int itn = next_long(it + stride, stride, n_items, H, qtiles, cu, nxt);
+        if (itn >= n_items) break;
+        it = itn;
+        cur = nxt;
+        ++n;
+      }
+    }
+  } else if (warp == 1) {
+    // ==================================================== MMA issuer
+    if (lane == 0) {
+      uint32_t cpar = 0;    // bit c: parity of the next completion of chunk barrier c
+      uint32_t sfree = 0;   // completions of kLSFree consumed
+      const uint32_t idS = idesc_tf32(QB, QB);
+      const uint32_t idO = idesc_tf32_bmn(QB, DH);
+      const uint32_t idO2 = idesc_tf32_bmn(QB, 2 * DH);
+      const uint32_t q_s = smem_u32(smem + kLQ);
+      const uint32_t tS = tmem;
+      while (ok) {
+        const int L = cur.L, nkb = (L + QB - 1) / QB;
+        if (!(ok = mbar_wait_abort(&bar[kLQReady], n & 1, status, abort_flag))) break;
+        // S = Q_raw K_raw^T + Q_raw K_lo^T + Q_lo K_raw^T for the K tile in
+        // ring stage st, identical in both passes.
+        auto issue_s = [&](uint32_t st) {
+#pragma unroll
+          for (int kk = 0; kk < DH / 8; ++kk) {
+            const uint32_t o = static_cast<uint32_t>((kk >> 2) * 16384 + (kk & 3) * 32);
+            const uint64_t a_raw = sw128_kmajor_desc(q_s + o);
+            mma_tf32(tS, a_raw, sw128_kmajor_desc(st + o), idS, kk > 0 ? 1u : 0u);
+            mma_tf32(tS, a_raw, sw128_kmajor_desc(st + 32768u + o), idS, 1u);
+            mma_tf32_ts(tS, tmem + kSColQlo + 8u * kk, sw128_kmajor_desc(st + o), idS, 1u);
+          }
+        };
+        // ---- pass 1: S_j for the row max
+        for (int j = 0; j < nkb && ok; ++j, ++t) {
+          const int s = static_cast<int>(t & 1);
+          if (!(ok = mbar_wait_abort(&bar[kLReady + s], (t >> 1) & 1, status, abort_flag))) break;
+          if (j > 0 && !(ok = mbar_wait_abort(&bar[kLSFree], sfree++ & 1, status, abort_flag))) break;
+          tc_fence_after();
+          issue_s(smem_u32(smem + kLRing + s * kLStage));
+          mma_commit(&bar[kLSDone]);
+          mma_commit(&bar[kLFree + s]);
+        }
+        if (!ok) break;
+        // ---- pass 2: S_j again, then O += P_j V_j chunk by chunk
+        for (int j = 0; j < nkb && ok; ++j) {
+          {
+            const int s = static_cast<int>(t & 1);
+            if (!(ok = mbar_wait_abort(&bar[kLReady + s], (t >> 1) & 1, status, abort_flag))) break;
+            if (j == 0 && !(ok = mbar_wait_abort(&bar[kLSFree], sfree++ & 1, status, abort_flag))) break;
+            tc_fence_after();
+            issue_s(smem_u32(smem + kLRing + s * kLStage));
+            mma_commit(&bar[kLSDone]);
+            mma_commit(&bar[kLFree + s]);
+            if (j == nkb - 1) mma_commit(&bar[kLQFree]);
+            ++t;
+          }
+          {
+            const int s = static_cast<int>(t & 1);
+            if (!(ok = mbar_wait_abort(&bar[kLReady + s], (t >> 1) & 1, status, abort_flag))) break;
+            const uint32_t st = smem_u32(smem + kLRing + s * kLStage);
+            const int nchunk = min(QB / KC, (L - QB * j + KC - 1) / KC);
+            for (int c = 0; c < nchunk; ++c) {
+              if (!(ok = mbar_wait_abort(&bar[kLChunk + c], (cpar >> c) & 1u, status, abort_flag))) break;
+              cpar ^= 1u << c;
+              tc_fence_after();
+              // P_hi [V | V_lo] as one N = 128 MMA, then P_lo V at N = 64.
+#pragma unroll
+              for (int kk = 0; kk < KC / 8; ++kk) {
+                const uint32_t vo = static_cast<uint32_t>(c * 4096 + kk * 1024);
+                const uint64_t v_all = sw128b32_mnmajor_desc(st + vo, 16384);
+                mma_tf32_ts(tmem + kSColO, tS + 32u * c + 8u * kk, v_all, idO2,
+                            (j | c | kk) != 0 ? 1u : 0u);
+                mma_tf32_ts(tmem + kSColO, tmem + kSColPlo + 32u * c + 8u * kk, v_all, idO, 1u);
+              }
+            }
+            if (!ok) break;
+            mma_commit(&bar[kLFree + s]);
+            ++t;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&bar[kLODone]);
+        LItem nxt;
+        const int itn = next_long(it + stride, stride, n_items, H, qtiles, cu, nxt);
+        if (itn >= n_items) break;
+        it = itn;
+        cur = nxt;
+        ++n;
+      }
+    }
+  } else if (warp < kSoftWarp0) {
+    // ================================================== prep warps
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const int ptid = (warp - kPrepWarp0) * 32 + lane;  // 0..127
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    while (ok) {
+      const int L = cur.L, nkb = (L + QB - 1) / QB;
+      // Q_lo of this thread's row into TMEM once the previous item's last S
+      // has read the previous Q_lo.
+      if (!(ok = mbar_wait_abort(&bar[kLQFull], n & 1, status, abort_flag))) break;
+      if (n >= 1 && !(ok = mbar_wait_abort(&bar[kLQFree], (n - 1) & 1, status, abort_flag))) break;
+      tc_fence_after();
+#pragma unroll
+      for (int blk = 0; blk < 2; ++blk) {
+        uint32_t lo[32];
+#pragma unroll
+        for (int c4 = 0; c4 < 8; ++c4) {
+          const float4 x = lds128(smem_u32(smem + kLQ + blk * 16384 + row * 128) +
+                                  static_cast<uint32_t>((c4 ^ (row & 7)) << 4));
+          const float4 l = tf32_lo4(x);
+          lo[4 * c4] = __float_as_uint(l.x);
+          lo[4 * c4 + 1] = __float_as_uint(l.y);
+          lo[4 * c4 + 2] = __float_as_uint(l.z);
+          lo[4 * c4 + 3] = __float_as_uint(l.w);
+        }
+        tmem_st32(tmem + kSColQlo + 32u * blk + lane_off, lo);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[kLQReady]);
+      for (int i = 0; i < 3 * nkb; ++i, ++t) {
+        const int s = static_cast<int>(t & 1);
+        if (!(ok = mbar_wait_abort(&bar[kLFull + s], (t >> 1) & 1, status, abort_flag))) break;
+        const uint32_t raw = smem_u32(smem + kLRing + s * kLStage), lo = raw + 32768u;
+        {
+          if (i < nkb || ((i - nkb) & 1) == 0) {
+            tile_lo_32k(raw, lo, ptid);  // K_j (either pass)
+          } else {
+            // V_j: lo, with keys (rows) past L zeroed in both parts.
+            const int kvalid = L - QB * ((i - nkb) >> 1);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              float4 x[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e)
+                x[e] = lds128(raw + static_cast<uint32_t>((ptid + (h * 8 + e) * 128) * 16));
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const uint32_t o = static_cast<uint32_t>((ptid + (h * 8 + e) * 128) * 16);
+                if (static_cast<int>((o & 16383u) >> 7) >= kvalid) {
+                  x[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+                  sts128(raw + o, x[e]);
+                }
+                sts128(lo + o, tf32_lo4(x[e]));
+              }
+            }
+          }
+          fence_proxy_async_smem();
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar[kLReady + s]);
+      }
+      if (!ok) break;
+      LItem nxt;
+      const int itn = next_long(it + stride, stride, n_items, H, qtiles, cu, nxt);
+      if (itn >= n_items) break;
+      it = itn;
+      cur = nxt;
+      ++n;
+    }
+  } else {
+    // ================================================ softmax warps
+    // Named barriers are reached by all eight warps at the same points of
+    // every item; a failed wait only ends an inner loop, and the AND-votes
+    // end the item loop for all of them together.
+    const int sw = warp - kSoftWarp0;  // 0..7
+    const int quad = warp & 3, par = sw >> 2;
+    const int row = quad * 32 + lane;  // query row within the tile = TMEM lane
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const uint32_t tS = tmem + lane_off;
+    float (*red_max)[QB] = reinterpret_cast<float (*)[QB]>(smem + kLRed);
+    float (*red_sum)[QB] = reinterpret_cast<float (*)[QB]>(smem + kLRed + 1024);
+    uint32_t sd = 0;  // completions of kLSDone consumed
+    bool good = ok;
+    while (true) {
+      const int L = cur.L, nkb = (L + QB - 1) / QB;
+      // ---- pass 1: the row's stabiliser over all keys
+      float mx = -INFINITY;
+      for (int j = 0; j < nkb && good; ++j) {
+        if (!(good = mbar_wait_abort(&bar[kLSDone], sd++ & 1, status, abort_flag))) break;
+        tc_fence_after();
+        const int kv = L - QB * j;
+        mx = fmaxf(mx, s_row_max(tS, par, min(QB / KC, (kv + KC - 1) / KC), kv));
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar[kLSFree]);
+      }
+      red_max[par][row] = mx;
+      if (!soft_all(good)) break;
+      mx = fmaxf(red_max[0][row], red_max[1][row]);
+      // ---- pass 2: P chunks (P_hi over S, P_lo into its slot), row sums
+      float sum = 0.0f;
+      for (int j = 0; j < nkb && good; ++j) {
+        if (!(good = mbar_wait_abort(&bar[kLSDone], sd++ & 1, status, abort_flag))) break;
+        tc_fence_after();
+        const int kv = L - QB * j;
+        sum = __fadd_rn(sum, p_chunks(tS, tmem + kSColPlo + lane_off, 3u, par,
+                                      min(QB / KC, (kv + KC - 1) / KC), kv, mx, [](int) {},
+                                      [&](int c) {
+                                        if (lane == 0) mbar_arrive(&bar[kLChunk + c]);
+                                      }));
+      }
+      red_sum[par][row] = sum;
+      if (!soft_all(good)) break;
+      const float total = __fadd_rn(red_sum[0][row], red_sum[1][row]);
+      // ---- O / sum straight to the output rows of this tile
+      good = mbar_wait_abort(&bar[kLODone], n & 1, status, abort_flag);
+      if (good) {
+        tc_fence_after();
+        uint32_t o[32], ob[32];
+        tmem_ld32(tmem + kSColO + lane_off + 32u * par, o);
+        tmem_ld32(tmem + kSColO + 64u + lane_off + 32u * par, ob);
+        tmem_ld_wait();
+        tc_fence_before();
+        const float inv = __fdiv_rn(1.0f, total);
+        if (cur.q0 + row < L) {
+          float* orow = out + static_cast<long>(cur.s0 + cur.q0 + row) * rs + cur.h * DH + 32 * par;
+#pragma unroll
+          for (int jj = 0; jj < 32; jj += 4) {
+            float4 a;
+            a.x = __fmul_rn(__fadd_rn(__uint_as_float(o[jj]), __uint_as_float(ob[jj])), inv);
+            a.y = __fmul_rn(__fadd_rn(__uint_as_float(o[jj + 1]), __uint_as_float(ob[jj + 1])), inv);
+            a.z = __fmul_rn(__fadd_rn(__uint_as_float(o[jj + 2]), __uint_as_float(ob[jj + 2])), inv);
+            a.w = __fmul_rn(__fadd_rn(__uint_as_float(o[jj + 3]), __uint_as_float(ob[jj + 3])), inv);
+            *reinterpret_cast<float4*>(orow + jj) = a;
+            mx_out = fmaxf(mx_out, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
+          }
+        }
+      }
+      LItem nxt;
+      const int itn = next_long(it + stride, stride, n_items, H, qtiles, cu, nxt);
+      if (itn >= n_items) break;
+      it = itn;
+      cur = nxt;
+      ++n;
+    }
+    ok = good;
+  }
+
+  __syncwarp();
+  const bool all_ok = __syncthreads_and(ok ? 1 : 0) != 0;
+  if (all_ok && amax != nullptr) amax_publish(amax, mx_out);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (fn == nullptr) {
@@ -1014,6 +1406,39 @@ cudaError_t launch_attention_tma_pair(const float* q, const float* k, const floa
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, attention_tma_pair_kernel, tmQ, tmK, tmV, cu, H,
                             static_cast<int>(n_items), out, amax, status);
+}
+
+// Every sequence of more than 256 tokens: items = (sequence, head, 128-row
+// query tile), qtiles = ceil(max_len / 128) tiles reserved per (sequence,
+// head); one persistent CTA per SM at most.
+cudaError_t launch_attention_tma_long(const float* q, const float* k, const float* v,
+                                      const int* cu, int B, int H, long T, int max_len, float* out,
+                                      uint32_t* amax, uint32_t* status, int num_sms,
+                                      cudaStream_t s) {
+  if (B <= 0 || H <= 0 || T <= 0 || max_len <= LMAX2) return cudaSuccess;
+  CUtensorMap tmQ, tmK, tmV;
+  const long cols = static_cast<long>(H) * DH;
+  if (!make_tmap_rows(&tmQ, q, T, cols, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tmap_rows(&tmK, k, T, cols, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tmap_rows(&tmV, v, T, cols, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
+    return cudaErrorInvalidValue;
+  static std::atomic<uint64_t> attr_set{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if ((attr_set.load() & bit) == 0) {
+    cudaError_t e = cudaFuncSetAttribute(attention_tma_long_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kLSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_set.fetch_or(bit);
+  }
+  const int qtiles = (max_len + QB - 1) / QB;
+  const long n_items = static_cast<long>(B) * H * qtiles;
+  if (n_items > (1L << 30)) return cudaErrorInvalidValue;
+  const int grid = static_cast<int>(std::min<long>(n_items, std::max(1, num_sms)));
+  attention_tma_long_kernel<<<grid, kThreads, kLSmemBytes, s>>>(
+      tmQ, tmK, tmV, cu, H, qtiles, static_cast<int>(n_items), out, amax, status);
+  return cudaGetLastError();
 }
 
 }  // namespace esmb200

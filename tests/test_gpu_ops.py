@@ -106,8 +106,12 @@ def test_rope_varlen_positions_restart(cuda, O):
             assert np.array_equal(tx.cpu().numpy()[cu[b]], x[cu[b]])
 
 
+# head_dim 64 runs three tensor-core kernels by length: <= 128, 129..256 and
+# > 256 (128-row query tiles, keys in 128-key blocks; the last block ragged).
 @pytest.mark.parametrize("lens,H,dh", [([1], 1, 16), ([7, 13, 1], 2, 16), ([33, 250, 90], 20, 64),
-                                       ([129, 300], 4, 64), ([1024], 2, 64), ([17, 5], 3, 32)])
+                                       ([129, 300], 4, 64), ([1024], 2, 64), ([17, 5], 3, 32),
+                                       ([402, 3, 257, 130, 513], 20, 64), ([700, 1000, 260], 3, 64),
+                                       ([1500, 384, 385], 2, 64)])
 def test_attention_varlen_matches_oracle(cuda, O, lens, H, dh):
     from esm_b200 import ops
 
@@ -156,18 +160,41 @@ def test_attention_isolation_poisoned_kv(cuda):
     assert np.array_equal(a.cpu().numpy()[:40], b.cpu().numpy()[:40])
 
 
-def test_attention_large_scores_finite(cuda):
+def test_attention_isolation_long_sequences(cuda):
+    """The same property across the > 256 kernel's ragged last key block and
+    query tile: sequence 1 (300 tokens) shares its last 128-row tiles with
+    sequence 2, whose K/V are poisoned."""
     from esm_b200 import ops
 
-    cu = np.array([0, 64], np.int32)
-    q = np.full((64, 1, 64), 30.0, np.float32)
-    k = np.full((64, 1, 64), 30.0, np.float32)
-    v = np.random.default_rng(0).standard_normal((64, 1, 64)).astype(np.float32)
+    rng = np.random.default_rng(6)
+    cu = np.array([0, 300, 700], np.int32)
+    H, dh = 2, 64
+    q, k, v = (rng.standard_normal((3, 700, H, dh)).astype(np.float32))
+    a = ops.attention_varlen(_t(q, cuda), _t(k, cuda), _t(v, cuda), _t(cu, cuda), H, dh)
+    k2, v2 = k.copy(), v.copy()
+    k2[300:] = 1e4
+    v2[300:] = -1e4
+    b = ops.attention_varlen(_t(q, cuda), _t(k2, cuda), _t(v2, cuda), _t(cu, cuda), H, dh)
+    ops.synchronize()
+    assert np.array_equal(a.cpu().numpy()[:300], b.cpu().numpy()[:300])
+
+
+@pytest.mark.parametrize("L", [64, 600])
+def test_attention_large_scores_finite(cuda, L):
+    """Scores of 57600 (q = k = 30): the softmax's row max keeps every
+    exponential finite; uniform weights give the mean of V."""
+    from esm_b200 import ops
+
+    cu = np.array([0, L], np.int32)
+    q = np.full((L, 1, 64), 30.0, np.float32)
+    k = np.full((L, 1, 64), 30.0, np.float32)
+    v = np.random.default_rng(0).standard_normal((L, 1, 64)).astype(np.float32)
     out = ops.attention_varlen(_t(q, cuda), _t(k, cuda), _t(v, cuda), _t(cu, cuda), 1, 64)
     ops.synchronize()
     o = out.cpu().numpy()
     assert np.isfinite(o).all()
     np.testing.assert_allclose(o[0, 0], v.mean(axis=0)[0], rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(o[L - 1, 0], v.mean(axis=0)[0], rtol=1e-4, atol=1e-5)
 
 
 # K % 4 == 0 takes the 3xTF32 tensor-core path (BN = 128 tiles, or CTA pairs
