@@ -1,6 +1,6 @@
 """Small, self-checking cases of the hot kernels, sized for a profiler capture.
 
-    PYTHONPATH=esm-cpp_b200 python -m esm_b200.kernel_cases layer|gemm|ln|attn|all
+    PYTHONPATH=esm-cpp_b200 python -m esm_b200.kernel_cases layer|gemm|ln|attn|attn_long|attn_time|all
 
 Each case holds a few hundred MB on the device at most (inputs still larger
 than L2 where the kernel streams them) and launches its kernel a handful of
@@ -13,6 +13,10 @@ times, so `ncu -k regex:<kernel> -s <n> -c <k>` over it ends in a minute or two.
   ln     layernorm over 32768 x 1280
   attn   attention_varlen over 512 sequences of the bench length distribution
          (20 heads, head_dim 64)
+  attn_long  attention_varlen over 128 sequences of 402 tokens (the
+         deep-mutational-scan length; the > 256 kernel), 20 heads, head_dim 64
+  attn_time  CUDA-event timing of attention_varlen at equal-length shapes
+         (10 launches after 3 warm-ups each), one JSON line; not for ncu
 """
 from __future__ import annotations
 
@@ -78,6 +82,48 @@ def _attn(torch, dev):
     print("attn ok", T, float(o.abs().max()))
 
 
+def _attn_long(torch, dev):
+    lens = np.full(128, 402, np.int64)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), device=dev)
+    T, H, dh = int(cu[-1]), 20, 64
+    g = torch.Generator(device=dev).manual_seed(4)
+    q = torch.randn((T, H, dh), device=dev, generator=g) * 0.125
+    k = torch.randn((T, H, dh), device=dev, generator=g)
+    v = torch.randn((T, H, dh), device=dev, generator=g)
+    for _ in range(2):
+        o = ops.attention_varlen(q, k, v, cu, H, dh)
+    ops.synchronize()
+    assert bool(torch.isfinite(o).all())
+    print("attn_long ok", T, float(o.abs().max()))
+
+
+def _attn_time(torch, dev):
+    import json
+
+    res = {}
+    for nseq, L in ((512, 122), (256, 250), (400, 402), (128, 402), (256, 300), (64, 1000)):
+        cu = torch.tensor(np.arange(nseq + 1, dtype=np.int32) * L, device=dev)
+        T, H, dh = nseq * L, 20, 64
+        g = torch.Generator(device=dev).manual_seed(4)
+        q = torch.randn((T, H, dh), device=dev, generator=g) * 0.125
+        k = torch.randn((T, H, dh), device=dev, generator=g)
+        v = torch.randn((T, H, dh), device=dev, generator=g)
+        for _ in range(3):
+            ops.attention_varlen(q, k, v, cu, H, dh)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(10):
+            ops.attention_varlen(q, k, v, cu, H, dh)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / 10
+        res[f"{nseq}x{L}"] = {"ms": round(ms, 3),
+                              "tflops": round(nseq * H * L * L * dh * 4 / ms / 1e9, 1)}
+        del q, k, v
+    print(json.dumps(res))
+
+
 def main(argv=None) -> int:
     import torch
 
@@ -92,6 +138,10 @@ def main(argv=None) -> int:
         _ln(torch, dev)
     if which in ("attn", "all"):
         _attn(torch, dev)
+    if which in ("attn_long", "all"):
+        _attn_long(torch, dev)
+    if which == "attn_time":
+        _attn_time(torch, dev)
     return 0
 
 
