@@ -62,6 +62,10 @@ struct esmcu_model {
   float *lm_w = nullptr, *lm_b = nullptr, *lm_ln_w = nullptr, *lm_ln_b = nullptr,
         *lm_bias = nullptr;
   float* lm_w_lo = nullptr;   // lm_w - tf32(lm_w), for the 3xTF32 dense GEMM
+  // INT8 lm_head.dense (ESM_QUANTIZE_LM_HEAD, model.cpp:1209-1211), rows of
+  // stride ldk_d, with its per-channel scales; null = the FP32 head.
+  int8_t* lm_wq = nullptr;
+  float* lm_ws = nullptr;
   float* embed_lo = nullptr;  // the same for the tied decoder (embed^T)
   // Device staging of the hidden states for ForwardWithHiddenStates.
   float* hs_dev = nullptr;
@@ -341,13 +345,13 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
 
   // INT8 GEMM helper: A = quantised activations in q8 (row stride lda).
   auto gemm_i8 = [&](const int8_t* W, long ldk, int N, const float* ws, const float* bias,
-                     EpiParams epi) -> int {
+                     EpiParams epi, int M = -1) -> int {
     GemmI8Args g;
     g.A = q8;
     g.lda = ldk;
     g.W = W;
     g.ldw = ldk;
-    g.M = T;
+    g.M = M < 0 ? T : M;
     g.N = N;
     g.K = static_cast<int>(ldk);
     g.w_scale = ws;
@@ -376,9 +380,10 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
     return ESMCU_OK;
   };
   // Quantise an fp32 activation [T, K] into q8 with row stride ldk.
-  auto quantize = [&](const float* x, int K, long ldk, uint32_t* am) -> int {
-    if (per_token) LAUNCH(m, launch_quantize_per_token(x, K, T, K, q8, ldk, ascale, s));
-    else LAUNCH(m, launch_quantize_per_tensor(x, K, T, K, am, q8, ldk, ascale, s));
+  auto quantize = [&](const float* x, int K, long ldk, uint32_t* am, int M = -1) -> int {
+    const int rows_q = M < 0 ? T : M;
+    if (per_token) LAUNCH(m, launch_quantize_per_token(x, K, rows_q, K, q8, ldk, ascale, s));
+    else LAUNCH(m, launch_quantize_per_tensor(x, K, rows_q, K, am, q8, ldk, ascale, s));
     return ESMCU_OK;
   };
   auto observe = [&](int layer, int site, const float* x, size_t n) {
@@ -522,10 +527,15 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
                                  cudaMemcpyDeviceToDevice, s));
   }
 
-  // ---- final LN + LM head (model.cpp:1181-1239), FP32
+  // ---- final LN + LM head (model.cpp:1181-1239), FP32 unless lm_head.dense
+  // is INT8.  Its per-tensor activation scale is the absmax of all T rows
+  // of the final LN output (the reference quantises the whole operand), taken
+  // by the LN itself into the first spare amax slot.
+  const bool lm_int8 = m->lm_wq != nullptr;
+  uint32_t* am_lm = amax + 4 * c.num_layers * kAmaxSlots;
   sec.begin("final_ln");
   LAUNCH(m, launch_layernorm(hidden, m->final_ln_w, m->final_ln_b, c.layer_norm_eps, ln, T, d,
-                             nullptr, nullptr, 0, nullptr, s));
+                             lm_int8 && !per_token ? am_lm : nullptr, nullptr, 0, nullptr, s));
   sec.end();
   if (hidden_out)  // the last entry is the final LayerNorm's output
     ESMCU_CUDA(cudaMemcpyAsync(hidden_out + static_cast<size_t>(c.num_layers) * Tdh, ln, Tdh * 4,
@@ -545,7 +555,10 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
     e.kind = kEpiGelu;  // dense -> GELU (model.cpp:1192-1223)
     e.C = attn;
     e.ldc = d;
-    if (d % 4 == 0) {
+    if (lm_int8) {  // LinearInt8 (model.cpp:1209-1211)
+      TRY(quantize(head_in, d, m->ldk_d, am_lm, TH));
+      TRY(gemm_i8(m->lm_wq, m->ldk_d, d, m->lm_ws, m->lm_b, e, TH));
+    } else if (d % 4 == 0) {
       // 3xTF32 on the tensor cores; the lo part of `ln` goes to `k` (free
       // once the layers are done).
       LAUNCH(m, launch_tf32_lo(head_in, k, static_cast<long>(TH) * d, s));
@@ -919,6 +932,24 @@ int esmcu_model_set_head(esmcu_model* m, const float* final_ln_w, const float* f
   TRY(upload_vec(m, &m->lm_ln_b, lm_ln_b, d, "lm_ln_b"));
   TRY(upload_vec(m, &m->lm_bias, lm_decoder_bias, static_cast<size_t>(m->cfg.vocab_size), "lm_bias"));
   m->head_set = true;
+  return ESMCU_OK;
+}
+
+int esmcu_model_set_head_int8(esmcu_model* m, const int8_t* lm_dense_wq, const float* lm_dense_ws) {
+  if (m == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "null model");
+  TRY(use_device(m->ctx));
+  if (lm_dense_wq == nullptr) {  // back to the FP32 head (the buffers stay owned)
+    m->lm_wq = nullptr;
+    m->lm_ws = nullptr;
+    return ESMCU_OK;
+  }
+  const int d = m->cfg.hidden_size;
+  int8_t* wq = nullptr;
+  float* ws = nullptr;
+  TRY(upload_i8_padded(m, &wq, &lm_dense_wq, &d, 1, d, m->ldk_d));
+  TRY(upload_vec(m, &ws, lm_dense_ws, static_cast<size_t>(d), "lm_dense_ws"));
+  m->lm_wq = wq;
+  m->lm_ws = ws;
   return ESMCU_OK;
 }
 

@@ -11,6 +11,7 @@ the GPU.  There is no CPU execution path.
 from __future__ import annotations
 
 import ctypes as C
+import os
 from dataclasses import dataclass
 from pathlib import Path
 
@@ -42,6 +43,7 @@ class Config:
     mask_token_id: int = MASK_ID
     weights_quantized: bool = False
     first_block_fc1_fp16: bool = False
+    lm_head_dense_quantized: bool = False
 
 
 def _hf_layer_keys(i: int) -> dict:
@@ -237,13 +239,20 @@ class Model:
 
     # ------------------------------------------------------- quantisation
     def quantize_weights(self) -> None:
-        """model.cpp:1470-1494: per-layer Linears to per-channel int8."""
+        """model.cpp:1470-1494: per-layer Linears to per-channel int8, and
+        lm_head.dense too when ESM_QUANTIZE_LM_HEAD is set to anything but
+        "", "0" or "off" (model.cpp:1487-1492; the LM head's LayerNorm and the
+        tied decoder stay FP32)."""
         if self._cfg.weights_quantized:
             return
         for lw in self.layers:
             for n in LINEARS:
                 q, s = quantize_weight(lw[n + "_w"])
                 lw[n + "_wq"], lw[n + "_ws"] = q, s
+        env = os.environ.get("ESM_QUANTIZE_LM_HEAD")
+        if env and env not in ("0", "off"):
+            self.head["lm_dense_wq"], self.head["lm_dense_ws"] = quantize_weight(self.head["lm_dense_w"])
+            self._cfg.lm_head_dense_quantized = True
         self._cfg.weights_quantized = True
         self._dirty = True
 
@@ -312,6 +321,9 @@ class Model:
         _lib.call("esmcu_model_set_head", dev, fp(h["final_ln_w"]), fp(h["final_ln_b"]),
                   fp(h["lm_dense_w"]), fp(h["lm_dense_b"]), fp(h["lm_ln_w"]), fp(h["lm_ln_b"]),
                   fp(h["lm_bias"]))
+        if c.lm_head_dense_quantized:
+            _lib.call("esmcu_model_set_head_int8", dev, fp(h["lm_dense_wq"], np.int8),
+                      fp(h["lm_dense_ws"]))
         self._dirty = False
 
     def close(self) -> None:

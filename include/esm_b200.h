@@ -191,6 +191,13 @@ int esmcu_model_set_head(esmcu_model* m, const float* final_ln_w, const float* f
                          const float* lm_dense_w, const float* lm_dense_b,
                          const float* lm_ln_w, const float* lm_ln_b,
                          const float* lm_decoder_bias);
+/* lm_head.dense as INT8 (Config::lm_head_dense_quantized, model.h:43-47;
+ * set by QuantizeWeights under ESM_QUANTIZE_LM_HEAD, model.cpp:1487-1492):
+ * per-channel int8 [d, d] (row-major, rows of d bytes) and scales [d]; the
+ * forward then runs LinearInt8 for it (model.cpp:1209-1211) with the
+ * model's activation quantisation.  NULL lm_dense_wq restores the FP32
+ * dense set by esmcu_model_set_head. */
+int esmcu_model_set_head_int8(esmcu_model* m, const int8_t* lm_dense_wq, const float* lm_dense_ws);
 /* Model::ForwardPacked (model.cpp:1093-1255): host ids [T], masks [T] or
  * NULL, cu_seqlens [B+1] -> host logits [T, V] in packed order.  T == 0
  * writes nothing. */

@@ -323,7 +323,10 @@ def forward_packed(model, ids, cu, masks=None, per_token: bool = False, hidden=N
     fl = layernorm(h, hd["final_ln_w"], hd["final_ln_b"], c.layer_norm_eps)
     if hidden is not None:
         hidden[-1] = fl.copy()
-    g = gelu(linear_f32(fl, hd["lm_dense_w"], hd["lm_dense_b"]))
+    if getattr(c, "lm_head_dense_quantized", False):  # LinearInt8 (model.cpp:1209-1211)
+        g = gelu(linear_int8(fl, hd["lm_dense_wq"], hd["lm_dense_ws"], hd["lm_dense_b"], per_token))
+    else:
+        g = gelu(linear_f32(fl, hd["lm_dense_w"], hd["lm_dense_b"]))
     lm = layernorm(g, hd["lm_ln_w"], hd["lm_ln_b"], c.layer_norm_eps)
     return linear_f32(lm, model.embed, hd["lm_bias"])
 

@@ -297,3 +297,41 @@ def test_multi_replica_dispatch_matches_single(tiny_q8):
     for g, w in zip(got, want):
         assert np.array_equal(g, w)
     other.close()
+
+
+def test_int8_lm_head_matches_oracle_and_reference(O, R, tmp_path, monkeypatch, cuda):
+    """ESM_QUANTIZE_LM_HEAD=on (model.cpp:1487-1492): lm_head.dense runs as
+    LinearInt8 (model.cpp:1209-1211) through esmcu_model_set_head_int8.  The
+    device forward matches the oracle and the compiled reference under the
+    whole-forward W8A8 gate; the masked-marginal head (scored rows only,
+    activation scale still over all T rows) matches the full logits' rows."""
+    from esm_b200 import Model, synth
+
+    st = tmp_path / "tiny_lm8.safetensors"
+    synth.random_model(TINY, seed=31).save_to_safetensors(st)
+    seqs, ids, cu = _batch([40, 3, 130, 250], 32)
+    monkeypatch.setenv("ESM_QUANTIZE_LM_HEAD", "on")
+    m = Model.load(st)
+    m.quantize_weights()
+    assert m.config.lm_head_dense_quantized
+    got = m.forward_packed(ids, cu, out=np.empty((ids.size, 33), np.float32))
+    want = O.forward_packed(m, ids, cu)
+    np.testing.assert_allclose(got, want, rtol=1e-3, atol=W8A8_ATOL)
+    _pearson_each(got, want, cu)
+    ref = O.RefModel(st)
+    ref.quantize()
+    O.ref_force_isa("avx512vnni")
+    try:
+        rw = ref.forward_packed(ids, cu)
+    finally:
+        O.ref_force_isa(None)
+    np.testing.assert_allclose(got, rw, rtol=1e-3, atol=W8A8_ATOL)
+    _pearson_each(got, rw, cu)
+    rows = np.array([5, 1, 64, 249], np.int32)
+    lp = m.masked_marginals(seqs, rows)
+    full = m.forward_scheduled(seqs)
+    x = np.stack([full[i][r] for i, r in enumerate(rows)]).astype(np.float64)
+    mx = x.max(axis=1, keepdims=True)
+    want_lp = x - mx - np.log(np.exp(x - mx).sum(axis=1, keepdims=True))
+    assert np.abs(lp - want_lp).max() / (1 + np.abs(want_lp).max()) < 1e-5
+    m.close()
