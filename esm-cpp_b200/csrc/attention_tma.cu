@@ -58,7 +58,7 @@ constexpr uint32_t kOffQ = 0, kOffKV = 32768, kOffLo = 65536;
 constexpr uint32_t kSVpre = 2 * kSlotBytes, kSBarOff = kSVpre + 32768;
 constexpr int kSSmemBytes = static_cast<int>(kSBarOff) + 256 + 1024;
 constexpr uint32_t kSColO = 128, kSColPlo = 256, kSColQlo = 384;
-constexpr uint32_t kColO = 256, kColPlo = 384, kColQlo = 448;  // CTA-pair kernel
+constexpr uint32_t kColO = 256, kColPlo = 384, kColQlo = 448;  // CTA-pair and long kernels
 // CTA-pair kernel: the V buffer first (it is the raw V operand, and V_lo in
 // a slot's third region sits one positive LBO above it), the two slots, a
 // 1 KB zero block (the B operand's second half in P_lo [V | 0]), barriers.
@@ -923,38 +923,47 @@ __global__ void __maxnreg__(128)
 //           2^((S - m) log2 e) chunk by chunk into TMEM as in the short
 //           kernel, O += P V_j (3xTF32), row sums summed over the blocks.
 // O is never rescaled; the price is S computed twice.
-// Tiles flow through a ring of two 64 KB stages (raw | lo, the short
-// kernel's slot layout): the producer loads pass 1's K_j, then pass 2's
-// K_0, V_0, K_1, V_1, ...; the prep warps form each tile's lo part and zero
-// V rows past L.  Within pass 2, S_{j+1} is issued right behind P.V_j
-// (in-order MMAs, as across items in the short kernel); in pass 1 the
-// softmax warps release S explicitly.
-// TMEM: S [0,128) O [128,256) P_lo [256,384) Q_lo [384,448).
+// Two S buffers: S_{j+1} runs on the tensor cores while the softmax warps
+// read or convert S_j.  Pass 2 issues S_0, S_1, P.V_0, S_2, P.V_1, ...; P_lo
+// has two 32-column slots, chunk c reusing slot c & 1 once the P.V that read
+// it last is done.  Tiles flow through a ring of three 64 KB stages (raw |
+// lo, the short kernel's slot layout) in the order the MMAs take them: pass
+// 1's K_0 .. K_{n-1}, then K_0, K_1, V_0, K_2, V_1, ..., V_{n-1}; the prep
+// warps form each tile's lo part and zero V rows past L.  A tile's load and
+// lo take about two S computations, hence three stages.
+// TMEM: S0 [0,128) S1 [128,256) O [256,384) P_lo [384,448) Q_lo [448,512).
+constexpr uint32_t kLNst = 3;  // ring stages
 constexpr uint32_t kLQ = 0, kLRing = 32768, kLStage = 65536;
-constexpr uint32_t kLRed = kLRing + 2 * kLStage;  // red_max [2][128] | red_sum [2][128]
-constexpr uint32_t kLBarOff = kLRed + 2048;
+constexpr uint32_t kLRed = kLRing + kLNst * kLStage;  // [2][128] floats: row max, then row sum
+constexpr uint32_t kLBarOff = kLRed + 1024;
 constexpr int kLSmemBytes = static_cast<int>(kLBarOff) + 256 + 1024;
+// 227 KB per block on sm_100a, less the kernel's static shared memory (128 B).
+static_assert(kLSmemBytes + 256 <= 232448, "long-kernel shared memory");
 enum : int {
-  kLFull = 0,    // [2] TMA tile landed in stage s
-  kLReady = 2,   // [2] prep done with stage s (4 prep warps)
-  kLFree = 4,    // [2] MMAs done with stage s
-  kLQFull = 6,   // TMA Q landed
-  kLQReady = 7,  // Q_lo in TMEM (4 prep warps)
-  kLQFree = 8,   // the item's last S done: Q and Q_lo free
-  kLSDone = 9,   // an S is in TMEM
-  kLSFree = 10,  // pass 1: S read (8 softmax warps)
-  kLODone = 11,  // the item's P.V done
-  kLChunk = 12,  // [4] P chunk c written (4 softmax warps)
-  kLNumBars = 16
+  kLFull = 0,     // [3] TMA tile landed in ring stage s
+  kLReady = 3,    // [3] prep done with stage s (4 prep warps)
+  kLFree = 6,     // [3] MMAs done with stage s
+  kLQFull = 9,    // TMA Q landed
+  kLQReady = 10,  // Q_lo in TMEM (4 prep warps)
+  kLQFree = 11,   // the item's last S done: Q and Q_lo free
+  kLSDone = 12,   // [2] S buffer b holds a finished S
+  kLSFree = 14,   // [2] the softmax warps are done with S buffer b (8 warps)
+  kLODone = 16,   // the item's P.V done
+  kLLoFree = 17,  // [2] the P.V that read P_lo slot s is done
+  kLChunk = 19,   // [4] P chunk c written (4 softmax warps)
+  kLNumBars = 23
 };
+// Ring stage and phase parity of tile t.
+__device__ __forceinline__ int ring_stage(uint32_t t) { return static_cast<int>(t % kLNst); }
+__device__ __forceinline__ uint32_t ring_parity(uint32_t t) { return (t / kLNst) & 1u; }
 
-struct LItem {
+struct QTile {
   int h, s0, L, q0;
 };
 
 // Item it = (b * H + h) * qtiles + qt; valid when L > 256 and q0 < L.
-__device__ __forceinline__ bool decode_long(int it, int H, int qtiles, const int* __restrict__ cu,
-                                            LItem& w) {
+__device__ __forceinline__ bool decode_qtile(int it, int H, int qtiles, const int* __restrict__ cu,
+                                             QTile& w) {
   const int per_seq = H * qtiles;
   const int b = it / per_seq;
   const int r = it - b * per_seq;
@@ -965,12 +974,32 @@ __device__ __forceinline__ bool decode_long(int it, int H, int qtiles, const int
   return w.L > LMAX2 && w.q0 < w.L;
 }
 
-__device__ __forceinline__ int next_long(int it, int stride, int n_items, int H, int qtiles,
-                                         const int* __restrict__ cu, LItem& w) {
+__device__ __forceinline__ int next_qtile(int it, int stride, int n_items, int H, int qtiles,
+                                          const int* __restrict__ cu, QTile& w) {
   for (; it < n_items; it += stride)
-    if (decode_long(it, H, qtiles, cu, w)) return it;
+    if (decode_qtile(it, H, qtiles, cu, w)) return it;
   return n_items;
 }
+
+// Pass-2 tile i of an item with nkb key blocks: K_0, then K_m and V_{m-1}
+// alternately, V_{nkb-1} last.
+__device__ __forceinline__ void pass2_tile(int i, int nkb, bool& is_v, int& j) {
+  if (i == 0) {
+    is_v = false;
+    j = 0;
+  } else if (i == 2 * nkb - 1) {
+    is_v = true;
+    j = nkb - 1;
+  } else if (i & 1) {
+    is_v = false;
+    j = (i + 1) >> 1;
+  } else {
+    is_v = true;
+    j = (i >> 1) - 1;
+  }
+}
+__device__ __forceinline__ int pass2_k(int j) { return j == 0 ? 0 : 2 * j - 1; }
+__device__ __forceinline__ int pass2_v(int j, int nkb) { return j == nkb - 1 ? 2 * nkb - 1 : 2 * j + 2; }
 
 __global__ void __maxnreg__(128)
     attention_tma_long_kernel(const __grid_constant__ CUtensorMap tmQ,
@@ -986,24 +1015,27 @@ __global__ void __maxnreg__(128)
   volatile uint32_t* abort_flag = tslot + 1;
 
   const int stride = gridDim.x;
-  LItem first;
-  const int it0 = next_long(blockIdx.x, stride, n_items, H, qtiles, cu, first);
+  QTile first;
+  const int it0 = next_qtile(blockIdx.x, stride, n_items, H, qtiles, cu, first);
   if (it0 >= n_items) return;  // CTA-uniform, before any barrier
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const long rs = static_cast<long>(H) * DH;  // token row stride (floats)
 
   if (tid == 0) {
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < static_cast<int>(kLNst); ++i) {
       mbar_init(&bar[kLFull + i], 1);
       mbar_init(&bar[kLReady + i], 4);
       mbar_init(&bar[kLFree + i], 1);
     }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar[kLSDone + i], 1);
+      mbar_init(&bar[kLSFree + i], 8);
+      mbar_init(&bar[kLLoFree + i], 1);
+    }
     mbar_init(&bar[kLQFull], 1);
     mbar_init(&bar[kLQReady], 4);
     mbar_init(&bar[kLQFree], 1);
-    mbar_init(&bar[kLSDone], 1);
-    mbar_init(&bar[kLSFree], 8);
     mbar_init(&bar[kLODone], 1);
     for (int c = 0; c < 4; ++c) mbar_init(&bar[kLChunk + c], 4);
     *abort_flag = 0u;
@@ -1020,10 +1052,10 @@ __global__ void __maxnreg__(128)
 
   bool ok = true;
   float mx_out = 0.0f;
-  LItem cur = first;
+  QTile cur = first;
   int it = it0;
-  int n = 0;       // this CTA's item counter
-  uint32_t t = 0;  // ring tile counter (producer, prep and MMA count alike)
+  int n = 0;        // this CTA's item counter
+  uint32_t tb = 0;  // ring index of the item's first tile (3 nkb tiles per item)
 
   if (warp == 0) {
     // ================================================== TMA producer
@@ -1038,13 +1070,15 @@ __global__ void __maxnreg__(128)
         for (int blk = 0; blk < 2; ++blk)
           tma_load_2d(smem + kLQ + blk * 16384, &tmQ, &bar[kLQFull], cur.h * DH + 32 * blk,
                       cur.s0 + cur.q0);
-        for (int i = 0; i < 3 * nkb; ++i, ++t) {
-          const int s = static_cast<int>(t & 1);
-          if (t >= 2 && !(ok = mbar_wait_abort(&bar[kLFree + s], ((t >> 1) + 1) & 1, status, abort_flag)))
+        for (int i = 0; i < 3 * nkb; ++i) {
+          const uint32_t t = tb + static_cast<uint32_t>(i);
+          const int s = ring_stage(t);
+          // The stage's previous tile, t - kLNst, must be consumed.
+          if (t >= kLNst && !(ok = mbar_wait_abort(&bar[kLFree + s], ring_parity(t - kLNst), status, abort_flag)))
             break;
-          // Tiles 0..nkb-1: pass 1's K_j; then K_j, V_j alternately.
-          const bool is_v = i >= nkb && ((i - nkb) & 1);
-          const int j = i < nkb ? i : (i - nkb) >> 1;
+          bool is_v = false;
+          int j = i;
+          if (i >= nkb) pass2_tile(i - nkb, nkb, is_v, j);
           uint8_t* st = smem + kLRing + s * kLStage;
           mbar_arrive_expect_tx(&bar[kLFull + s], 2 * 16384);
           for (int blk = 0; blk < 2; ++blk)
@@ -1052,8 +1086,9 @@ __global__ void __maxnreg__(128)
                         cur.s0 + QB * j);
         }
         if (!ok) break;
-        LItem nxt;
-        const int itn = next_long(it + stride, stride, n_items, H, qtiles, cu, nxt);
+        tb += 3u * static_cast<uint32_t>(nkb);
+        QTile nxt;
+        const int itn = next_qtile(it + stride, stride, n_items, H, qtiles, cu, nxt);
         if (itn >= n_items) break;
         it = itn;
         cur = nxt;
@@ -1063,80 +1098,81 @@ __global__ void __maxnreg__(128)
   } else if (warp == 1) {
     // ==================================================== MMA issuer
     if (lane == 0) {
-      uint32_t cpar = 0;    // bit c: parity of the next completion of chunk barrier c
-      uint32_t sfree = 0;   // completions of kLSFree consumed
+      uint32_t cpar = 0;  // bit c: parity of the next completion of chunk barrier c
+      uint32_t ns = 0;    // S computations issued (S buffer ns & 1)
       const uint32_t idS = idesc_tf32(QB, QB);
       const uint32_t idO = idesc_tf32_bmn(QB, DH);
       const uint32_t idO2 = idesc_tf32_bmn(QB, 2 * DH);
       const uint32_t q_s = smem_u32(smem + kLQ);
-      const uint32_t tS = tmem;
+
+      // S = Q_raw K_raw^T + Q_raw K_lo^T + Q_lo K_raw^T for the K tile at
+      // ring index t into the next S buffer (identical in both passes);
+      // returns false on a failed wait.
+      auto issue_s = [&](uint32_t t) -> bool {
+        const int s = ring_stage(t);
+        if (!mbar_wait_abort(&bar[kLReady + s], ring_parity(t), status, abort_flag)) return false;
+        const uint32_t b = ns & 1;
+        if (ns >= 2 && !mbar_wait_abort(&bar[kLSFree + b], ((ns >> 1) + 1) & 1, status, abort_flag))
+          return false;
+        ++ns;
+        tc_fence_after();
+        const uint32_t st = smem_u32(smem + kLRing + s * kLStage), tS = tmem + 128u * b;
+#pragma unroll
+        for (int kk = 0; kk < DH / 8; ++kk) {
+          const uint32_t o = static_cast<uint32_t>((kk >> 2) * 16384 + (kk & 3) * 32);
+          const uint64_t a_raw = sw128_kmajor_desc(q_s + o);
+          mma_tf32(tS, a_raw, sw128_kmajor_desc(st + o), idS, kk > 0 ? 1u : 0u);
+          mma_tf32(tS, a_raw, sw128_kmajor_desc(st + 32768u + o), idS, 1u);
+          mma_tf32_ts(tS, tmem + kColQlo + 8u * kk, sw128_kmajor_desc(st + o), idS, 1u);
+        }
+        mma_commit(&bar[kLSDone + b]);
+        mma_commit(&bar[kLFree + s]);
+        return true;
+      };
       while (ok) {
         const int L = cur.L, nkb = (L + QB - 1) / QB;
         if (!(ok = mbar_wait_abort(&bar[kLQReady], n & 1, status, abort_flag))) break;
-        // S = Q_raw K_raw^T + Q_raw K_lo^T + Q_lo K_raw^T for the K tile in
-        // ring stage st, identical in both passes.
-        auto issue_s = [&](uint32_t st) {
-#pragma unroll
-          for (int kk = 0; kk < DH / 8; ++kk) {
-            const uint32_t o = static_cast<uint32_t>((kk >> 2) * 16384 + (kk & 3) * 32);
-            const uint64_t a_raw = sw128_kmajor_desc(q_s + o);
-            mma_tf32(tS, a_raw, sw128_kmajor_desc(st + o), idS, kk > 0 ? 1u : 0u);
-            mma_tf32(tS, a_raw, sw128_kmajor_desc(st + 32768u + o), idS, 1u);
-            mma_tf32_ts(tS, tmem + kSColQlo + 8u * kk, sw128_kmajor_desc(st + o), idS, 1u);
-          }
-        };
         // ---- pass 1: S_j for the row max
-        for (int j = 0; j < nkb && ok; ++j, ++t) {
-          const int s = static_cast<int>(t & 1);
-          if (!(ok = mbar_wait_abort(&bar[kLReady + s], (t >> 1) & 1, status, abort_flag))) break;
-          if (j > 0 && !(ok = mbar_wait_abort(&bar[kLSFree], sfree++ & 1, status, abort_flag))) break;
-          tc_fence_after();
-          issue_s(smem_u32(smem + kLRing + s * kLStage));
-          mma_commit(&bar[kLSDone]);
+        for (int j = 0; j < nkb && ok; ++j) ok = issue_s(tb + static_cast<uint32_t>(j));
+        if (!ok) break;
+        // ---- pass 2: S_0, S_1, P.V_0, S_2, P.V_1, ...
+        const uint32_t t2 = tb + static_cast<uint32_t>(nkb);
+        const uint32_t b0 = ns & 1;  // S buffer of pass 2's S_0
+        if (!(ok = issue_s(t2))) break;
+        if (nkb == 1) mma_commit(&bar[kLQFree]);
+        for (int j = 0; j < nkb && ok; ++j) {
+          if (j + 1 < nkb) {
+            if (!(ok = issue_s(t2 + static_cast<uint32_t>(pass2_k(j + 1))))) break;
+            if (j + 2 == nkb) mma_commit(&bar[kLQFree]);  // the item's last S
+          }
+          const uint32_t t = t2 + static_cast<uint32_t>(pass2_v(j, nkb));
+          const int s = ring_stage(t);
+          if (!(ok = mbar_wait_abort(&bar[kLReady + s], ring_parity(t), status, abort_flag))) break;
+          const uint32_t st = smem_u32(smem + kLRing + s * kLStage);
+          const uint32_t tS = tmem + 128u * ((b0 + static_cast<uint32_t>(j)) & 1u);
+          const int nchunk = min(QB / KC, (L - QB * j + KC - 1) / KC);
+          for (int c = 0; c < nchunk; ++c) {
+            if (!(ok = mbar_wait_abort(&bar[kLChunk + c], (cpar >> c) & 1u, status, abort_flag))) break;
+            cpar ^= 1u << c;
+            tc_fence_after();
+            // P_hi [V | V_lo] as one N = 128 MMA, then P_lo V at N = 64.
+#pragma unroll
+            for (int kk = 0; kk < KC / 8; ++kk) {
+              const uint32_t vo = static_cast<uint32_t>(c * 4096 + kk * 1024);
+              const uint64_t v_all = sw128b32_mnmajor_desc(st + vo, 16384);
+              mma_tf32_ts(tmem + kColO, tS + 32u * c + 8u * kk, v_all, idO2, (j | c | kk) != 0 ? 1u : 0u);
+              mma_tf32_ts(tmem + kColO, tmem + kColPlo + 32u * (c & 1) + 8u * kk, v_all, idO, 1u);
+            }
+            mma_commit(&bar[kLLoFree + (c & 1)]);
+          }
+          if (!ok) break;
           mma_commit(&bar[kLFree + s]);
         }
         if (!ok) break;
-        // ---- pass 2: S_j again, then O += P_j V_j chunk by chunk
-        for (int j = 0; j < nkb && ok; ++j) {
-          {
-            const int s = static_cast<int>(t & 1);
-            if (!(ok = mbar_wait_abort(&bar[kLReady + s], (t >> 1) & 1, status, abort_flag))) break;
-            if (j == 0 && !(ok = mbar_wait_abort(&bar[kLSFree], sfree++ & 1, status, abort_flag))) break;
-            tc_fence_after();
-            issue_s(smem_u32(smem + kLRing + s * kLStage));
-            mma_commit(&bar[kLSDone]);
-            mma_commit(&bar[kLFree + s]);
-            if (j == nkb - 1) mma_commit(&bar[kLQFree]);
-            ++t;
-          }
-          {
-            const int s = static_cast<int>(t & 1);
-            if (!(ok = mbar_wait_abort(&bar[kLReady + s], (t >> 1) & 1, status, abort_flag))) break;
-            const uint32_t st = smem_u32(smem + kLRing + s * kLStage);
-            const int nchunk = min(QB / KC, (L - QB * j + KC - 1) / KC);
-            for (int c = 0; c < nchunk; ++c) {
-              if (!(ok = mbar_wait_abort(&bar[kLChunk + c], (cpar >> c) & 1u, status, abort_flag))) break;
-              cpar ^= 1u << c;
-              tc_fence_after();
-              // P_hi [V | V_lo] as one N = 128 MMA, then P_lo V at N = 64.
-#pragma unroll
-              for (int kk = 0; kk < KC / 8; ++kk) {
-                const uint32_t vo = static_cast<uint32_t>(c * 4096 + kk * 1024);
-                const uint64_t v_all = sw128b32_mnmajor_desc(st + vo, 16384);
-                mma_tf32_ts(tmem + kSColO, tS + 32u * c + 8u * kk, v_all, idO2,
-                            (j | c | kk) != 0 ? 1u : 0u);
-                mma_tf32_ts(tmem + kSColO, tmem + kSColPlo + 32u * c + 8u * kk, v_all, idO, 1u);
-              }
-            }
-            if (!ok) break;
-            mma_commit(&bar[kLFree + s]);
-            ++t;
-          }
-        }
-        if (!ok) break;
         mma_commit(&bar[kLODone]);
-        LItem nxt;
-        const int itn = next_long(it + stride, stride, n_items, H, qtiles, cu, nxt);
+        tb += 3u * static_cast<uint32_t>(nkb);
+        QTile nxt;
+        const int itn = next_qtile(it + stride, stride, n_items, H, qtiles, cu, nxt);
         if (itn >= n_items) break;
         it = itn;
         cur = nxt;
@@ -1169,47 +1205,50 @@ __global__ void __maxnreg__(128)
           lo[4 * c4 + 2] = __float_as_uint(l.z);
           lo[4 * c4 + 3] = __float_as_uint(l.w);
         }
-        tmem_st32(tmem + kSColQlo + 32u * blk + lane_off, lo);
+        tmem_st32(tmem + kColQlo + 32u * blk + lane_off, lo);
       }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[kLQReady]);
-      for (int i = 0; i < 3 * nkb; ++i, ++t) {
-        const int s = static_cast<int>(t & 1);
-        if (!(ok = mbar_wait_abort(&bar[kLFull + s], (t >> 1) & 1, status, abort_flag))) break;
+      for (int i = 0; i < 3 * nkb; ++i) {
+        const uint32_t t = tb + static_cast<uint32_t>(i);
+        const int s = ring_stage(t);
+        if (!(ok = mbar_wait_abort(&bar[kLFull + s], ring_parity(t), status, abort_flag))) break;
+        bool is_v = false;
+        int j = i;
+        if (i >= nkb) pass2_tile(i - nkb, nkb, is_v, j);
         const uint32_t raw = smem_u32(smem + kLRing + s * kLStage), lo = raw + 32768u;
-        {
-          if (i < nkb || ((i - nkb) & 1) == 0) {
-            tile_lo_32k(raw, lo, ptid);  // K_j (either pass)
-          } else {
-            // V_j: lo, with keys (rows) past L zeroed in both parts.
-            const int kvalid = L - QB * ((i - nkb) >> 1);
+        if (!is_v) {
+          tile_lo_32k(raw, lo, ptid);  // K_j (either pass)
+        } else {
+          // V_j: lo, with keys (rows) past L zeroed in both parts.
+          const int kvalid = L - QB * j;
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              float4 x[8];
+          for (int h = 0; h < 2; ++h) {
+            float4 x[8];
 #pragma unroll
-              for (int e = 0; e < 8; ++e)
-                x[e] = lds128(raw + static_cast<uint32_t>((ptid + (h * 8 + e) * 128) * 16));
+            for (int e = 0; e < 8; ++e)
+              x[e] = lds128(raw + static_cast<uint32_t>((ptid + (h * 8 + e) * 128) * 16));
 #pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                const uint32_t o = static_cast<uint32_t>((ptid + (h * 8 + e) * 128) * 16);
-                if (static_cast<int>((o & 16383u) >> 7) >= kvalid) {
-                  x[e] = make_float4(0.f, 0.f, 0.f, 0.f);
-                  sts128(raw + o, x[e]);
-                }
-                sts128(lo + o, tf32_lo4(x[e]));
+            for (int e = 0; e < 8; ++e) {
+              const uint32_t o = static_cast<uint32_t>((ptid + (h * 8 + e) * 128) * 16);
+              if (static_cast<int>((o & 16383u) >> 7) >= kvalid) {
+                x[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+                sts128(raw + o, x[e]);
               }
+              sts128(lo + o, tf32_lo4(x[e]));
             }
           }
-          fence_proxy_async_smem();
         }
+        fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bar[kLReady + s]);
       }
       if (!ok) break;
-      LItem nxt;
-      const int itn = next_long(it + stride, stride, n_items, H, qtiles, cu, nxt);
+      tb += 3u * static_cast<uint32_t>(nkb);
+      QTile nxt;
+      const int itn = next_qtile(it + stride, stride, n_items, H, qtiles, cu, nxt);
       if (itn >= n_items) break;
       it = itn;
       cur = nxt;
@@ -1224,49 +1263,72 @@ __global__ void __maxnreg__(128)
     const int quad = warp & 3, par = sw >> 2;
     const int row = quad * 32 + lane;  // query row within the tile = TMEM lane
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-    const uint32_t tS = tmem + lane_off;
-    float (*red_max)[QB] = reinterpret_cast<float (*)[QB]>(smem + kLRed);
-    float (*red_sum)[QB] = reinterpret_cast<float (*)[QB]>(smem + kLRed + 1024);
-    uint32_t sd = 0;  // completions of kLSDone consumed
+    // One exchange array for the row max and then the row sum; a named
+    // barrier after every read keeps each write behind all reads of the
+    // previous value.
+    float (*red)[QB] = reinterpret_cast<float (*)[QB]>(smem + kLRed);
+    uint32_t ns = 0;       // S computations consumed (S buffer ns & 1)
+    uint32_t lo_uses = 0;  // this warp's writes of P_lo slot par (chunks c with c & 1 == par)
     bool good = ok;
+    // Waits for S number ns; returns its TMEM address (this warp's lanes).
+    auto next_s = [&](uint32_t& b) -> bool {
+      b = ns & 1;
+      const bool w = mbar_wait_abort(&bar[kLSDone + b], (ns >> 1) & 1, status, abort_flag);
+      ++ns;
+      tc_fence_after();
+      return w;
+    };
+    auto release_s = [&](uint32_t b) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[kLSFree + b]);
+    };
     while (true) {
       const int L = cur.L, nkb = (L + QB - 1) / QB;
-      // ---- pass 1: the row's stabiliser over all keys
+      // ---- pass 1: the row max over all keys
       float mx = -INFINITY;
       for (int j = 0; j < nkb && good; ++j) {
-        if (!(good = mbar_wait_abort(&bar[kLSDone], sd++ & 1, status, abort_flag))) break;
-        tc_fence_after();
+        uint32_t b;
+        if (!(good = next_s(b))) break;
         const int kv = L - QB * j;
-        mx = fmaxf(mx, s_row_max(tS, par, min(QB / KC, (kv + KC - 1) / KC), kv));
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bar[kLSFree]);
+        mx = fmaxf(mx, s_row_max(tmem + 128u * b + lane_off, par, min(QB / KC, (kv + KC - 1) / KC), kv));
+        release_s(b);
       }
-      red_max[par][row] = mx;
+      red[par][row] = mx;
       if (!soft_all(good)) break;
-      mx = fmaxf(red_max[0][row], red_max[1][row]);
-      // ---- pass 2: P chunks (P_hi over S, P_lo into its slot), row sums
+      mx = fmaxf(red[0][row], red[1][row]);
+      soft_sync();
+      // ---- pass 2: P chunks (P_hi over S, P_lo into slot c & 1), row sums
       float sum = 0.0f;
       for (int j = 0; j < nkb && good; ++j) {
-        if (!(good = mbar_wait_abort(&bar[kLSDone], sd++ & 1, status, abort_flag))) break;
-        tc_fence_after();
+        uint32_t b;
+        if (!(good = next_s(b))) break;
         const int kv = L - QB * j;
-        sum = __fadd_rn(sum, p_chunks(tS, tmem + kSColPlo + lane_off, 3u, par,
-                                      min(QB / KC, (kv + KC - 1) / KC), kv, mx, [](int) {},
+        sum = __fadd_rn(sum, p_chunks(tmem + 128u * b + lane_off, tmem + kColPlo + lane_off, 1u, par,
+                                      min(QB / KC, (kv + KC - 1) / KC), kv, mx,
+                                      [&](int) {
+                                        if (lo_uses > 0 && good)
+                                          good = mbar_wait_abort(&bar[kLLoFree + par], (lo_uses - 1) & 1,
+                                                                 status, abort_flag);
+                                        ++lo_uses;
+                                        tc_fence_after();
+                                      },
                                       [&](int c) {
                                         if (lane == 0) mbar_arrive(&bar[kLChunk + c]);
                                       }));
+        release_s(b);
       }
-      red_sum[par][row] = sum;
+      red[par][row] = sum;
       if (!soft_all(good)) break;
-      const float total = __fadd_rn(red_sum[0][row], red_sum[1][row]);
+      const float total = __fadd_rn(red[0][row], red[1][row]);
+      soft_sync();
       // ---- O / sum straight to the output rows of this tile
       good = mbar_wait_abort(&bar[kLODone], n & 1, status, abort_flag);
       if (good) {
         tc_fence_after();
         uint32_t o[32], ob[32];
-        tmem_ld32(tmem + kSColO + lane_off + 32u * par, o);
-        tmem_ld32(tmem + kSColO + 64u + lane_off + 32u * par, ob);
+        tmem_ld32(tmem + kColO + lane_off + 32u * par, o);
+        tmem_ld32(tmem + kColO + 64u + lane_off + 32u * par, ob);
         tmem_ld_wait();
         tc_fence_before();
         const float inv = __fdiv_rn(1.0f, total);
@@ -1284,8 +1346,8 @@ __global__ void __maxnreg__(128)
           }
         }
       }
-      LItem nxt;
-      const int itn = next_long(it + stride, stride, n_items, H, qtiles, cu, nxt);
+      QTile nxt;
+      const int itn = next_qtile(it + stride, stride, n_items, H, qtiles, cu, nxt);
       if (itn >= n_items) break;
       it = itn;
       cur = nxt;
