@@ -66,6 +66,9 @@ struct esmcu_model {
   // stride ldk_d, with its per-channel scales; null = the FP32 head.
   int8_t* lm_wq = nullptr;
   float* lm_ws = nullptr;
+  // Config::first_block_fc1_fp16 (model.h:38-41): layer 0's fc1 input is
+  // rounded to fp16 precision (model.cpp:1031-1033).
+  bool fc1_fp16 = false;
   float* embed_lo = nullptr;  // the same for the tied decoder (embed^T)
   // Device staging of the hidden states for ForwardWithHiddenStates.
   float* hs_dev = nullptr;
@@ -470,21 +473,28 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
     }
     sec.end();
     // ---- FFN block
+    // Layer 0 with the fp16 escape: LN to fp32, observe, round, then quantise
+    // from the rounded values (their absmax is the per-tensor scale).
+    const bool round0 = m->fc1_fp16 && li == 0;
     sec.begin("ffn_ln");
-    if (ln_fused) {
+    if (ln_fused && !round0) {
       LAUNCH(m, launch_layernorm_quant(hidden, L.ln2_w, L.ln2_b, c.layer_norm_eps, T, d,
                                        am + 2 * kAmaxSlots, lnstat, ln_sync + 2 * li + 1, q8,
                                        m->ldk_d, ascale, ctx->d_status, s));
-    } else if (quant && per_token) {
+    } else if (quant && per_token && !round0) {
       LAUNCH(m, launch_layernorm(hidden, L.ln2_w, L.ln2_b, c.layer_norm_eps, nullptr, T, d, nullptr,
                                  q8, m->ldk_d, ascale, s));
     } else {
       LAUNCH(m, launch_layernorm(hidden, L.ln2_w, L.ln2_b, c.layer_norm_eps, ln, T, d,
-                                 quant ? am + 2 * kAmaxSlots : nullptr, nullptr, 0, nullptr, s));
+                                 quant && !round0 ? am + 2 * kAmaxSlots : nullptr, nullptr, 0, nullptr,
+                                 s));
     }
     sec.end();
     observe(li, 2, ln, Td);
-    if (quant && !per_token && !ln_fused) {
+    if (round0)
+      LAUNCH(m, launch_round_fp16(ln, static_cast<long>(Td), quant && !per_token ? am + 2 * kAmaxSlots : nullptr,
+                                  s));
+    if (quant && (round0 || (!per_token && !ln_fused))) {
       sec.begin("quantize");
       TRY(quantize(ln, d, m->ldk_d, am + 2 * kAmaxSlots));
       sec.end();
@@ -932,6 +942,12 @@ int esmcu_model_set_head(esmcu_model* m, const float* final_ln_w, const float* f
   TRY(upload_vec(m, &m->lm_ln_b, lm_ln_b, d, "lm_ln_b"));
   TRY(upload_vec(m, &m->lm_bias, lm_decoder_bias, static_cast<size_t>(m->cfg.vocab_size), "lm_bias"));
   m->head_set = true;
+  return ESMCU_OK;
+}
+
+int esmcu_model_set_first_block_fc1_fp16(esmcu_model* m, int enabled) {
+  if (m == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "null model");
+  m->fc1_fp16 = enabled != 0;
   return ESMCU_OK;
 }
 

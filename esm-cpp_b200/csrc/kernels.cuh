@@ -112,6 +112,9 @@ cudaError_t launch_quantize_per_tensor(const float* x, long ldx, int M, int K,
 cudaError_t launch_quantize_per_token(const float* x, long ldx, int M, int K, int8_t* q,
                                       long ldq, float* row_scales, cudaStream_t s);
 cudaError_t launch_absmax(const float* x, long n, uint32_t* amax_bits, cudaStream_t s);
+// x = float(half(x)) in place (round to nearest even); optional absmax of the
+// rounded values into amax_bits.
+cudaError_t launch_round_fp16(float* x, long n, uint32_t* amax_bits, cudaStream_t s);
 
 // --------------------------------------------------------------- LayerNorm
 // out = LN(x) with the reference's rounding (double sums, float normalise).
@@ -140,7 +143,8 @@ cudaError_t launch_layernorm_quant(const float* x, const float* g, const float* 
 // T = cu[B], min_len / max_len = shortest / longest sequence (host-known).
 // Optional absmax of out into *amax.  head_dim 64 runs on the tensor cores
 // (needs the status word): one CTA per (sequence, head) for L <= 128, a CTA
-// pair for 128 < L <= 256; other shapes on FP32 SIMT.
+// pair for 128 < L <= 256, one CTA per (sequence, head, 128-row query tile)
+// above; other head dims on FP32 SIMT.
 cudaError_t launch_attention_varlen(const float* q, const float* k, const float* v,
                                     const int* cu, int B, int H, int dh, long T, int min_len,
                                     int max_len, float* out, uint32_t* amax, uint32_t* status,

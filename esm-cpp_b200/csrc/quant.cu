@@ -8,6 +8,8 @@
 //
 // Per-token: the same formula with one scale per row (the reference's
 // QuantizeActivationSymmetricRef, pack.cpp:134-147, applied row by row).
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -95,6 +97,20 @@ __global__ void absmax_kernel(const float* __restrict__ x, long n, uint32_t* ama
   amax_publish(amax_bits, mx);
 }
 
+// x = float(half(x)), round to nearest even (the layer-0 fc1 input escape,
+// model.cpp:912-930, 1031-1033); with amax_bits, also the absmax of the
+// rounded values.
+__global__ void round_fp16_kernel(float* __restrict__ x, long n, uint32_t* amax_bits) {
+  float mx = 0.0f;
+  for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const float r = __half2float(__float2half_rn(x[i]));
+    x[i] = r;
+    mx = fmaxf(mx, fabsf(r));
+  }
+  if (amax_bits != nullptr) amax_publish(amax_bits, mx);
+}
+
 int grid_for(long work, int block) {
   long g = (work + block - 1) / block;
   if (g > 148L * 16) g = 148L * 16;
@@ -121,6 +137,12 @@ cudaError_t launch_quantize_per_token(const float* x, long ldx, int M, int K, in
   const long threads = static_cast<long>(M) * 32;
   quantize_per_token_kernel<<<static_cast<int>((threads + 255) / 256), 256, 0, s>>>(
       x, ldx, M, K, q, ldq, row_scales);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_round_fp16(float* x, long n, uint32_t* amax_bits, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  round_fp16_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, n, amax_bits);
   return cudaGetLastError();
 }
 

@@ -95,6 +95,7 @@ _SIGS = {
     "esmcu_model_set_embeddings": (C.c_int, [_VP, _VP]),
     "esmcu_model_set_layer": (C.c_int, [_VP, C.c_int, C.POINTER(LayerWeights)]),
     "esmcu_model_set_head_int8": (C.c_int, [_VP, _VP, _VP]),
+    "esmcu_model_set_first_block_fc1_fp16": (C.c_int, [_VP, C.c_int]),
     "esmcu_model_set_head": (C.c_int, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP]),
     "esmcu_model_forward_packed": (C.c_int, [_VP, _VP, _VP, C.c_int, _VP, C.c_int, _VP]),
     "esmcu_model_forward_scheduled": (C.c_int, [_VP, _VP, _VP, _VP, C.c_int, C.c_float, C.c_int,

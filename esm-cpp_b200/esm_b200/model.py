@@ -233,9 +233,10 @@ class Model:
         self._dirty = True
 
     def set_first_block_fc1_fp16(self, enabled: bool) -> None:
-        if enabled:
-            raise NotImplementedError("the layer-0 fc1 FP16 escape is not on this engine's path")
-        self._cfg.first_block_fc1_fp16 = False
+        """Config::first_block_fc1_fp16: round layer 0's fc1 input to fp16
+        precision (model.cpp:1031-1033); saved as esm.first_block_fc1_fp16."""
+        self._cfg.first_block_fc1_fp16 = bool(enabled)
+        self._dirty = True
 
     # ------------------------------------------------------- quantisation
     def quantize_weights(self) -> None:
@@ -321,6 +322,8 @@ class Model:
         _lib.call("esmcu_model_set_head", dev, fp(h["final_ln_w"]), fp(h["final_ln_b"]),
                   fp(h["lm_dense_w"]), fp(h["lm_dense_b"]), fp(h["lm_ln_w"]), fp(h["lm_ln_b"]),
                   fp(h["lm_bias"]))
+        if c.first_block_fc1_fp16:
+            _lib.call("esmcu_model_set_first_block_fc1_fp16", dev, 1)
         if c.lm_head_dense_quantized:
             _lib.call("esmcu_model_set_head_int8", dev, fp(h["lm_dense_wq"], np.int8),
                       fp(h["lm_dense_ws"]))

@@ -198,6 +198,10 @@ int esmcu_model_set_head(esmcu_model* m, const float* final_ln_w, const float* f
  * model's activation quantisation.  NULL lm_dense_wq restores the FP32
  * dense set by esmcu_model_set_head. */
 int esmcu_model_set_head_int8(esmcu_model* m, const int8_t* lm_dense_wq, const float* lm_dense_ws);
+/* Config::first_block_fc1_fp16 (model.h:38-41; GGUF key
+ * esm.first_block_fc1_fp16): nonzero rounds layer 0's fc1 input to fp16
+ * precision, round to nearest even, before its Linear (model.cpp:1031-1033). */
+int esmcu_model_set_first_block_fc1_fp16(esmcu_model* m, int enabled);
 /* Model::ForwardPacked (model.cpp:1093-1255): host ids [T], masks [T] or
  * NULL, cu_seqlens [B+1] -> host logits [T, V] in packed order.  T == 0
  * writes nothing. */

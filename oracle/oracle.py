@@ -304,7 +304,7 @@ def forward_packed(model, ids, cu, masks=None, per_token: bool = False, hidden=N
             return linear_int8(x, lw[n + "_wq"], lw[n + "_ws"], lw[n + "_b"], per_token)
         return linear_f32(x, lw[n + "_w"], lw[n + "_b"])
 
-    for lw in model.layers:
+    for li, lw in enumerate(model.layers):
         ln = layernorm(h, lw["attn_ln_w"], lw["attn_ln_b"], c.layer_norm_eps)
         q = lin(ln, lw, "q")
         k = lin(ln, lw, "k")
@@ -315,6 +315,8 @@ def forward_packed(model, ids, cu, masks=None, per_token: bool = False, hidden=N
         att = attention_varlen(q, k, v, cu, H, dh)
         h = (h + lin(att, lw, "out")).astype(F32)
         ln = layernorm(h, lw["ffn_ln_w"], lw["ffn_ln_b"], c.layer_norm_eps)
+        if li == 0 and getattr(c, "first_block_fc1_fp16", False):
+            ln = ln.astype(np.float16).astype(F32)  # model.cpp:1031-1033, RNE
         inter = gelu(lin(ln, lw, "fc1"))
         h = (h + lin(inter, lw, "fc2")).astype(F32)
         if hidden is not None:

@@ -335,3 +335,40 @@ def test_int8_lm_head_matches_oracle_and_reference(O, R, tmp_path, monkeypatch, 
     want_lp = x - mx - np.log(np.exp(x - mx).sum(axis=1, keepdims=True))
     assert np.abs(lp - want_lp).max() / (1 + np.abs(want_lp).max()) < 1e-5
     m.close()
+
+
+@pytest.mark.parametrize("quantized", [False, True])
+def test_first_block_fc1_fp16_matches_oracle_and_reference(O, R, tmp_path, cuda, quantized):
+    """esm.first_block_fc1_fp16 (model.cpp:1031-1033) on the device: layer 0's
+    fc1 input rounded to fp16 (and, per tensor, its absmax taken after the
+    rounding) against the oracle and the compiled reference loading the same
+    GGUF."""
+    from esm_b200 import Model, synth
+
+    m = synth.random_model(TINY, seed=41)
+    if quantized:
+        stats = m.calibrate(synth.residue_ids([40, 60, 90], seed=42))
+        m.apply_smoothquant(stats, 0.5)
+        m.quantize_weights()
+    m.set_first_block_fc1_fp16(True)
+    gg = tmp_path / "fc1fp16.gguf"
+    m.save_to_gguf(gg)
+    dev = Model.load(gg)
+    assert dev.config.first_block_fc1_fp16
+    seqs, ids, cu = _batch([40, 3, 130, 250], 43)
+    got = dev.forward_packed(ids, cu, out=np.empty((ids.size, 33), np.float32))
+    want = O.forward_packed(dev, ids, cu)
+    O.ref_force_isa("avx512vnni")
+    try:
+        rw = O.RefModel(gg).forward_packed(ids, cu)
+    finally:
+        O.ref_force_isa(None)
+    if quantized:
+        for w in (want, rw):
+            np.testing.assert_allclose(got, w, rtol=1e-3, atol=W8A8_ATOL)
+            _pearson_each(got, w, cu)
+    else:
+        _close(got, want)
+        _close(got, rw)
+    dev.close()
+    m.close()
