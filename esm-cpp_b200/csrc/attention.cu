@@ -129,20 +129,20 @@ __global__ void __launch_bounds__(QT)
 
 cudaError_t launch_attention_tma(const float* q, const float* k, const float* v, const int* cu,
                                  int B, int H, long T, float* out, uint32_t* amax,
-                                 uint32_t* status, int num_sms, cudaStream_t s);
+                                 uint32_t* status, int num_sms, bool qk_bf16, cudaStream_t s);
 cudaError_t launch_attention_tma_pair(const float* q, const float* k, const float* v,
                                       const int* cu, int B, int H, long T, float* out,
-                                      uint32_t* amax, uint32_t* status, int num_sms,
+                                      uint32_t* amax, uint32_t* status, int num_sms, bool qk_bf16,
                                       cudaStream_t s);
 cudaError_t launch_attention_tma_long(const float* q, const float* k, const float* v,
                                       const int* cu, int B, int H, long T, int max_len, float* out,
-                                      uint32_t* amax, uint32_t* status, int num_sms,
+                                      uint32_t* amax, uint32_t* status, int num_sms, bool qk_bf16,
                                       cudaStream_t s);
 
 cudaError_t launch_attention_varlen(const float* q, const float* k, const float* v,
                                     const int* cu, int B, int H, int dh, long T, int min_len,
                                     int max_len, float* out, uint32_t* amax, uint32_t* status,
-                                    int num_sms, cudaStream_t s) {
+                                    int num_sms, cudaStream_t s, bool qk_bf16) {
   if (B <= 0 || H <= 0 || max_len <= 0) return cudaSuccess;
   if (dh <= 0 || dh > 128 || (dh & 3)) return cudaErrorInvalidValue;
   // head_dim 64: tensor cores (3xTF32) -- one CTA per (sequence, head) for
@@ -150,16 +150,18 @@ cudaError_t launch_attention_varlen(const float* q, const float* k, const float*
   // query tile) above; other head dims: FP32 SIMT.
   if (dh == 64 && status != nullptr) {
     if (min_len <= 128) {
-      cudaError_t e = launch_attention_tma(q, k, v, cu, B, H, T, out, amax, status, num_sms, s);
+      cudaError_t e =
+          launch_attention_tma(q, k, v, cu, B, H, T, out, amax, status, num_sms, qk_bf16, s);
       if (e != cudaSuccess) return e;
     }
     if (max_len > 128 && min_len <= 256) {
-      cudaError_t e = launch_attention_tma_pair(q, k, v, cu, B, H, T, out, amax, status, num_sms, s);
+      cudaError_t e =
+          launch_attention_tma_pair(q, k, v, cu, B, H, T, out, amax, status, num_sms, qk_bf16, s);
       if (e != cudaSuccess) return e;
     }
     if (max_len > 256) {
       cudaError_t e = launch_attention_tma_long(q, k, v, cu, B, H, T, max_len, out, amax, status,
-                                                num_sms, s);
+                                                num_sms, qk_bf16, s);
       if (e != cudaSuccess) return e;
     }
     return cudaSuccess;

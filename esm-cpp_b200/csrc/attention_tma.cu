@@ -225,7 +225,7 @@ __global__ void __maxnreg__(128)
                          const __grid_constant__ CUtensorMap tmK,
                          const __grid_constant__ CUtensorMap tmV, const int* __restrict__ cu,
                          int H, int n_items, float* __restrict__ out, uint32_t* amax,
-                         uint32_t* status) {
+                         uint32_t* status, int qk_bf16) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -329,8 +329,10 @@ __global__ void __maxnreg__(128)
           const uint64_t b_raw = sw128_kmajor_desc(slot + kOffKV + o);
           const uint64_t b_lo = sw128_kmajor_desc(slot + kOffLo + o);
           mma_tf32(tS, a_raw, b_raw, idS, kk > 0 ? 1u : 0u);
-          mma_tf32(tS, a_raw, b_lo, idS, 1u);
-          mma_tf32_ts(tS, tmem + kSColQlo + 8u * kk, b_raw, idS, 1u);
+          if (!qk_bf16) {  // bf16-valued Q and K are exact in tf32: no lo terms
+            mma_tf32(tS, a_raw, b_lo, idS, 1u);
+            mma_tf32_ts(tS, tmem + kSColQlo + 8u * kk, b_raw, idS, 1u);
+          }
         }
         mma_commit(&bar[kSDone + s]);
         // The next item, looked up while this one's wait is pending.
@@ -580,7 +582,7 @@ __global__ void __maxnreg__(128)
                               const __grid_constant__ CUtensorMap tmK,
                               const __grid_constant__ CUtensorMap tmV, const int* __restrict__ cu,
                               int H, int n_items, float* __restrict__ out, uint32_t* amax,
-                              uint32_t* status) {
+                              uint32_t* status, int qk_bf16) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -701,8 +703,10 @@ __global__ void __maxnreg__(128)
           const uint64_t b_raw = sw128_kmajor_desc(slot + kOffKV + o);
           const uint64_t b_lo = sw128_kmajor_desc(slot + kOffLo + o);
           mma_tf32_pair(tmem, a_raw, b_raw, idS, kk > 0 ? 1u : 0u);
-          mma_tf32_pair(tmem, a_raw, b_lo, idS, 1u);
-          mma_tf32_ts_pair(tmem, tmem + kColQlo + 8u * kk, b_raw, idS, 1u);
+          if (!qk_bf16) {  // bf16-valued Q and K are exact in tf32: no lo terms
+            mma_tf32_pair(tmem, a_raw, b_lo, idS, 1u);
+            mma_tf32_ts_pair(tmem, tmem + kColQlo + 8u * kk, b_raw, idS, 1u);
+          }
         }
         commit_both(kPSDone);
         // The next item, looked up while this one's wait is pending.
@@ -1006,7 +1010,7 @@ __global__ void __maxnreg__(128)
                               const __grid_constant__ CUtensorMap tmK,
                               const __grid_constant__ CUtensorMap tmV, const int* __restrict__ cu,
                               int H, int qtiles, int n_items, float* __restrict__ out,
-                              uint32_t* amax, uint32_t* status) {
+                              uint32_t* amax, uint32_t* status, int qk_bf16) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -1122,8 +1126,10 @@ __global__ void __maxnreg__(128)
           const uint32_t o = static_cast<uint32_t>((kk >> 2) * 16384 + (kk & 3) * 32);
           const uint64_t a_raw = sw128_kmajor_desc(q_s + o);
           mma_tf32(tS, a_raw, sw128_kmajor_desc(st + o), idS, kk > 0 ? 1u : 0u);
-          mma_tf32(tS, a_raw, sw128_kmajor_desc(st + 32768u + o), idS, 1u);
-          mma_tf32_ts(tS, tmem + kColQlo + 8u * kk, sw128_kmajor_desc(st + o), idS, 1u);
+          if (!qk_bf16) {  // bf16-valued Q and K are exact in tf32: no lo terms
+            mma_tf32(tS, a_raw, sw128_kmajor_desc(st + 32768u + o), idS, 1u);
+            mma_tf32_ts(tS, tmem + kColQlo + 8u * kk, sw128_kmajor_desc(st + o), idS, 1u);
+          }
         }
         mma_commit(&bar[kLSDone + b]);
         mma_commit(&bar[kLFree + s]);
@@ -1402,7 +1408,7 @@ bool make_tmap_rows(CUtensorMap* map, const float* base, long T, long cols,
 // longer ones elsewhere).  T = cu[B] (host-known), num_sms = grid bound.
 cudaError_t launch_attention_tma(const float* q, const float* k, const float* v, const int* cu,
                                  int B, int H, long T, float* out, uint32_t* amax,
-                                 uint32_t* status, int num_sms, cudaStream_t s) {
+                                 uint32_t* status, int num_sms, bool qk_bf16, cudaStream_t s) {
   if (B <= 0 || H <= 0 || T <= 0) return cudaSuccess;
   CUtensorMap tmQ, tmK, tmV;
   const long cols = static_cast<long>(H) * DH;
@@ -1425,14 +1431,14 @@ cudaError_t launch_attention_tma(const float* q, const float* k, const float* v,
   const int grid = static_cast<int>(std::min<long>(n_items, std::max(1, num_sms)));
   attention_tma_kernel<<<grid, kThreads, kSSmemBytes, s>>>(tmQ, tmK, tmV, cu, H,
                                                           static_cast<int>(n_items), out, amax,
-                                                          status);
+                                                          status, qk_bf16 ? 1 : 0);
   return cudaGetLastError();
 }
 
 // Every sequence of 129..256 tokens, one CTA pair per (sequence, head).
 cudaError_t launch_attention_tma_pair(const float* q, const float* k, const float* v,
                                       const int* cu, int B, int H, long T, float* out,
-                                      uint32_t* amax, uint32_t* status, int num_sms,
+                                      uint32_t* amax, uint32_t* status, int num_sms, bool qk_bf16,
                                       cudaStream_t s) {
   if (B <= 0 || H <= 0 || T <= 0) return cudaSuccess;
   CUtensorMap tmQ, tmK, tmV;
@@ -1467,7 +1473,7 @@ cudaError_t launch_attention_tma_pair(const float* q, const float* k, const floa
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, attention_tma_pair_kernel, tmQ, tmK, tmV, cu, H,
-                            static_cast<int>(n_items), out, amax, status);
+                            static_cast<int>(n_items), out, amax, status, qk_bf16 ? 1 : 0);
 }
 
 // Every sequence of more than 256 tokens: items = (sequence, head, 128-row
@@ -1475,7 +1481,7 @@ cudaError_t launch_attention_tma_pair(const float* q, const float* k, const floa
 // head); one persistent CTA per SM at most.
 cudaError_t launch_attention_tma_long(const float* q, const float* k, const float* v,
                                       const int* cu, int B, int H, long T, int max_len, float* out,
-                                      uint32_t* amax, uint32_t* status, int num_sms,
+                                      uint32_t* amax, uint32_t* status, int num_sms, bool qk_bf16,
                                       cudaStream_t s) {
   if (B <= 0 || H <= 0 || T <= 0 || max_len <= LMAX2) return cudaSuccess;
   CUtensorMap tmQ, tmK, tmV;
@@ -1499,7 +1505,7 @@ cudaError_t launch_attention_tma_long(const float* q, const float* k, const floa
   if (n_items > (1L << 30)) return cudaErrorInvalidValue;
   const int grid = static_cast<int>(std::min<long>(n_items, std::max(1, num_sms)));
   attention_tma_long_kernel<<<grid, kThreads, kLSmemBytes, s>>>(
-      tmQ, tmK, tmV, cu, H, qtiles, static_cast<int>(n_items), out, amax, status);
+      tmQ, tmK, tmV, cu, H, qtiles, static_cast<int>(n_items), out, amax, status, qk_bf16 ? 1 : 0);
   return cudaGetLastError();
 }
 

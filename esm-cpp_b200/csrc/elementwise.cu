@@ -1,6 +1,8 @@
 // Elementwise glue of the forward: GELU, residual add, Q scale, varlen RoPE,
 // the q|k|v split for the FP32 path, token positions and the embedding
 // gather with the per-sequence token-dropout rescale.
+#include <cuda_bf16.h>
+
 #include "common.cuh"
 #include "epilogue.cuh"
 #include "kernels.cuh"
@@ -32,6 +34,15 @@ __global__ void residual_kernel(float* __restrict__ y, const float* __restrict__
   for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<long>(gridDim.x) * blockDim.x)
     y[i] = __fadd_rn(y[i], x[i]);
+}
+
+// y = float(bf16(x)), round to nearest even: the Q and K of the reference's
+// opt-in BF16 attention (attention.cpp:686-700, 707-768 converts them with
+// _mm512_cvtne2ps_pbh).
+__global__ void round_bf16_kernel(const float* x, float* y, long n) {
+  for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long>(gridDim.x) * blockDim.x)
+    y[i] = __bfloat162float(__float2bfloat16_rn(x[i]));
 }
 
 // lo = x - tf32(x): the part of an fp32 operand a tf32 MMA drops (it reads
@@ -218,6 +229,12 @@ cudaError_t launch_gelu(const float* x, float* out, long n, cudaStream_t s) {
 cudaError_t launch_residual_add(float* y, const float* x, long n, cudaStream_t s) {
   if (n <= 0) return cudaSuccess;
   residual_kernel<<<grid_for(n, 256), 256, 0, s>>>(y, x, n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_round_bf16(const float* x, float* y, long n, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  round_bf16_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, y, n);
   return cudaGetLastError();
 }
 

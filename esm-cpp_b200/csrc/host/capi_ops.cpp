@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -37,6 +38,14 @@ int use_device(esmcu_context* ctx) {
     ESMCU_CUDA(cudaSetDevice(ctx->device));
   }
   return ESMCU_OK;
+}
+
+bool attention_bf16_enabled(int head_dim) {
+  if (head_dim % 32 != 0) return false;  // attention.cpp:695: FP32 otherwise
+  const char* v = std::getenv("ESM_AMX_ATTENTION");
+  if (v == nullptr) return false;
+  const std::string s = v;
+  return s == "on" || s == "1" || s == "true";
 }
 
 int ensure_scratch(esmcu_context* ctx, size_t bytes) {
@@ -418,8 +427,20 @@ int esmcu_attention_varlen(esmcu_context* ctx, const float* q, const float* k, c
     max_len = std::max(max_len, cu_h[b + 1] - cu_h[b]);
     min_len = std::min(min_len, cu_h[b + 1] - cu_h[b]);
   }
+  const bool qk_bf16 = attention_bf16_enabled(dh);
+  if (qk_bf16) {
+    // The caller's q and k stay untouched: bf16-rounded copies in scratch.
+    const size_t n = static_cast<size_t>(cu_h[B]) * H * dh;
+    ESMCU_TRY(ensure_scratch(ctx, 2 * n * sizeof(float)));
+    float* qb = static_cast<float*>(ctx->scratch);
+    float* kb = qb + n;
+    ESMCU_CUDA(launch_round_bf16(q, qb, static_cast<long>(n), ctx->stream));
+    ESMCU_CUDA(launch_round_bf16(k, kb, static_cast<long>(n), ctx->stream));
+    q = qb;
+    k = kb;
+  }
   ESMCU_CUDA(launch_attention_varlen(q, k, v, cu, B, H, dh, cu_h[B], min_len, max_len, out, nullptr,
-                                     ctx->d_status, ctx->num_sms, ctx->stream));
+                                     ctx->d_status, ctx->num_sms, ctx->stream, qk_bf16));
   return ESMCU_OK;
 }
 

@@ -38,6 +38,12 @@ int check_device_status(esmcu_context* ctx);
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+// ESM_AMX_ATTENTION = "on" | "1" | "true": the reference's opt-in BF16
+// attention (attention.cpp:686-700), Q and K rounded to bf16 before the
+// scores, for head dims that are multiples of 32.  Read at every forward (the
+// reference reads it once per process).
+bool attention_bf16_enabled(int head_dim);
+
 }  // namespace esmb200
 
 #define ESMCU_CUDA(call)                                          \

@@ -339,6 +339,7 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
   // LayerNorm + per-tensor quantisation in one kernel (no fp32 LN output)
   // unless an observer needs that output.
   const bool ln_fused = quant && !per_token && stats == nullptr && d % 128 == 0 && d <= 2048;
+  const bool qk_bf16 = attention_bf16_enabled(c.head_dim);
   LAUNCH(m, launch_positions(cu, B, pos, s));
   sec.begin("embed");
   LAUNCH(m, launch_embed(m->embed, d, ids, mk, cu, B, c.mask_token_id, hidden, s));
@@ -449,9 +450,13 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
       sec.end();
     }
     sec.begin("attention");
+    if (qk_bf16) {  // ESM_AMX_ATTENTION: Q and K (scaled, RoPE'd) rounded to bf16
+      LAUNCH(m, launch_round_bf16(q, q, static_cast<long>(Td), s));
+      LAUNCH(m, launch_round_bf16(k, k, static_cast<long>(Td), s));
+    }
     LAUNCH(m, launch_attention_varlen(q, k, v, cu, B, H, dh, T, a.min_len, max_len, attn,
                                       (quant && !per_token) ? am + 1 * kAmaxSlots : nullptr,
-                                      ctx->d_status, ctx->num_sms, s));
+                                      ctx->d_status, ctx->num_sms, s, qk_bf16));
     sec.end();
     observe(li, 1, attn, Td);
     if (quant) {

@@ -144,11 +144,12 @@ cudaError_t launch_layernorm_quant(const float* x, const float* g, const float* 
 // Optional absmax of out into *amax.  head_dim 64 runs on the tensor cores
 // (needs the status word): one CTA per (sequence, head) for L <= 128, a CTA
 // pair for 128 < L <= 256, one CTA per (sequence, head, 128-row query tile)
-// above; other head dims on FP32 SIMT.
+// above; other head dims on FP32 SIMT.  qk_bf16: q and k hold bf16 values
+// (launch_round_bf16), so S needs no lo terms on the tensor cores.
 cudaError_t launch_attention_varlen(const float* q, const float* k, const float* v,
                                     const int* cu, int B, int H, int dh, long T, int min_len,
                                     int max_len, float* out, uint32_t* amax, uint32_t* status,
-                                    int num_sms, cudaStream_t s);
+                                    int num_sms, cudaStream_t s, bool qk_bf16 = false);
 
 // ------------------------------------------------------------- elementwise
 cudaError_t launch_gelu(const float* x, float* out, long n, cudaStream_t s);
@@ -160,6 +161,8 @@ cudaError_t launch_rope_varlen(float* x, const float* cos_t, const float* sin_t,
 cudaError_t launch_split_qkv_rope(const float* qkv, float* q, float* k, float* v, int T,
                                   int d, int H, int dh, const int* pos, const float* cos_t,
                                   const float* sin_t, float q_scale, cudaStream_t s);
+// y = float(bf16(x)), round to nearest even (y may equal x).
+cudaError_t launch_round_bf16(const float* x, float* y, long n, cudaStream_t s);
 // Token -> position inside its sequence, from cu_seqlens.
 cudaError_t launch_positions(const int* cu, int B, int* pos, cudaStream_t s);
 // out [R, d] = x[rows[r]] (rows must index rows of x).

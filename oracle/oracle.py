@@ -248,7 +248,26 @@ def rope_apply_varlen(x, cos_t, sin_t, cu, H, dh, fused=True):
     return x
 
 
-def attention_varlen(q, k, v, cu, H, dh):
+def round_bf16(x):
+    """float32 -> nearest bfloat16 value (ties to even), kept as float32: the
+    conversion of the reference's BF16 attention (attention.cpp:707-768,
+    _mm512_cvtne2ps_pbh).  NaN stays NaN."""
+    x = _a(x)
+    b = x.view(np.uint32).astype(np.uint64)
+    r = ((b + 0x7FFF + ((b >> 16) & 1)) & 0xFFFF0000).astype(np.uint32).view(F32)
+    return np.where(np.isnan(x), x, r).astype(F32)
+
+
+def attention_bf16_enabled(dh: int) -> bool:
+    """ESM_AMX_ATTENTION (attention.cpp:686-700), for head dims % 32 == 0."""
+    return dh % 32 == 0 and os.environ.get("ESM_AMX_ATTENTION", "") in ("on", "1", "true")
+
+
+def attention_varlen(q, k, v, cu, H, dh, bf16: bool = False):
+    """AttentionVarlenRef; with bf16, Q and K rounded to bfloat16 first (the
+    reference's opt-in BF16 attention: exact bf16 products, fp32 sums)."""
+    if bf16:
+        q, k = round_bf16(q), round_bf16(k)
     q, k, v, cu = _a(q), _a(k), _a(v), _a(cu, np.int32)
     out = np.zeros_like(q)
     orc().orc_attention_varlen(q.ctypes.data, k.ctypes.data, v.ctypes.data, cu.ctypes.data,
@@ -312,7 +331,7 @@ def forward_packed(model, ids, cu, masks=None, per_token: bool = False, hidden=N
         q = (q * qs).astype(F32)
         q = rope_apply_varlen(q, cos_t, sin_t, cu, H, dh, fused=True)
         k = rope_apply_varlen(k, cos_t, sin_t, cu, H, dh, fused=True)
-        att = attention_varlen(q, k, v, cu, H, dh)
+        att = attention_varlen(q, k, v, cu, H, dh, bf16=attention_bf16_enabled(dh))
         h = (h + lin(att, lw, "out")).astype(F32)
         ln = layernorm(h, lw["ffn_ln_w"], lw["ffn_ln_b"], c.layer_norm_eps)
         if li == 0 and getattr(c, "first_block_fc1_fp16", False):

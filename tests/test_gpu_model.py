@@ -372,3 +372,22 @@ def test_first_block_fc1_fp16_matches_oracle_and_reference(O, R, tmp_path, cuda,
         _close(got, rw)
     dev.close()
     m.close()
+
+
+@pytest.mark.parametrize("which", ["fp32", "q8"])
+def test_bf16_attention_forward_matches_oracle(which, tiny_fp32, tiny_q8, O, monkeypatch):
+    """ESM_AMX_ATTENTION=on through the whole forward: Q and K rounded to bf16
+    after the scale and RoPE, as the reference's AttentionVarlenAvx512Bf16
+    does, against the oracle's forward with the same switch."""
+    m = tiny_fp32 if which == "fp32" else tiny_q8
+    seqs, ids, cu = _batch([40, 3, 130, 300], 52)
+    off = m.forward_packed(ids, cu, out=np.empty((ids.size, 33), np.float32))
+    monkeypatch.setenv("ESM_AMX_ATTENTION", "on")
+    got = m.forward_packed(ids, cu, out=np.empty((ids.size, 33), np.float32))
+    want = O.forward_packed(m, ids, cu)
+    if which == "fp32":
+        _close(got, want)
+        assert np.abs(got - off).max() > 1e-5
+    else:
+        np.testing.assert_allclose(got, want, rtol=1e-3, atol=W8A8_ATOL)
+        _pearson_each(got, want, cu)

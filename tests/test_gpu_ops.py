@@ -125,6 +125,31 @@ def test_attention_varlen_matches_oracle(cuda, O, lens, H, dh):
     _close(out.cpu().numpy(), O.attention_varlen(q, k, v, cu, H, dh))
 
 
+def test_attention_bf16_mode_matches_oracle(cuda, O, monkeypatch):
+    """ESM_AMX_ATTENTION=on (attention.cpp:686-700): Q and K rounded to bf16
+    (round to nearest even) before the scores, on all three tensor-core
+    kernels (<= 128, 129..256, > 256 tokens); S then needs one tf32 MMA
+    per k-step.  head_dim 16 is not a multiple of 32 and stays FP32, as in
+    the reference.  The caller's q and k are not modified."""
+    from esm_b200 import ops
+
+    monkeypatch.setenv("ESM_AMX_ATTENTION", "on")
+    rng = np.random.default_rng(71)
+    for lens, H, dh in (([90, 3, 200, 402, 129, 1], 8, 64), ([33, 70], 2, 16)):
+        cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+        T = int(cu[-1])
+        q, k, v = (rng.standard_normal((3, T, H, dh)).astype(np.float32))
+        q *= np.float32(1.0 / np.sqrt(dh))
+        tq, tk = _t(q, cuda), _t(k, cuda)
+        out = ops.attention_varlen(tq, tk, _t(v, cuda), _t(cu, cuda), H, dh)
+        ops.synchronize()
+        assert np.array_equal(tq.cpu().numpy(), q) and np.array_equal(tk.cpu().numpy(), k)
+        bf16 = dh % 32 == 0
+        _close(out.cpu().numpy(), O.attention_varlen(q, k, v, cu, H, dh, bf16=bf16))
+        if bf16:
+            assert np.abs(out.cpu().numpy() - O.attention_varlen(q, k, v, cu, H, dh)).max() > 1e-4
+
+
 def test_attention_matches_reference_avx512(cuda, O, R):
     from esm_b200 import ops
 
