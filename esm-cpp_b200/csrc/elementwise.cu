@@ -100,7 +100,7 @@ __global__ void split_qkv_rope_kernel(const float* __restrict__ qkv, float* __re
                                       float* __restrict__ k, float* __restrict__ v, int T, int d,
                                       int H, int dh, const int* __restrict__ pos,
                                       const float* __restrict__ cos_t,
-                                      const float* __restrict__ sin_t, float q_scale) {
+                                      const float* __restrict__ sin_t, float q_scale, int qk_bf16) {
   const int half = dh / 2;
   const long total = static_cast<long>(T) * H * half;
   for (long w = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; w < total;
@@ -115,13 +115,15 @@ __global__ void split_qkv_rope_kernel(const float* __restrict__ qkv, float* __re
     const float c = __ldg(cos_t + static_cast<long>(p) * dh + i);
     const float s = __ldg(sin_t + static_cast<long>(p) * dh + i);
     // q: scale before RoPE (model.cpp:976-988)
+    // ESM_AMX_ATTENTION: q and k stored rounded to bf16.
+    auto st = [qk_bf16](float x) { return qk_bf16 ? __bfloat162float(__float2bfloat16_rn(x)) : x; };
     float lo = __fmul_rn(src[i], q_scale), hi = __fmul_rn(src[i + half], q_scale);
-    q[o + i] = __fmaf_rn(-hi, s, __fmul_rn(lo, c));
-    q[o + i + half] = __fmaf_rn(hi, c, __fmul_rn(lo, s));
+    q[o + i] = st(__fmaf_rn(-hi, s, __fmul_rn(lo, c)));
+    q[o + i + half] = st(__fmaf_rn(hi, c, __fmul_rn(lo, s)));
     lo = src[d + i];
     hi = src[d + i + half];
-    k[o + i] = __fmaf_rn(-hi, s, __fmul_rn(lo, c));
-    k[o + i + half] = __fmaf_rn(hi, c, __fmul_rn(lo, s));
+    k[o + i] = st(__fmaf_rn(-hi, s, __fmul_rn(lo, c)));
+    k[o + i + half] = st(__fmaf_rn(hi, c, __fmul_rn(lo, s)));
     v[o + i] = src[2 * d + i];
     v[o + i + half] = src[2 * d + i + half];
   }
@@ -260,11 +262,12 @@ cudaError_t launch_rope_varlen(float* x, const float* cos_t, const float* sin_t,
 
 cudaError_t launch_split_qkv_rope(const float* qkv, float* q, float* k, float* v, int T, int d,
                                   int H, int dh, const int* pos, const float* cos_t,
-                                  const float* sin_t, float q_scale, cudaStream_t s) {
+                                  const float* sin_t, float q_scale, cudaStream_t s,
+                                  bool qk_bf16) {
   if (T <= 0) return cudaSuccess;
   const long work = static_cast<long>(T) * H * (dh / 2);
   split_qkv_rope_kernel<<<grid_for(work, 256), 256, 0, s>>>(qkv, q, k, v, T, d, H, dh, pos,
-                                                            cos_t, sin_t, q_scale);
+                                                            cos_t, sin_t, q_scale, qk_bf16 ? 1 : 0);
   return cudaGetLastError();
 }
 

@@ -3,6 +3,8 @@
 // optional running absmax of what was stored.
 #pragma once
 
+#include <cuda_bf16.h>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -134,6 +136,10 @@ __device__ __forceinline__ void epi_qkv_rope_values(const EpiParams& e, uint32_t
         f2_unpack(f2_fma(hi, c2[k], f2_mul(lo, s2[k])), y[i + 32], y[i + 33]);
       }
     }
+    if (e.qk_bf16) {
+#pragma unroll
+      for (int j = 0; j < 64; ++j) y[j] = __bfloat162float(__float2bfloat16_rn(y[j]));
+    }
   }
 }
 
@@ -160,6 +166,10 @@ __device__ __forceinline__ void epi_qkv_rope_head(const EpiParams& e, long m, in
       const float ci = __ldg(c + i), si = __ldg(s + i);
       y[i] = __fmaf_rn(-hi, si, __fmul_rn(lo, ci));
       y[i + 32] = __fmaf_rn(hi, ci, __fmul_rn(lo, si));
+    }
+    if (e.qk_bf16) {
+#pragma unroll
+      for (int j = 0; j < 64; ++j) y[j] = __bfloat162float(__float2bfloat16_rn(y[j]));
     }
   }
 #pragma unroll

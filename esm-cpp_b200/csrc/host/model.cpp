@@ -430,6 +430,7 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
         e.cos_t = m->cos_t;
         e.sin_t = m->sin_t;
         e.q_scale = q_scale;
+        e.qk_bf16 = qk_bf16 ? 1 : 0;
       } else {
         e.kind = kEpiStore;
         e.C = qkv;
@@ -446,14 +447,13 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
     sec.end();
     if (!fused_rope) {
       sec.begin("q_scale_rope");
-      LAUNCH(m, launch_split_qkv_rope(qkv, q, k, v, T, d, H, dh, pos, m->cos_t, m->sin_t, q_scale, s));
+      LAUNCH(m, launch_split_qkv_rope(qkv, q, k, v, T, d, H, dh, pos, m->cos_t, m->sin_t, q_scale, s,
+                                      qk_bf16));
       sec.end();
     }
     sec.begin("attention");
-    if (qk_bf16) {  // ESM_AMX_ATTENTION: Q and K (scaled, RoPE'd) rounded to bf16
-      LAUNCH(m, launch_round_bf16(q, q, static_cast<long>(Td), s));
-      LAUNCH(m, launch_round_bf16(k, k, static_cast<long>(Td), s));
-    }
+    // With ESM_AMX_ATTENTION, q and k arrive rounded to bf16 from the QKV
+    // epilogue or the split kernel.
     LAUNCH(m, launch_attention_varlen(q, k, v, cu, B, H, dh, T, a.min_len, max_len, attn,
                                       (quant && !per_token) ? am + 1 * kAmaxSlots : nullptr,
                                       ctx->d_status, ctx->num_sms, s, qk_bf16));

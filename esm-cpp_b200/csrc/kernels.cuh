@@ -39,6 +39,9 @@ struct EpiParams {
   const float* cos_t = nullptr;  // [max_len, 64]
   const float* sin_t = nullptr;
   float q_scale = 1.0f;
+  // kEpiQkvRope: q and k stored rounded to bf16 (round to nearest even), the
+  // opt-in BF16 attention of the reference (ESM_AMX_ATTENTION).
+  int qk_bf16 = 0;
 };
 
 // ---------------------------------------------------------------- INT8 GEMM
@@ -160,7 +163,8 @@ cudaError_t launch_rope_varlen(float* x, const float* cos_t, const float* sin_t,
 // qkv [T, 3d] -> q, k, v [T, d]; q *= q_scale; RoPE on q and k.
 cudaError_t launch_split_qkv_rope(const float* qkv, float* q, float* k, float* v, int T,
                                   int d, int H, int dh, const int* pos, const float* cos_t,
-                                  const float* sin_t, float q_scale, cudaStream_t s);
+                                  const float* sin_t, float q_scale, cudaStream_t s,
+                                  bool qk_bf16 = false);
 // y = float(bf16(x)), round to nearest even (y may equal x).
 cudaError_t launch_round_bf16(const float* x, float* y, long n, cudaStream_t s);
 // Token -> position inside its sequence, from cu_seqlens.
