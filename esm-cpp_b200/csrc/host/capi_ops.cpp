@@ -267,6 +267,22 @@ int esmcu_quantize_activations(esmcu_context* ctx, const float* A, int M, int K,
   return ESMCU_OK;
 }
 
+int esmcu_quantize_weights(esmcu_context* ctx, const float* W, int N, int K, int8_t* q,
+                           float* scales) {
+  ESMCU_TRY(use_device(ctx));
+  if (N < 0 || K < 0) return fail(ESMCU_ERR_INVALID_ARGUMENT, "bad shape");
+  if (N == 0) return ESMCU_OK;
+  ESMCU_TRY(check_ptr(scales, "scales"));
+  if (K == 0) {  // every row is all-zero: scale 0
+    ESMCU_CUDA(cudaMemsetAsync(scales, 0, static_cast<size_t>(N) * sizeof(float), ctx->stream));
+    return ESMCU_OK;
+  }
+  ESMCU_TRY(check_ptr(W, "W"));
+  ESMCU_TRY(check_ptr(q, "q"));
+  ESMCU_CUDA(launch_quantize_weights(W, N, K, q, scales, ctx->stream));
+  return ESMCU_OK;
+}
+
 int esmcu_gemm_int8_s32(esmcu_context* ctx, const int8_t* q, int ldq, const int8_t* W, int ldw,
                         int32_t* acc, int M, int N, int K) {
   ESMCU_TRY(use_device(ctx));

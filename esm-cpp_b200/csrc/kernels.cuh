@@ -115,6 +115,10 @@ cudaError_t launch_quantize_per_tensor(const float* x, long ldx, int M, int K,
 cudaError_t launch_quantize_per_token(const float* x, long ldx, int M, int K, int8_t* q,
                                       long ldq, float* row_scales, cudaStream_t s);
 cudaError_t launch_absmax(const float* x, long n, uint32_t* amax_bits, cudaStream_t s);
+// quant::Quantize of weights W [N, K] (dense rows) -> q [N, K] int8 and
+// per-row scales [N].
+cudaError_t launch_quantize_weights(const float* W, int N, int K, int8_t* q, float* scale,
+                                    cudaStream_t s);
 // x = float(half(x)) in place (round to nearest even); optional absmax of the
 // rounded values into amax_bits.
 cudaError_t launch_round_fp16(float* x, long n, uint32_t* amax_bits, cudaStream_t s);

@@ -111,6 +111,36 @@ __global__ void round_fp16_kernel(float* __restrict__ x, long n, uint32_t* amax_
   if (amax_bits != nullptr) amax_publish(amax_bits, mx);
 }
 
+// quant::Quantize (pack.cpp:149-177): per output channel (row) n,
+// scale = max|W[n,:]| / 127 (IEEE divide), inv = 1 / scale, q = clamp(
+// rne(w * inv), +-127); an all-zero row gets scale 0 and zero codes.  One warp
+// per row; the max is order-free, so the codes and scales are bit-identical
+// to the reference's.
+__global__ void quantize_weight_rows_kernel(const float* __restrict__ W, int N, int K,
+                                            int8_t* __restrict__ q, float* __restrict__ scale) {
+  const int warps = static_cast<int>(blockDim.x >> 5), lane = static_cast<int>(threadIdx.x & 31);
+  for (long n = static_cast<long>(blockIdx.x) * warps + (threadIdx.x >> 5); n < N;
+       n += static_cast<long>(gridDim.x) * warps) {
+    const float* row = W + n * K;
+    int8_t* qr = q + n * K;
+    float mx = 0.0f;
+    for (int k = lane; k < K; k += 32) mx = fmaxf(mx, fabsf(row[k]));
+    mx = warp_max(mx);
+    if (mx == 0.0f) {
+      if (lane == 0) scale[n] = 0.0f;
+      for (int k = lane; k < K; k += 32) qr[k] = 0;
+      continue;
+    }
+    const float sc = __fdiv_rn(mx, 127.0f);
+    const float inv = __fdiv_rn(1.0f, sc);
+    if (lane == 0) scale[n] = sc;
+    for (int k = lane; k < K; k += 32) {
+      const float v = fminf(fmaxf(rintf(__fmul_rn(row[k], inv)), -127.0f), 127.0f);
+      qr[k] = static_cast<int8_t>(static_cast<int>(v));
+    }
+  }
+}
+
 int grid_for(long work, int block) {
   long g = (work + block - 1) / block;
   if (g > 148L * 16) g = 148L * 16;
@@ -137,6 +167,14 @@ cudaError_t launch_quantize_per_token(const float* x, long ldx, int M, int K, in
   const long threads = static_cast<long>(M) * 32;
   quantize_per_token_kernel<<<static_cast<int>((threads + 255) / 256), 256, 0, s>>>(
       x, ldx, M, K, q, ldq, row_scales);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_weights(const float* W, int N, int K, int8_t* q, float* scale,
+                                    cudaStream_t s) {
+  if (N <= 0 || K <= 0) return cudaSuccess;
+  quantize_weight_rows_kernel<<<grid_for(static_cast<long>(N) * 32, 256), 256, 0, s>>>(W, N, K, q,
+                                                                                     scale);
   return cudaGetLastError();
 }
 

@@ -77,6 +77,7 @@ _SIGS = {
                                             C.c_int, C.c_int]),
     "esmcu_quantize_activations": (C.c_int, [_VP, _VP, C.c_int, C.c_int, _VP, C.c_int, _VP,
                                              C.c_int]),
+    "esmcu_quantize_weights": (C.c_int, [_VP, _VP, C.c_int, C.c_int, _VP, _VP]),
     "esmcu_gemm_int8_s32": (C.c_int, [_VP, _VP, C.c_int, _VP, C.c_int, _VP, C.c_int, C.c_int,
                                       C.c_int]),
     "esmcu_layernorm": (C.c_int, [_VP, _VP, _VP, _VP, C.c_float, _VP, C.c_int, C.c_int]),

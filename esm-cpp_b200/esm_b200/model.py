@@ -239,20 +239,33 @@ class Model:
         self._dirty = True
 
     # ------------------------------------------------------- quantisation
-    def quantize_weights(self) -> None:
+    def quantize_weights(self, on_device: bool = False) -> None:
         """model.cpp:1470-1494: per-layer Linears to per-channel int8, and
         lm_head.dense too when ESM_QUANTIZE_LM_HEAD is set to anything but
         "", "0" or "off" (model.cpp:1487-1492; the LM head's LayerNorm and the
-        tied decoder stay FP32)."""
+        tied decoder stay FP32).  on_device=True runs quant::Quantize on this
+        model's GPU (esmcu_quantize_weights) instead of numpy; the codes and
+        scales are the same bits."""
         if self._cfg.weights_quantized:
             return
+        quant = quantize_weight
+        if on_device:
+            import torch
+
+            from . import ops
+
+            dev = torch.device("cuda", self.device)
+
+            def quant(w):
+                q, s = ops.quantize_weights(torch.from_numpy(np.ascontiguousarray(w, F32)).to(dev))
+                return q.cpu().numpy(), s.cpu().numpy()
         for lw in self.layers:
             for n in LINEARS:
-                q, s = quantize_weight(lw[n + "_w"])
+                q, s = quant(lw[n + "_w"])
                 lw[n + "_wq"], lw[n + "_ws"] = q, s
         env = os.environ.get("ESM_QUANTIZE_LM_HEAD")
         if env and env not in ("0", "off"):
-            self.head["lm_dense_wq"], self.head["lm_dense_ws"] = quantize_weight(self.head["lm_dense_w"])
+            self.head["lm_dense_wq"], self.head["lm_dense_ws"] = quant(self.head["lm_dense_w"])
             self._cfg.lm_head_dense_quantized = True
         self._cfg.weights_quantized = True
         self._dirty = True

@@ -76,6 +76,19 @@ def quantize_activations(A, act_quant: int = _lib.ACT_PER_TENSOR):
     return q, s
 
 
+def quantize_weights(W):
+    """quant::Quantize on the device: W [N, K] float32 -> (q int8 [N, K],
+    scales float32 [N]), bit-identical to prep.quantize_weight."""
+    import torch
+
+    W = W.contiguous()
+    N, K = W.shape
+    q = torch.empty((N, K), dtype=torch.int8, device=W.device)
+    s = torch.empty((N,), dtype=torch.float32, device=W.device)
+    _lib.call("esmcu_quantize_weights", context(_dev(W)), _p(W), N, K, _p(q), _p(s))
+    return q, s
+
+
 def gemm_int8_s32(q, Wq):
     """int32 acc [M,N] = q [M,K] . Wq [N,K]^T on the tensor cores."""
     import torch

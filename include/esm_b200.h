@@ -119,6 +119,13 @@ int esmcu_quantize_activations(esmcu_context* ctx, const float* A, int M, int K,
                                int ldq, float* scales_out, int act_quant);
 int esmcu_gemm_int8_s32(esmcu_context* ctx, const int8_t* q, int ldq, const int8_t* W, int ldw,
                         int32_t* acc, int M, int N, int K);
+/* quant::Quantize (quant.h:17-56; pack.cpp:149-177) on the device: W [N, K]
+ * fp32 (dense rows) -> q [N, K] int8 and per-output-channel scales [N],
+ * scale = max|row| / 127, q = clamp(rne(w * (1/scale)), +-127), an all-zero
+ * row scale 0; bit-identical to the reference.  Asynchronous on the context
+ * stream, device pointers. */
+int esmcu_quantize_weights(esmcu_context* ctx, const float* W, int N, int K, int8_t* q,
+                           float* scales);
 
 /* kernels.h:32-33 LayerNorm over rows of width d. */
 int esmcu_layernorm(esmcu_context* ctx, const float* x, const float* gamma, const float* beta,

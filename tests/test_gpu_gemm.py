@@ -122,3 +122,44 @@ def test_config2_full_size_sampled_rows(cuda, O, N, K):
     assert np.array_equal(q.cpu().numpy(), q_ref)
     rows = np.sort(rng.choice(M, 64, replace=False))
     assert np.array_equal(acc.cpu().numpy()[rows], O.gemm_i8_s32(q_ref[rows], Wq))
+
+
+@pytest.mark.parametrize("N,K", [(1, 1), (7, 33), (257, 1000), (3840, 1280)])
+def test_quantize_weights_on_device_bit_exact(cuda, O, N, K):
+    """esmcu_quantize_weights = quant::Quantize (pack.cpp:149-177): codes and
+    scales bit-identical to the numpy restatement and the oracle's C one,
+    including all-zero rows (scale 0), rounding ties and outlier rows."""
+    import torch
+
+    from esm_b200 import ops
+    from esm_b200.prep import quantize_weight
+
+    rng = np.random.default_rng(N * 31 + K)
+    W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    W[:: max(N // 3, 1)] *= 50.0                      # outlier rows
+    if N > 2:
+        W[1] = 0.0                                    # all-zero row
+        W[2, :] = np.float32(1.0)                     # ties: w * inv = 127 exactly
+        W[2, :: 2] = np.float32(0.5 / 127.0)           # and a half-step (rne)
+    q, s = ops.quantize_weights(torch.from_numpy(W).to(cuda))
+    q, s = q.cpu().numpy(), s.cpu().numpy()
+    qh, sh = quantize_weight(W)
+    qo, so = O.quantize_weights(W)
+    assert np.array_equal(q, qh) and np.array_equal(s, sh)
+    assert np.array_equal(q, qo) and np.array_equal(s, so)
+
+
+def test_model_quantize_weights_on_device_matches_host(cuda):
+    from esm_b200 import synth
+
+    arch = dict(num_hidden_layers=2, hidden_size=128, num_attention_heads=2, head_dim=64,
+                intermediate_size=512)
+    a, b = synth.random_model(arch, seed=61), synth.random_model(arch, seed=61)
+    a.quantize_weights()
+    b.quantize_weights(on_device=True)
+    for la, lb in zip(a.layers, b.layers):
+        for n in ("q", "k", "v", "out", "fc1", "fc2"):
+            assert np.array_equal(la[n + "_wq"], lb[n + "_wq"])
+            assert np.array_equal(la[n + "_ws"], lb[n + "_ws"])
+    a.close()
+    b.close()
