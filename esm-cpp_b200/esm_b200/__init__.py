@@ -12,6 +12,7 @@ reference's Python API.
 from ._lib import ACT_PER_TENSOR, ACT_PER_TOKEN, EsmCudaError, lib  # noqa: F401
 from .model import (CLS_ID, EOS_ID, MASK_ID, PAD_ID, VOCAB_SIZE, ActivationObserver,  # noqa: F401
                     Config, Model, forward_scheduled_multi)
+from .streaming import StreamingScheduler  # noqa: F401
 
 __version__ = "0.1.0"
 

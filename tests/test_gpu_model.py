@@ -391,3 +391,22 @@ def test_bf16_attention_forward_matches_oracle(which, tiny_fp32, tiny_q8, O, mon
     else:
         np.testing.assert_allclose(got, want, rtol=1e-3, atol=W8A8_ATOL)
         _pearson_each(got, want, cu)
+
+
+def test_streaming_scheduler_matches_forward_scheduled(tiny_fp32):
+    """esm_b200.streaming over two replicas (both on device 0 here): every
+    request's logits equal its rows of one forward_scheduled over all the
+    sequences (FP32: batch mates change nothing beyond rounding)."""
+    from esm_b200 import Model, synth
+    from esm_b200.streaming import StreamingScheduler
+
+    other = Model(tiny_fp32.config, tiny_fp32.embed, tiny_fp32.layers, tiny_fp32.head, device=0)
+    seqs = synth.residue_ids(synth.varlen_lengths(60, seed=81, mean=60, sd=40, lo=3, hi=300), seed=82)
+    want = tiny_fp32.forward_scheduled(seqs)
+    with StreamingScheduler([tiny_fp32, other], max_tokens=1500, max_wait_ms=2) as s:
+        futs = s.submit_many(seqs)
+        got = [f.result(timeout=60) for f in futs]
+    for g, w in zip(got, want):
+        assert g.shape == w.shape
+        _close(g, w, tol=1e-5)
+    other.close()
