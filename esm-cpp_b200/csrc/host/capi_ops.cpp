@@ -432,8 +432,8 @@ int esmcu_attention_varlen(esmcu_context* ctx, const float* q, const float* k, c
   ESMCU_TRY(check_ptr(v, "v"));
   ESMCU_TRY(check_ptr(cu, "cu_seqlens"));
   ESMCU_TRY(check_ptr(out, "out"));
-  // The sequence lengths decide the kernel (tensor cores up to 256 tokens),
-  // so read cu_seqlens back once.
+  // The sequence lengths decide the kernels (one per length class), so read
+  // cu_seqlens back once.
   std::vector<int> cu_h(static_cast<size_t>(B) + 1);
   ESMCU_CUDA(cudaMemcpyAsync(cu_h.data(), cu, cu_h.size() * sizeof(int), cudaMemcpyDeviceToHost,
                              ctx->stream));

@@ -145,7 +145,9 @@ int esmcu_rope_apply_varlen(esmcu_context* ctx, float* x, const float* cos_t,
                             const float* sin_t, const int* cu_seqlens, int batch_size,
                             int num_heads, int head_dim);
 /* kernels.h:119-121 AttentionVarlen: q (pre-scaled, RoPE'd), k, v, out
- * [T, H, dh]; per-sequence softmax attention over cu_seqlens. */
+ * [T, H, dh]; per-sequence softmax attention over cu_seqlens.  With
+ * ESM_AMX_ATTENTION=on and head_dim % 32 == 0, q and k are rounded to bf16
+ * first, in scratch (attention.cpp:686-700); the inputs are not modified. */
 int esmcu_attention_varlen(esmcu_context* ctx, const float* q, const float* k, const float* v,
                            const int* cu_seqlens, int batch_size, int num_heads, int head_dim,
                            float* out);
