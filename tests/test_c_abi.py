@@ -122,3 +122,19 @@ def test_bad_arguments_are_rejected_without_a_device():
 
     with pytest.raises(EsmCudaError):
         ops.rope_build_tables(4, 3)  # odd head_dim
+
+
+def test_model_entry_points_reject_null_handles_without_a_device():
+    """The model-level entry points added for hidden states, scoring, the
+    INT8 LM head, the fc1 fp16 flag and device quantisation return
+    ESMCU_ERR_INVALID_ARGUMENT for a null handle before touching a device."""
+    from esm_b200 import _lib
+
+    L = _lib.lib()
+    bad = 1  # ESMCU_ERR_INVALID_ARGUMENT
+    assert L.esmcu_model_forward_hidden_states(None, None, None, 0, None, 0, None, None) == bad
+    assert L.esmcu_model_masked_marginals(None, None, None, None, None, 1, 1.2, 256, None) == bad
+    assert L.esmcu_model_set_head_int8(None, None, None) == bad
+    assert L.esmcu_model_set_first_block_fc1_fp16(None, 1) == bad
+    assert L.esmcu_quantize_weights(None, None, 4, 4, None, None) == bad
+    assert L.esmcu_last_error()
