@@ -21,6 +21,18 @@ def version() -> str:
     return lib().esmcu_version().decode()
 
 
+def current_isa() -> str:
+    """esm_cpp.current_isa (the ISA the reference's kernels dispatch to): here
+    always the one target these kernels are built for."""
+    return "sm_100a"
+
+
+def host_isa() -> str:
+    """esm_cpp.host_isa: the best ISA the machine offers; for this engine
+    the same as current_isa (there is no other path)."""
+    return "sm_100a"
+
+
 def device_count() -> int:
     import ctypes
 

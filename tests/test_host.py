@@ -134,3 +134,11 @@ def test_synthetic_workloads_have_baseline_shapes():
     assert all(s[0] == 0 and s[-1] == 2 and s[1:-1].min() >= 4 and s[1:-1].max() <= 23 for s in seqs)
     dms = synth.dms_sequences(0, length=10)
     assert len(dms) == 1 + 19 * 10 and all(len(s) == 12 for s in dms)
+
+
+def test_isa_queries():
+    """esm_cpp.current_isa / host_isa (_core.cpp:83-89): this engine has one
+    target."""
+    import esm_b200
+
+    assert esm_b200.current_isa() == esm_b200.host_isa() == "sm_100a"
