@@ -1,5 +1,14 @@
-// Packed-varlen attention for sequences of at most 128 tokens (head_dim 64)
-// on the tcgen05 tensor cores, FP32-accurate (3xTF32), fed by TMA.
+// Packed-varlen attention (head_dim 64) on the tcgen05 tensor cores,
+// FP32-accurate (3xTF32), fed by TMA.  Three kernels by sequence length:
+//   attention_tma_kernel       L <= 128: one CTA per (sequence, head)
+//   attention_tma_pair_kernel  129..256: one CTA pair (cta_group::2) per
+//                              (sequence, head)
+//   attention_tma_long_kernel  > 256: one CTA per (sequence, head, 128-row
+//                              query tile), two passes over 128-key blocks
+// With qk_bf16 (the reference's opt-in BF16 attention) Q and K already hold
+// bf16 values, which tf32 represents exactly: S needs no lo terms.  The
+// description below is the single-CTA kernel's; the other two follow it and
+// say where they differ.
 //
 // Same contract as the reference's AttentionVarlen (attention.cpp:99-144):
 // q pre-scaled and RoPE'd, per-sequence softmax over cu_seqlens, exact
