@@ -16,6 +16,9 @@ Every array is produced by a reference entry point named in the key:
              tensors are stored alongside) and of the same model in FP32.
   hidden_*   Model::ForwardWithHiddenStates of that model, FP32 and W8A8
              (hidden_golden.npz), one sequence at a time, concatenated.
+  optin_golden.npz  the opt-in paths on that model: INT8 LM head, the
+             layer-0 fc1 fp16 flag, BF16 attention, masked-marginal
+             log-probabilities.
 """
 from __future__ import annotations
 
@@ -166,10 +169,99 @@ def hidden_fixture(path, model_path):
     np.savez_compressed(path, **out)
 
 
+def bf16_attention_inputs():
+    """Seeded q (scaled by 1/8), k, v [T, 2, 64] and cu for the BF16-attention
+    fixture: lengths 60, 7, 270, 1."""
+    rng = np.random.default_rng(96)
+    H, dh = 2, 64
+    cu = np.concatenate([[0], np.cumsum([60, 7, 270, 1])]).astype(np.int32)
+    q, k, v = rng.standard_normal((3, int(cu[-1]), H, dh)).astype(F32)
+    q *= F32(0.125)
+    return q, k, v, cu, H, dh
+
+
+def optin_fixture(path, model_path):
+    """The reference's opt-in paths on the tiny model of `model_fixture`:
+    ESM_QUANTIZE_LM_HEAD=on logits of its calibrated, migrated model
+    (model.cpp:1487-1492, 1209-1211); the
+    logits of a GGUF carrying esm.first_block_fc1_fp16 (model.cpp:250-254,
+    1031-1033); ESM_AMX_ATTENTION=on attention (attention.cpp:686-700, run in
+    a child process: the reference reads the variable once per process); and
+    masked-marginal log-probabilities from its ForwardScheduled
+    (eval/proteingym.py:75-98).  Logits use the VNNI ISA (one activation
+    scale per operand)."""
+    import os
+    import subprocess
+
+    from esm_b200 import Model, synth
+
+    M = np.load(model_path)
+    ids, cu = M["ids"], M["cu"]
+    out = {}
+    with tempfile.TemporaryDirectory() as td:
+        st = Path(td) / "m.safetensors"
+        st.write_bytes(M["safetensors"].tobytes())
+        # INT8 LM head, on the calibrated + migrated model of model_fixture
+        # (same calibration, so the layers equal gguf_q8's and match the
+        # oracle to the FP32 class; SmoothQuant leaves lm_head.dense alone)
+        ref = O.RefModel(st)
+        ref.calibrate_smoothquant(synth.residue_ids([30, 60], seed=79), 99.9, 0.5)
+        os.environ["ESM_QUANTIZE_LM_HEAD"] = "on"
+        try:
+            ref.quantize()
+        finally:
+            del os.environ["ESM_QUANTIZE_LM_HEAD"]
+        O.ref_force_isa("avx512vnni")
+        out["lmhead8_logits"] = ref.forward_packed(ids, cu)
+        # layer-0 fc1 fp16 flag, travelling in a GGUF this package writes
+        m = Model.load(st)
+        m.quantize_weights()
+        m.set_first_block_fc1_fp16(True)
+        gg = Path(td) / "fc1.gguf"
+        m.save_to_gguf(gg)
+        out["fc1fp16_gguf"] = np.frombuffer(gg.read_bytes(), np.uint8)
+        out["fc1fp16_logits"] = O.RefModel(gg).forward_packed(ids, cu)
+        # masked marginals: one masked copy of a wild type per position
+        wt = synth.residue_ids([40], seed=95)[0]
+        pos = np.array([0, 7, 19, 39], np.int32)
+        copies = []
+        for p in pos:
+            x = wt.copy()
+            x[p + 1] = 32
+            copies.append(x)
+        lg = O.RefModel(st).forward_scheduled(copies)
+        out["mm_wt"], out["mm_pos"] = wt, pos
+        out["mm_logprobs"] = np.array([[O.log_softmax_at(lg[i][p + 1], t) for t in range(33)]
+                                       for i, p in enumerate(pos)], F32)
+        O.ref_force_isa(None)
+        # BF16 attention, in a child process with the variable set; the
+        # inputs are regenerated from the seed by the test (their sums are
+        # stored to catch a change of the generator's stream)
+        q, k, v, acu, H, dh = bf16_attention_inputs()
+        np.savez(Path(td) / "att.npz", q=q, k=k, v=v, cu=acu)
+        script = (
+            "import sys, numpy as np\n"
+            f"sys.path.insert(0, {str(ROOT / 'oracle')!r})\n"
+            "import oracle as O\n"
+            f"d = np.load({str(Path(td) / 'att.npz')!r})\n"
+            "q, k, v, cu = (np.ascontiguousarray(d[n]) for n in ('q', 'k', 'v', 'cu'))\n"
+            "o = np.zeros_like(q)\n"
+            f"O.ref_check(O.ref().ref_attention_varlen(q.ctypes.data, k.ctypes.data, v.ctypes.data, "
+            f"cu.ctypes.data, cu.size - 1, {H}, {dh}, o.ctypes.data))\n"
+            f"np.save({str(Path(td) / 'att_out.npy')!r}, o)\n")
+        subprocess.run([sys.executable, "-c", script], check=True,
+                       env=dict(os.environ, ESM_AMX_ATTENTION="on"))
+        out.update(bf16att_sums=np.array([q.sum(dtype=np.float64), k.sum(dtype=np.float64),
+                                          v.sum(dtype=np.float64)]),
+                   bf16att_out=np.load(Path(td) / "att_out.npy"))
+    np.savez_compressed(path, **out)
+
+
 if __name__ == "__main__":
     O.build()
     ops_fixture(HERE / "ops_golden.npz")
     model_fixture(HERE / "model_golden.npz")
     hidden_fixture(HERE / "hidden_golden.npz", HERE / "model_golden.npz")
+    optin_fixture(HERE / "optin_golden.npz", HERE / "model_golden.npz")
     for p in sorted(HERE.glob("*.npz")):
         print(p.name, p.stat().st_size, "bytes")
