@@ -138,3 +138,31 @@ def test_model_entry_points_reject_null_handles_without_a_device():
     assert L.esmcu_model_set_first_block_fc1_fp16(None, 1) == bad
     assert L.esmcu_quantize_weights(None, None, 4, 4, None, None) == bad
     assert L.esmcu_last_error()
+
+
+def test_plan_batches_fuzz_against_reference_and_oracle(O, R):
+    """PlanBatches (scheduler.cpp:13-75) under property-based inputs: the
+    C-ABI host packer, the oracle and the compiled reference make the same
+    groups in the same order (per-tensor W8A8 numerics depend on them)."""
+    from hypothesis import HealthCheck, given, settings
+    from hypothesis import strategies as st
+
+    from esm_b200 import ops
+
+    @settings(max_examples=150, deadline=None, suppress_health_check=list(HealthCheck))
+    @given(lens=st.lists(st.integers(0, 1024), min_size=1, max_size=600),
+           thr=st.sampled_from([1.0, 1.05, 1.2, 1.5, 3.0]),
+           mb=st.sampled_from([0, 1, 7, 64, 256, 1000]))
+    def check(lens, thr, mb):
+        a = np.array(lens, np.int32)
+        order = np.zeros(a.size, np.int32)
+        sizes = np.zeros(a.size, np.int32)
+        ng = R.ref_plan_batches(a.ctypes.data, a.size, thr, mb, order.ctypes.data, sizes.ctypes.data)
+        want, p = [], 0
+        for s in sizes[:ng]:
+            want.append(order[p:p + s].tolist())
+            p += s
+        assert ops.plan_batches(a, thr, mb) == want
+        assert O.plan_batches(a, thr, mb) == want
+
+    check()
