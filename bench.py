@@ -122,7 +122,7 @@ def build_model(device: int, seed: int = 0):
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of the four INT8
 # GEMM launches of one layer, per token: ncu capture of the layer case of
-# esm_b200.kernel_cases (first config-3a group, 13,305 tokens; QKV 176.4 MB,
+# kernel_cases.py (first config-3a group, 13,305 tokens; QKV 176.4 MB,
 # out-proj 97.0 MB, fc1 247.7 MB, fc2 253.2 MB).  Traffic grows with the
 # tokens of a launch (activations and outputs; the weights are ~3% of it).
 GEMM_DRAM_BYTES_PER_TOKEN_LAYER = 774.30e6 / 13305

@@ -79,13 +79,16 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity.  Returns false (and sets
-// the timeout bit in *status) when the bound is reached.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status) {
+// the timeout bit in *status) when the bound (limit_ns of %globaltimer) is
+// reached.  Kernels use the default bound; the wait self-test passes a short
+// one.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status,
+                                          uint64_t limit_ns = kWaitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0 && global_timer_ns() - t0 > kWaitNs) break;
+    if ((i & 255u) == 0 && global_timer_ns() - t0 > limit_ns) break;
     if (i > 64) __nanosleep(32);
   }
   atomicOr(status, kStatusTimeout);
@@ -95,14 +98,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
 // mbar_wait that also gives up as soon as *abort (shared memory) is set by
 // another waiter of the CTA, and sets it itself on a timeout.
 __device__ __forceinline__ bool mbar_wait_abort(uint64_t* bar, uint32_t parity, uint32_t* status,
-                                                volatile uint32_t* abort) {
+                                                volatile uint32_t* abort,
+                                                uint64_t limit_ns = kWaitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0) {
       if (*abort) return false;
-      if (global_timer_ns() - t0 > kWaitNs) break;
+      if (global_timer_ns() - t0 > limit_ns) break;
     }
     if (i > 64) __nanosleep(32);
   }

@@ -131,8 +131,19 @@ int esmcu_open(int device, esmcu_context** out) {
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_status, sizeof(uint32_t));
   if (e == cudaSuccess) e = cudaMemset(ctx->d_status, 0, sizeof(uint32_t));
   if (e != cudaSuccess) {
+    if (ctx->d_status) cudaFree(ctx->d_status);
+    if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
     return cuda_fail(e, "esmcu_open");
+  }
+  // The no-alloc entry point's fixed scratch is committed here, on this
+  // device, so that its first call allocates nothing.
+  if (noalloc_prepare() != ESMCU_OK) {
+    const std::string msg = esmcu_last_error();
+    cudaFree(ctx->d_status);
+    cudaStreamDestroy(ctx->own_stream);
+    delete ctx;
+    return fail(ESMCU_ERR_CUDA, "esmcu_open: " + msg);
   }
   ctx->stream = ctx->own_stream;
   *out = ctx;

@@ -35,6 +35,9 @@ int use_device(esmcu_context* ctx);
 int ensure_scratch(esmcu_context* ctx, size_t bytes);
 // Reads (and clears) the device status word after a stream synchronise.
 int check_device_status(esmcu_context* ctx);
+// Loads the module holding esmcu_linear_int8_noalloc's fixed scratch on the
+// current device (noalloc.cu); esmcu_open calls it.
+int noalloc_prepare();
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 

@@ -338,7 +338,8 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
   float2* lnstat = reinterpret_cast<float2*>(base + a.lnstat);
   // LayerNorm + per-tensor quantisation in one kernel (no fp32 LN output)
   // unless an observer needs that output.
-  const bool ln_fused = quant && !per_token && stats == nullptr && d % 128 == 0 && d <= 2048;
+  const bool ln_fused = quant && !per_token && stats == nullptr && d % 128 == 0 &&
+                        (d <= 2048 || d == 2560);
   const bool qk_bf16 = attention_bf16_enabled(c.head_dim);
   LAUNCH(m, launch_positions(cu, B, pos, s));
   sec.begin("embed");

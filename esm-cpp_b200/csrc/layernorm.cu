@@ -200,12 +200,14 @@ __device__ __forceinline__ uint32_t quant4(float4 y, float inv) {
          ((static_cast<uint32_t>(a2) & 0xffu) << 16) | ((static_cast<uint32_t>(a3) & 0xffu) << 24);
 }
 
-// 12 warps per block, two blocks per SM (at most 80 registers: gamma and beta
-// come from shared memory and the statistics take one pass), a row per warp.
+// 12 warps per block, a row per warp.  Up to d = 2048 (NV <= 16) two blocks
+// share an SM (at most 80 registers: gamma and beta come from shared memory
+// and the statistics take one pass); d = 2560 (ESM-2 3B, NV = 20) holds 80
+// floats of the row per lane and runs one block per SM.
 constexpr int kLqThreads = 384;
 
 template <int NV>
-__global__ void __launch_bounds__(kLqThreads, 2)
+__global__ void __launch_bounds__(kLqThreads, NV <= 16 ? 2 : 1)
     ln_quant_kernel(const float* __restrict__ x, const float* __restrict__ g,
                     const float* __restrict__ b, float eps, int rows, int d, uint32_t* amax,
                     float2* stats, uint32_t* counter, int8_t* __restrict__ q, long ldq,
@@ -334,7 +336,7 @@ cudaError_t launch_layernorm_quant(const float* x, const float* g, const float* 
   if (rows <= 0) return cudaSuccess;
   const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(g) |
                          reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(q)) & 15) == 0;
-  if (d % 128 != 0 || d > 2048 || !aligned || ldq < d || (ldq % 16) != 0 || status == nullptr)
+  if (d % 128 != 0 || d > 2560 || !aligned || ldq < d || (ldq % 16) != 0 || status == nullptr)
     return cudaErrorNotSupported;
   switch (d / 128) {
     case 1: return launch_lq<1>(x, g, b, eps, rows, d, amax, stats, counter, q, ldq, scale_out, status, s);
@@ -347,6 +349,7 @@ cudaError_t launch_layernorm_quant(const float* x, const float* g, const float* 
     case 10: return launch_lq<10>(x, g, b, eps, rows, d, amax, stats, counter, q, ldq, scale_out, status, s);
     case 12: return launch_lq<12>(x, g, b, eps, rows, d, amax, stats, counter, q, ldq, scale_out, status, s);
     case 16: return launch_lq<16>(x, g, b, eps, rows, d, amax, stats, counter, q, ldq, scale_out, status, s);
+    case 20: return launch_lq<20>(x, g, b, eps, rows, d, amax, stats, counter, q, ldq, scale_out, status, s);
     default: return cudaErrorNotSupported;
   }
 }

@@ -12,17 +12,23 @@
 // exits.
 //
 // Limits and sharing: the scratch holds kNoAllocScratchBytes (16 MiB), so
-// 256 + 4*M (rounded up to 256) + M*ldq (+ N*ldq when K % 16 != 0) bytes
-// must fit, ldq = K rounded up to 16; larger calls are rejected with
+// 256 + 4*M (rounded up to 256) + M*ldq bytes, plus N*ldq more when K % 16 != 0
+// or W is not 16-byte aligned (W is then copied to padded rows), must fit,
+// ldq = K rounded up to 16; larger calls are rejected with
 // ESMCU_ERR_OUT_OF_RANGE.  Every call on a device shares the one array, and
 // it keeps the last call's contents: the absmax slots are cleared by each
 // call, and calls that overlap on the GPU (different streams, or different
-// host threads on the same device) race on it -- serialise them.  The first
-// call on a device looks the array's device address up (cudaGetSymbolAddress
-// with that device current); make that first call before any stream capture.
+// host threads on the same device) race on it -- serialise them.
+//
+// Set-up: esmcu_open calls noalloc_prepare for its device, with that device
+// current.  Looking the array's address up (cudaGetSymbolAddress) loads this
+// file's module, which is when the driver commits the 16 MiB; doing it at
+// open time means the first noalloc call neither allocates nor waits for a
+// module load, even under lazy module loading.  Each call looks the address
+// up again (cheap once the module is loaded) instead of caching it, so a
+// context torn down and re-created by the caller gets the current address.
 #include <cuda_runtime.h>
 
-#include <mutex>
 #include <string>
 
 #include "host/context.h"
@@ -39,33 +45,26 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 
 namespace {
 
-constexpr int kMaxDevices = 64;
-
-std::mutex g_addr_mu;
-void* g_addr[kMaxDevices] = {};
-
-// Device address of the scratch on the current device (looked up once per
-// device); nullptr with the error recorded on failure.
-void* scratch_address(int device) {
-  if (device < 0 || device >= kMaxDevices) {
-    set_error("esmcu_linear_int8_noalloc: device index beyond the supported range");
+// Device address of the scratch on the current device; nullptr with the
+// error recorded on failure.
+void* scratch_address() {
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || p == nullptr) {
+    set_error(std::string("esmcu_linear_int8_noalloc: cudaGetSymbolAddress: ") +
+              cudaGetErrorString(e));
     return nullptr;
   }
-  std::lock_guard<std::mutex> lk(g_addr_mu);
-  if (g_addr[device] == nullptr) {
-    void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr) {
-      set_error(std::string("esmcu_linear_int8_noalloc: cudaGetSymbolAddress: ") +
-                cudaGetErrorString(e));
-      return nullptr;
-    }
-    g_addr[device] = p;
-  }
-  return g_addr[device];
+  return p;
 }
 
 }  // namespace
+
+// Called by esmcu_open with the context's device current: loads the module
+// that holds the scratch array (committing its memory now, not at the first
+// noalloc call).
+int noalloc_prepare() { return scratch_address() != nullptr ? ESMCU_OK : ESMCU_ERR_CUDA; }
+
 }  // namespace esmb200
 
 using namespace esmb200;
@@ -75,12 +74,15 @@ extern "C" int esmcu_linear_int8_noalloc(esmcu_context* ctx, const float* A, con
                                          int M, int N, int K, int act_quant) {
   int rc = use_device(ctx);
   if (rc != ESMCU_OK) return rc;
+  // The same checks, in the same order, as esmcu_linear_int8.
   if (M < 0 || N < 0 || K < 0) return fail(ESMCU_ERR_INVALID_ARGUMENT, "negative shape");
+  if (M == 0 || N == 0) return ESMCU_OK;
+  if (A == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "A is null");
+  if (W == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "W is null");
+  if (w_scales == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "w_scales is null");
+  if (C == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "C is null");
   if (act_quant != ESMCU_ACT_PER_TENSOR && act_quant != ESMCU_ACT_PER_TOKEN)
     return fail(ESMCU_ERR_INVALID_ARGUMENT, "bad act_quant");
-  if (M == 0 || N == 0) return ESMCU_OK;
-  if (A == nullptr || W == nullptr || w_scales == nullptr || C == nullptr)
-    return fail(ESMCU_ERR_INVALID_ARGUMENT, "A, W, w_scales and C must be non-null");
   if (K == 0) {  // gemm_int8.cpp:512-519: K <= 0 zeroes C
     ESMCU_CUDA(cudaMemsetAsync(C, 0, sizeof(float) * static_cast<size_t>(M) * N, ctx->stream));
     return ESMCU_OK;
@@ -98,7 +100,7 @@ extern "C" int esmcu_linear_int8_noalloc(esmcu_context* ctx, const float* A, con
                     " bytes of scratch for M=" + std::to_string(M) + ", K=" + std::to_string(K) +
                     "; the fixed scratch holds " + std::to_string(kNoAllocScratchBytes) +
                     " (use esmcu_linear_int8 or split M)");
-  char* base = static_cast<char*>(scratch_address(ctx->device));
+  char* base = static_cast<char*>(scratch_address());
   if (base == nullptr) return ESMCU_ERR_CUDA;
   uint32_t* amax = reinterpret_cast<uint32_t*>(base);
   float* scales = reinterpret_cast<float*>(base + off_scales);

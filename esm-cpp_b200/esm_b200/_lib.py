@@ -66,6 +66,7 @@ _SIGS = {
     "esmcu_set_stream": (C.c_int, [_VP, _VP]),
     "esmcu_get_stream": (_VP, [_VP]),
     "esmcu_synchronize": (C.c_int, [_VP]),
+    "esmcu_bounded_wait_selftest": (C.c_int, [_VP, C.c_int, C.POINTER(C.c_int)]),
     "esmcu_malloc": (C.c_int, [_VP, C.c_size_t, C.POINTER(_VP)]),
     "esmcu_free": (C.c_int, [_VP, _VP]),
     "esmcu_memcpy_h2d": (C.c_int, [_VP, _VP, _VP, C.c_size_t]),

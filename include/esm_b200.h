@@ -69,6 +69,14 @@ int esmcu_set_stream(esmcu_context* ctx, void* cuda_stream);
 void* esmcu_get_stream(esmcu_context* ctx);
 /* Waits for the stream and reports device-side failures (timeouts). */
 int esmcu_synchronize(esmcu_context* ctx);
+/* Failure-detection self-test; no counterpart in the reference, which has no
+ * device waits.  Runs one small kernel whose mbarrier waits can never
+ * complete (one of two expected arrivals is made) and must give up after
+ * limit_us microseconds (0 < limit_us <= 1e6) through the same bounded-wait
+ * code every kernel here uses.  Returns ESMCU_ERR_TIMEOUT when they did, with
+ * *waiters_released = the number of waiting threads that gave up (4), and
+ * leaves the context usable. */
+int esmcu_bounded_wait_selftest(esmcu_context* ctx, int limit_us, int* waiters_released);
 /* Device memory helpers for C callers without another allocator. */
 int esmcu_malloc(esmcu_context* ctx, size_t bytes, void** dptr);
 int esmcu_free(esmcu_context* ctx, void* dptr);
@@ -97,13 +105,14 @@ int esmcu_linear_int8(esmcu_context* ctx, const float* A, const int8_t* W,
 /* No counterpart in the reference.  esmcu_linear_int8 without any device
  * allocation, for callers that cannot let the library call cudaMalloc (a
  * process whose HBM is all handed to its own pool, or one that cannot take
- * the synchronisation an allocation implies).  Same arguments and results;
- * its scratch is one fixed 16 MiB array per device, built into the library,
- * so 256 + 4*M (to 256) + M*ldq (+ N*ldq when K % 16 != 0) bytes must fit,
- * ldq = K rounded up to 16, else ESMCU_ERR_OUT_OF_RANGE.  All calls on a
- * device share that array: calls that overlap on the GPU race.  The first
- * call on a device looks up the array's address; make it before any stream
- * capture. */
+ * the synchronisation an allocation implies).  Same arguments, checks and
+ * results; its scratch is one fixed 16 MiB array per device, built into the
+ * library, so 256 + 4*M (to 256) + M*ldq bytes, plus N*ldq when K % 16 != 0
+ * or W is not 16-byte aligned, must fit, ldq = K rounded up to 16, else
+ * ESMCU_ERR_OUT_OF_RANGE.  All calls on a device share that array: calls
+ * that overlap on the GPU race.  esmcu_open loads the array onto its device
+ * (the driver commits the 16 MiB then), so the first call allocates
+ * nothing; open the context before handing HBM to a pool. */
 int esmcu_linear_int8_noalloc(esmcu_context* ctx, const float* A, const int8_t* W,
                               const float* w_scales, const float* bias, float* C, int M, int N,
                               int K, int act_quant);

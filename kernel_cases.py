@@ -1,6 +1,6 @@
 """Small, self-checking cases of the hot kernels, sized for a profiler capture.
 
-    PYTHONPATH=esm-cpp_b200 python -m esm_b200.kernel_cases layer|gemm|ln|attn|attn_long|attn_time|all
+    python kernel_cases.py layer|gemm|ln|attn|attn_long|attn_time|all
 
 Each case holds a few hundred MB on the device at most (inputs still larger
 than L2 where the kernel streams them) and launches its kernel a handful of
@@ -21,10 +21,13 @@ times, so `ncu -k regex:<kernel> -s <n> -c <k>` over it ends in a minute or two.
 from __future__ import annotations
 
 import sys
+from pathlib import Path
 
 import numpy as np
 
-from . import ops, synth
+sys.path.insert(0, str(Path(__file__).resolve().parent / "esm-cpp_b200"))
+
+from esm_b200 import ops, synth  # noqa: E402
 
 
 def _layer():

@@ -30,14 +30,29 @@ _orc = None
 _ref = None
 
 
+def reference_source() -> Path | None:
+    """The esm-cpp source tree: $REF_SRC when set (it must then hold
+    src/model.cpp), else a checkout named `reference` beside this
+    repository, else None (the prebuilt oracle/_ref, if any, is used)."""
+    src = os.environ.get("REF_SRC")
+    if src:
+        if not Path(src, "src", "model.cpp").exists():
+            raise FileNotFoundError(f"REF_SRC={src} has no src/model.cpp")
+        return Path(src)
+    sibling = HERE.parent.parent / "reference"
+    return sibling if (sibling / "src" / "model.cpp").exists() else None
+
+
 def build(ref: bool | None = None) -> None:
     """Builds liboracle.so (always) and libesmref.so (when the reference
-    sources are present)."""
+    sources are found, see reference_source)."""
     subprocess.run(["make", "-s", "-C", str(HERE), "oracle"], check=True)
-    src = os.environ.get("REF_SRC", "/root/reference")
+    src = reference_source()
     if ref is None:
-        ref = Path(src, "src", "model.cpp").exists()
+        ref = src is not None
     if ref:
+        if src is None:
+            raise FileNotFoundError("the reference sources were not found: set REF_SRC")
         subprocess.run(["make", "-s", "-j8", "-C", str(HERE), "ref", f"REF_SRC={src}"], check=True)
 
 

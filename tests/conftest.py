@@ -1,5 +1,7 @@
 """Shared fixtures.  GPU tests carry @pytest.mark.gpu; everything else runs on
 the CPU (no device needed).  The oracle (oracle/) is the checker only."""
+import json
+import os
 import sys
 from pathlib import Path
 
@@ -37,3 +39,18 @@ def cuda():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     return torch.device("cuda:0")
+
+
+@pytest.fixture(scope="session")
+def record():
+    """record(name, **values): appends one JSON line of measured values (a
+    parity test's observed Pearson, error or flip counts) to the file named
+    by $ESM_B200_RECORD, when it is set; otherwise does nothing."""
+    path = os.environ.get("ESM_B200_RECORD")
+
+    def _record(name, **values):
+        if path:
+            with open(path, "a") as f:
+                f.write(json.dumps({"test": name, **values}) + "\n")
+
+    return _record

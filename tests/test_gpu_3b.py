@@ -1,0 +1,123 @@
+"""ESM-2 3B width (BASELINE config 4 architecture: d = 2560, 40 heads x 64,
+FFN 10240) against the reference compiled from its own sources, on two
+layers of random-init weights (the per-layer kernels and shapes are those of
+the 36-layer model; depth only compounds rounding).
+
+This width takes paths that the 650M tests do not reach: the fused
+LayerNorm + quantisation kernel at 20 float4 per lane, the INT8 GEMMs at
+K = 2560 / 10240 and N = 7680 / 10240, and attention with 40 heads,
+including the > 256-token kernel at the deep-mutational-scan length 402.
+
+  FP32: logits within 1e-4 * (1 + |ref|), per-sequence Pearson >= 0.99999.
+  W8A8: both engines load one GGUF; the reference runs its VNNI path.
+        Per-sequence Pearson >= 0.9999 (two layers; one flipped int8 code
+        moves the logits by ~1e-3) and |error| <= 5e-2.
+  Scheduled: ForwardScheduled over 24 deep-mutational-scan sequences of 402
+        tokens (config 4's input, a wild type and its first substitutions)
+        on both engines, the same per-sequence gates.
+"""
+import os
+import tempfile
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+PEARSON_W8A8 = 0.9999
+ATOL_W8A8 = 5e-2
+
+
+def _pearsons(a, b, cu):
+    return [float(np.corrcoef(a[cu[i]:cu[i + 1]].ravel(), b[cu[i]:cu[i + 1]].ravel())[0, 1])
+            for i in range(len(cu) - 1)]
+
+
+@pytest.fixture(scope="module")
+def model3b(cuda, O, R):
+    from esm_b200 import synth
+
+    os.environ.setdefault("ESM_NUM_THREADS", str(os.cpu_count()))
+    m = synth.random_model("esm2_3b", seed=0, num_layers=2)
+    td = tempfile.TemporaryDirectory()
+    yield m, Path(td.name)
+    m.close()
+    td.cleanup()
+
+
+def _batch():
+    from esm_b200 import synth
+
+    seqs = synth.residue_ids([400, 128, 93, 250, 1], seed=21)
+    return synth.pack(seqs)
+
+
+def test_3b_fp32_matches_reference(model3b, O, record):
+    m, td = model3b
+    if m.config.weights_quantized:
+        pytest.skip("runs before the W8A8 tests quantise the shared model")
+    ids, cu = _batch()
+    st = td / "w.safetensors"
+    m.save_to_safetensors(st)
+    got = m.forward_packed(ids, cu, out=np.empty((ids.size, 33), np.float32))
+    O.ref_force_isa("avx512vnni")
+    try:
+        want = O.RefModel(st).forward_packed(ids, cu)
+    finally:
+        O.ref_force_isa(None)
+    rel = float((np.abs(got - want) / (1 + np.abs(want))).max())
+    ps = _pearsons(got, want, cu)
+    record("3b_fp32", max_rel_err=rel, pearson_min=min(ps))
+    assert rel <= 1e-4
+    assert min(ps) >= 0.99999
+
+
+@pytest.fixture(scope="module")
+def q8(model3b, O):
+    from esm_b200 import synth
+
+    m, td = model3b
+    if not m.config.weights_quantized:
+        stats = m.calibrate(synth.residue_ids(synth.varlen_lengths(8, seed=1), seed=2), 99.9)
+        m.apply_smoothquant(stats, 0.5)
+        m.quantize_weights()
+    p = td / "w.gguf"
+    m.save_to_gguf(p)
+    return m, O.RefModel(p)
+
+
+def test_3b_w8a8_matches_reference(q8, O, record):
+    m, ref = q8
+    ids, cu = _batch()
+    got = m.forward_packed(ids, cu, out=np.empty((ids.size, 33), np.float32))
+    O.ref_force_isa("avx512vnni")
+    try:
+        want = ref.forward_packed(ids, cu)
+    finally:
+        O.ref_force_isa(None)
+    ps = _pearsons(got, want, cu)
+    err = np.abs(got - want)
+    record("3b_w8a8", pearson_min=min(ps), mean_abs_err=float(err.mean()), max_abs_err=float(err.max()))
+    assert np.isfinite(got).all()
+    assert min(ps) >= PEARSON_W8A8, ps
+    np.testing.assert_allclose(got, want, rtol=1e-3, atol=ATOL_W8A8)
+
+
+def test_3b_w8a8_dms_scheduled_matches_reference(q8, O, record):
+    from esm_b200 import synth
+
+    m, ref = q8
+    seqs = synth.dms_sequences(seed=4)[:24]
+    assert all(len(s) == 402 for s in seqs)
+    got = m.forward_scheduled(seqs)
+    O.ref_force_isa("avx512vnni")
+    try:
+        want = ref.forward_scheduled(seqs)
+    finally:
+        O.ref_force_isa(None)
+    ps = [float(np.corrcoef(g.ravel(), w.ravel())[0, 1]) for g, w in zip(got, want)]
+    err = max(float(np.abs(g - w).max()) for g, w in zip(got, want))
+    record("3b_w8a8_dms_scheduled", pearson_min=min(ps), max_abs_err=err)
+    assert min(ps) >= PEARSON_W8A8, ps
+    assert err <= ATOL_W8A8 + 1e-3 * max(float(np.abs(w).max()) for w in want)

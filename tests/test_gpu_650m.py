@@ -1,15 +1,23 @@
 """ESM-2 650M (BASELINE config 3 architecture, random-init weights) against
-the reference compiled from its own sources, one packed group of 8
-sequences (residues ~ N(120,30) clipped to [90,250]):
+the reference compiled from its own sources.
 
-  FP32: logits within 1e-4 * (1 + |ref|), per-sequence Pearson >= 0.99999 --
-        every FP32 kernel (LN, 3xTF32 tensor-core attention, RoPE, GELU,
-        FP32 GEMMs) agrees with the reference's AVX-512 path.
-  W8A8: the reference calibrates nothing here; both engines load one GGUF
-        (this package's calibration + SmoothQuant + Quantize).  Logit
-        agreement must be at least the reference's agreement with itself
-        across its VNNI and default (AMX on Sapphire Rapids) paths, minus a
-        small margin, and Pearson >= 0.998.
+  FP32: one packed group of 8 sequences (residues ~ N(120,30) clipped to
+        [90,250]); logits within 1e-4 * (1 + |ref|), per-sequence Pearson
+        >= 0.99999 -- every FP32 kernel (LN, 3xTF32 tensor-core attention,
+        RoPE, GELU, FP32 GEMMs) agrees with the reference's AVX-512 path.
+  W8A8: both engines load one GGUF (this package's calibration + SmoothQuant
+        + Quantize); the reference runs its VNNI path (one activation scale
+        over all rows, like ours).  Two inputs, BASELINE config 3a (a packed
+        group of 8 varlen sequences) and config 3b (a uniform 8 x 256 batch).
+        Every int8 code and int32 sum is bit-exact op by op
+        (test_gpu_gemm.py); over 33 layers, last-ulp FP32 differences flip
+        single int8 roundings and the flips compound, as between the
+        reference's own ISA paths.  Gates: per-sequence Pearson >= 0.9990
+        (measured about 0.9996) and a mean |error| no larger than twice the
+        reference's own VNNI-vs-default spread.  The measured values are
+        recorded ($ESM_B200_RECORD) together with the per-layer fraction of
+        flipped int8 codes of the attention-LN quantisation, single sequence
+        by single sequence.
 """
 import os
 import tempfile
@@ -20,10 +28,12 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
+W8A8_PEARSON_650M = 0.9990
 
-def _pearson_min(a, b, cu):
-    return min(np.corrcoef(a[cu[i]:cu[i + 1]].ravel(), b[cu[i]:cu[i + 1]].ravel())[0, 1]
-               for i in range(len(cu) - 1))
+
+def _pearsons(a, b, cu):
+    return [float(np.corrcoef(a[cu[i]:cu[i + 1]].ravel(), b[cu[i]:cu[i + 1]].ravel())[0, 1])
+            for i in range(len(cu) - 1)]
 
 
 @pytest.fixture(scope="module")
@@ -40,8 +50,26 @@ def setup(cuda, O, R):
     td.cleanup()
 
 
-def test_650m_fp32_matches_reference(setup, O):
+@pytest.fixture(scope="module")
+def q8(setup, O):
+    """The same model calibrated, SmoothQuant-migrated and quantised here,
+    and the reference loading it from GGUF."""
+    from esm_b200 import synth
+
+    m, _, _, td = setup
+    if not m.config.weights_quantized:
+        stats = m.calibrate(synth.residue_ids(synth.varlen_lengths(32, seed=1), seed=2), 99.9)
+        m.apply_smoothquant(stats, 0.5)
+        m.quantize_weights()
+    p = td / "w.gguf"
+    m.save_to_gguf(p)
+    return m, O.RefModel(p)
+
+
+def test_650m_fp32_matches_reference(setup, O, record):
     m, ids, cu, td = setup
+    if m.config.weights_quantized:
+        pytest.skip("runs before the W8A8 tests quantise the shared model")
     st = td / "w.safetensors"
     m.save_to_safetensors(st)
     got = m.forward_packed(ids, cu, out=np.empty((ids.size, 33), np.float32))
@@ -50,28 +78,77 @@ def test_650m_fp32_matches_reference(setup, O):
         want = O.RefModel(st).forward_packed(ids, cu)
     finally:
         O.ref_force_isa(None)
-    assert (np.abs(got - want) / (1 + np.abs(want))).max() <= 1e-4
-    assert _pearson_min(got, want, cu) >= 0.99999
+    rel = float((np.abs(got - want) / (1 + np.abs(want))).max())
+    ps = _pearsons(got, want, cu)
+    record("650m_fp32_config3a", max_rel_err=rel, pearson_min=min(ps))
+    assert rel <= 1e-4
+    assert min(ps) >= 0.99999
 
 
-def test_650m_w8a8_within_reference_isa_spread(setup, O):
+def _config_input(name):
     from esm_b200 import synth
 
-    m, ids, cu, td = setup
-    stats = m.calibrate(synth.residue_ids(synth.varlen_lengths(32, seed=1), seed=2), 99.9)
-    m.apply_smoothquant(stats, 0.5)
-    m.quantize_weights()
+    if name == "config3a":
+        seqs = synth.residue_ids(synth.varlen_lengths(8, seed=5), seed=6)
+    else:  # config 3b: a uniform batch of 8 sequences of 256 tokens
+        seqs = synth.residue_ids([254] * 8, seed=7)
+    return synth.pack(seqs)
+
+
+@pytest.mark.parametrize("name", ["config3a", "config3b"])
+def test_650m_w8a8_within_reference_isa_spread(q8, O, record, name):
+    m, ref = q8
+    ids, cu = _config_input(name)
     got = m.forward_packed(ids, cu, out=np.empty((ids.size, 33), np.float32))
-    p = td / "w.gguf"
-    m.save_to_gguf(p)
     O.ref_force_isa("avx512vnni")
     try:
-        vnni = O.RefModel(p).forward_packed(ids, cu)
+        vnni = ref.forward_packed(ids, cu)
     finally:
         O.ref_force_isa(None)
-    default = O.RefModel(p).forward_packed(ids, cu)
-    ours = _pearson_min(got, vnni, cu)
-    spread = _pearson_min(vnni, default, cu)
-    assert ours >= 0.998
-    assert ours >= min(spread, 0.9995) - 5e-4, (ours, spread)
-    assert np.abs(got - vnni).mean() <= 2 * max(np.abs(vnni - default).mean(), 0.01)
+    default = ref.forward_packed(ids, cu)
+    ours = _pearsons(got, vnni, cu)
+    spread = _pearsons(vnni, default, cu)
+    err, err_spread = float(np.abs(got - vnni).mean()), float(np.abs(vnni - default).mean())
+    record(f"650m_w8a8_{name}", pearson_min=min(ours), pearson_mean=float(np.mean(ours)),
+           mean_abs_err=err, ref_isa_pearson_min=min(spread), ref_isa_mean_abs_err=err_spread,
+           ref_isa=O.ref().ref_current_isa().decode())
+    assert np.isfinite(got).all()
+    assert min(ours) >= W8A8_PEARSON_650M, ours
+    assert err <= 2 * max(err_spread, 0.01), (err, err_spread)
+
+
+def test_650m_w8a8_int8_code_flips_per_layer(q8, O, record):
+    """Single sequences through ForwardWithHiddenStates on both engines (the
+    reference's VNNI path): for every layer, the attention LayerNorm of each
+    engine's own input hidden state is quantised with its own per-tensor
+    scale, and the codes are compared.  Flips start at the last-ulp level and
+    grow with depth; the Pearson of the final logits stays high."""
+    from esm_b200 import synth
+
+    m, ref = q8
+    seqs = synth.residue_ids(synth.varlen_lengths(4, seed=11), seed=12)
+    n_layers = m.config.num_hidden_layers
+    flips = np.zeros(n_layers)
+    total = 0
+    pears = []
+    O.ref_force_isa("avx512vnni")
+    try:
+        for s in seqs:
+            logits, hs = m.forward_with_hidden_states(s)
+            rlogits, rh = ref.forward_hidden(s)
+            pears.append(float(np.corrcoef(logits.ravel(), rlogits.ravel())[0, 1]))
+            total += hs[0].size
+            for li in range(n_layers):
+                lw = m.layers[li]
+                a = O.layernorm(hs[li], lw["attn_ln_w"], lw["attn_ln_b"])
+                b = O.layernorm(rh[li], lw["attn_ln_w"], lw["attn_ln_b"])
+                qa, _ = O.quantize_act_per_tensor(a)
+                qb, _ = O.quantize_act_per_tensor(b)
+                flips[li] += int(np.count_nonzero(qa != qb))
+    finally:
+        O.ref_force_isa(None)
+    frac = flips / total
+    record("650m_w8a8_code_flips", flip_frac_per_layer=[float(f) for f in frac],
+           logits_pearson=pears)
+    assert frac[0] == 0.0  # the embedding output is bit-identical
+    assert min(pears) >= W8A8_PEARSON_650M, pears

@@ -5,8 +5,10 @@ scratch is a fixed array built into the library and shared by every call on a
 device, so each case makes two calls in a row -- the first with larger
 activations than the second, so a stale absmax left by the first would change
 the second's result -- and compares both, through the C-ABI alone, with the
-allocating esmcu_linear_int8 on the same inputs.  Both run the same kernels,
-so the tolerance is the op-level one of the INT8 GEMM tests: bit-exact.
+allocating esmcu_linear_int8 on the same inputs and with the CPU oracle
+(quantise, exact int32 dot, FinalizeStore16 dequant).  All three agree bit for
+bit, the tolerance of the INT8 GEMM tests.  The device's free memory is also
+read around repeated calls: a call that allocated would lower it.
 
 This file is collected last on purpose; it also passes when run on its own.
 """
@@ -69,9 +71,21 @@ def _weights(rng, N, K):
     return Wq, ws
 
 
+def _free_bytes():
+    import torch
+
+    torch.cuda.synchronize()
+    return torch.cuda.mem_get_info(0)[0]
+
+
 @pytest.mark.parametrize("act_quant", [0, 1])
-@pytest.mark.parametrize("M,N,K", [(512, 1280, 1280), (300, 257, 1000), (7, 33, 23)])
-def test_two_calls_match_allocating_entry_point(ctx, M, N, K, act_quant):
+@pytest.mark.parametrize("M,N,K,w_offset", [(512, 1280, 1280, 0), (300, 257, 1000, 0),
+                                             (7, 33, 23, 0), (64, 96, 1280, 3)])
+def test_two_calls_match_allocating_entry_point(ctx, M, N, K, w_offset, act_quant):
+    """w_offset > 0 passes W at an address that is not 16-byte aligned (with
+    K % 16 == 0), which takes the padded-copy path."""
+    import oracle as O
+
     from esm_b200 import _lib
 
     rng = np.random.default_rng(M * 7 + N * 3 + K + act_quant)
@@ -79,7 +93,10 @@ def test_two_calls_match_allocating_entry_point(ctx, M, N, K, act_quant):
     bias = (rng.standard_normal(N) * 0.1).astype(np.float32)
     d = _Dev(ctx)
     try:
-        dW, dws, db = d.put(Wq), d.put(ws), d.put(bias)
+        W_store = np.zeros(N * K + 16, np.int8)
+        W_store[w_offset:w_offset + N * K] = Wq.ravel()
+        dW = C.c_void_p(d.put(W_store).value + w_offset)
+        dws, db = d.put(ws), d.put(bias)
         dC_ref = d.put(np.zeros((M, N), np.float32))
         dC = d.put(np.zeros((M, N), np.float32))
         for call, amp in enumerate((10.0, 1.0)):
@@ -92,6 +109,29 @@ def test_two_calls_match_allocating_entry_point(ctx, M, N, K, act_quant):
             assert np.isfinite(got).all()
             assert np.array_equal(got, want), (
                 f"call {call}: max |diff| {np.abs(got - want).max():.3e}")
+            oracle = O.linear_int8(A, Wq, ws, bias, per_token=act_quant == 1)
+            assert np.array_equal(got, oracle), (
+                f"call {call}: vs oracle max |diff| {np.abs(got - oracle).max():.3e}")
+    finally:
+        d.free()
+
+
+def test_calls_allocate_no_device_memory(ctx):
+    from esm_b200 import _lib
+
+    M, N, K = 2048, 1280, 1280
+    rng = np.random.default_rng(11)
+    Wq, ws = _weights(rng, N, K)
+    d = _Dev(ctx)
+    try:
+        dA = d.put(rng.standard_normal((M, K)).astype(np.float32))
+        dW, dws = d.put(Wq), d.put(ws)
+        dC = d.put(np.zeros((M, N), np.float32))
+        before = _free_bytes()
+        for _ in range(3):
+            _lib.call("esmcu_linear_int8_noalloc", ctx, dA, dW, dws, None, dC, M, N, K, 0)
+        _lib.call("esmcu_synchronize", ctx)
+        assert _free_bytes() == before
     finally:
         d.free()
 
