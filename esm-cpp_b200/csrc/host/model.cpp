@@ -27,6 +27,7 @@
 #include "../kernels.cuh"
 #include "context.h"
 #include "esm_b200.h"
+#include "observer.h"
 #include "scheduler.h"
 
 using namespace esmb200;
@@ -283,24 +284,23 @@ void collect_profile(esmcu_model* m, bool reset) {
   m->pending.clear();
 }
 
-// Percentile of |x| exactly as ActivationObserver::Percentile indexes a
-// sorted sample (observer.cpp:33-51), over every value instead of a
-// 65536-entry reservoir.
-float host_percentile(const float* dev, size_t n, float pctile, cudaStream_t s) {
-  if (n == 0) return 0.0f;
+// Copies a device tensor of one observer site to the host and hands it to
+// the observer, which feeds its reservoir on a worker thread.
+int observe_site(Observer* obs, int layer, int site, const float* dev, size_t n, cudaStream_t s) {
+  static const char* kSites[4] = {"attn_ln_output", "attn_out", "ffn_ln_output", "inter_gelu"};
   std::vector<float> h(n);
-  cudaMemcpyAsync(h.data(), dev, n * 4, cudaMemcpyDeviceToHost, s);
-  cudaStreamSynchronize(s);
-  for (auto& v : h) v = std::fabs(v);
-  const float frac = std::clamp(pctile / 100.0f, 0.0f, 1.0f);
-  size_t idx = static_cast<size_t>(std::floor(frac * static_cast<float>(n - 1)));
-  if (idx >= n) idx = n - 1;
-  std::nth_element(h.begin(), h.begin() + static_cast<long>(idx), h.end());
-  return h[idx];
+  if (n) {
+    ESMCU_CUDA(cudaMemcpyAsync(h.data(), dev, n * 4, cudaMemcpyDeviceToHost, s));
+    ESMCU_CUDA(cudaStreamSynchronize(s));
+  }
+  obs->observe_async("layer" + std::to_string(layer) + "." + kSites[site], std::move(h));
+  return ESMCU_OK;
 }
 
-// The packed forward on device buffers already in the arena.  When stats
-// is non-null (calibration), writes the four per-layer site percentiles.
+// The packed forward on device buffers already in the arena.  When obs is
+// non-null (calibration, ForwardWithObserver), the four Linear inputs of
+// every layer are fed to it under the reference's site keys
+// (model.cpp:952-1050).
 // hidden (device, nullable): [num_layers + 1, T, d] receives the hidden
 // states of ForwardPackedInto's hidden_packed_out (model.cpp:1142-1189): the
 // embedding output, each layer's output, and in the last entry the final
@@ -309,7 +309,7 @@ float host_percentile(const float* dev, size_t n, float pctile, cudaStream_t s) 
 // only, and logits [R, V] receive their log-softmax (the masked-marginal
 // head of eval/proteingym.py:84-98).
 int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk, float* logits,
-                   int T, int B, int max_len, float pctile, float* stats, float* hidden_out = nullptr,
+                   int T, int B, int max_len, Observer* obs, float* hidden_out = nullptr,
                    const int* rows = nullptr, int R = 0) {
   const auto& c = m->cfg;
   esmcu_context* ctx = m->ctx;
@@ -338,7 +338,7 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
   float2* lnstat = reinterpret_cast<float2*>(base + a.lnstat);
   // LayerNorm + per-tensor quantisation in one kernel (no fp32 LN output)
   // unless an observer needs that output.
-  const bool ln_fused = quant && !per_token && stats == nullptr && d % 128 == 0 &&
+  const bool ln_fused = quant && !per_token && obs == nullptr && d % 128 == 0 &&
                         (d <= 2048 || d == 2560);
   const bool qk_bf16 = attention_bf16_enabled(c.head_dim);
   LAUNCH(m, launch_positions(cu, B, pos, s));
@@ -391,8 +391,8 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
     else LAUNCH(m, launch_quantize_per_tensor(x, K, rows_q, K, am, q8, ldk, ascale, s));
     return ESMCU_OK;
   };
-  auto observe = [&](int layer, int site, const float* x, size_t n) {
-    if (stats) stats[layer * 4 + site] = host_percentile(x, n, pctile, s);
+  auto observe = [&](int layer, int site, const float* x, size_t n) -> int {
+    return obs ? observe_site(obs, layer, site, x, n, s) : ESMCU_OK;
   };
   const size_t Td = static_cast<size_t>(T) * d;
 
@@ -412,7 +412,7 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
                                  quant ? am : nullptr, nullptr, 0, nullptr, s));
     }
     sec.end();
-    observe(li, 0, ln, Td);
+    TRY(observe(li, 0, ln, Td));
     if (quant && !per_token && !ln_fused) {
       sec.begin("quantize");
       TRY(quantize(ln, d, m->ldk_d, am));
@@ -459,7 +459,7 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
                                       (quant && !per_token) ? am + 1 * kAmaxSlots : nullptr,
                                       ctx->d_status, ctx->num_sms, s, qk_bf16));
     sec.end();
-    observe(li, 1, attn, Td);
+    TRY(observe(li, 1, attn, Td));
     if (quant) {
       sec.begin("quantize");
       TRY(quantize(attn, d, m->ldk_d, am + 1 * kAmaxSlots));
@@ -496,7 +496,7 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
                                  s));
     }
     sec.end();
-    observe(li, 2, ln, Td);
+    TRY(observe(li, 2, ln, Td));
     if (round0)
       LAUNCH(m, launch_round_fp16(ln, static_cast<long>(Td), quant && !per_token ? am + 2 * kAmaxSlots : nullptr,
                                   s));
@@ -519,7 +519,7 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
       }
     }
     sec.end();
-    observe(li, 3, inter, static_cast<size_t>(T) * ffn);
+    TRY(observe(li, 3, inter, static_cast<size_t>(T) * ffn));
     if (quant) {
       sec.begin("quantize");
       TRY(quantize(inter, ffn, m->ldk_ffn, am + 3 * kAmaxSlots));
@@ -667,13 +667,13 @@ int prepare(esmcu_model* m, int T, bool has_masks, const int32_t* cu, int B, Are
 
 // Packed forward from host buffers; logits (host) [T, V].
 int forward_packed_host(esmcu_model* m, const int32_t* ids, const int32_t* masks, int T,
-                        const int32_t* cu, int B, float* logits, float pctile, float* stats,
+                        const int32_t* cu, int B, float* logits, Observer* obs,
                         float* hidden = nullptr) {
   Arena a;
   int max_len = 0;
   TRY(prepare(m, T, masks != nullptr, cu, B, &a, &max_len));
   if (T == 0) return ESMCU_OK;  // model.cpp:1105-1108
-  if (ids == nullptr || (logits == nullptr && stats == nullptr && hidden == nullptr))
+  if (ids == nullptr || (logits == nullptr && obs == nullptr && hidden == nullptr))
     return fail(ESMCU_ERR_INVALID_ARGUMENT, "ids/logits is null");
   for (int t = 0; t < T; ++t)
     if (ids[t] < 0 || ids[t] >= m->cfg.vocab_size)
@@ -706,11 +706,12 @@ int forward_packed_host(esmcu_model* m, const int32_t* ids, const int32_t* masks
   }
   TRY(forward_device(m, a, reinterpret_cast<const int*>(base + a.ids),
                      masks ? reinterpret_cast<const int*>(base + a.masks) : nullptr, d_logits, T, B,
-                     max_len, pctile, stats, hidden ? m->hs_dev : nullptr));
+                     max_len, obs, hidden ? m->hs_dev : nullptr));
   if (logits) ESMCU_CUDA(cudaMemcpyAsync(pin + off_logits, d_logits, n_logits, cudaMemcpyDeviceToHost, s));
   ESMCU_CUDA(cudaStreamSynchronize(s));
   if (logits) std::memcpy(logits, pin + off_logits, n_logits);
   if (hidden) ESMCU_CUDA(cudaMemcpy(hidden, m->hs_dev, n_hidden, cudaMemcpyDeviceToHost));
+  if (obs) obs->wait();
   if (m->profiling) collect_profile(m, true);
   return check_device_status(m->ctx);
 }
@@ -822,7 +823,7 @@ int run_groups(esmcu_model* m, const std::vector<std::vector<int>>& groups, cons
     float* d_logits = reinterpret_cast<float*>(base + p.a.logits);
     TRY(forward_device(m, p.a, reinterpret_cast<const int*>(base + p.a.ids),
                        masks_concat ? reinterpret_cast<const int*>(base + p.a.masks) : nullptr,
-                       d_logits, p.T, p.B, p.max_len, 0.0f, nullptr, nullptr, d_rows, p.B));
+                       d_logits, p.T, p.B, p.max_len, nullptr, nullptr, d_rows, p.B));
     ESMCU_CUDA(cudaMemcpyAsync(hp + p.off_logits, d_logits,
                                static_cast<size_t>(score_rows ? p.B : p.T) * V * 4,
                                cudaMemcpyDeviceToHost, s));
@@ -1036,14 +1037,14 @@ int esmcu_model_set_layer(esmcu_model* m, int layer, const esmcu_layer_weights* 
 
 int esmcu_model_forward_packed(esmcu_model* m, const int32_t* ids, const int32_t* masks, int T,
                                const int32_t* cu, int B, float* logits) {
-  return forward_packed_host(m, ids, masks, T, cu, B, logits, 0.0f, nullptr);
+  return forward_packed_host(m, ids, masks, T, cu, B, logits, nullptr);
 }
 
 int esmcu_model_forward_hidden_states(esmcu_model* m, const int32_t* ids, const int32_t* masks,
                                       int T, const int32_t* cu, int B, float* logits,
                                       float* hidden_out) {
   if (hidden_out == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "hidden_out is null");
-  return forward_packed_host(m, ids, masks, T, cu, B, logits, 0.0f, nullptr, hidden_out);
+  return forward_packed_host(m, ids, masks, T, cu, B, logits, nullptr, hidden_out);
 }
 
 int esmcu_model_forward_packed_device(esmcu_model* m, const int32_t* d_ids,
@@ -1058,7 +1059,15 @@ int esmcu_model_forward_packed_device(esmcu_model* m, const int32_t* d_ids,
   m->launches = 0;
   ESMCU_CUDA(cudaMemcpyAsync(m->arena + a.cu, cu, static_cast<size_t>(B + 1) * 4,
                              cudaMemcpyHostToDevice, m->ctx->stream));
-  return forward_device(m, a, d_ids, d_masks, d_logits, T, B, max_len, 0.0f, nullptr);
+  return forward_device(m, a, d_ids, d_masks, d_logits, T, B, max_len, nullptr);
+}
+
+int esmcu_model_forward_observed(esmcu_model* m, esmcu_observer* obs, const int32_t* ids, int T,
+                                 const int32_t* cu, int B, float* logits) {
+  if (m == nullptr || obs == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "null argument");
+  if (m->cfg.weights_quantized)
+    return fail(ESMCU_ERR_INVALID_ARGUMENT, "calibration runs on the unquantised model");
+  return forward_packed_host(m, ids, nullptr, T, cu, B, logits, reinterpret_cast<Observer*>(obs));
 }
 
 int esmcu_model_observe_packed(esmcu_model* m, const int32_t* ids, int T, const int32_t* cu,
@@ -1066,7 +1075,15 @@ int esmcu_model_observe_packed(esmcu_model* m, const int32_t* ids, int T, const 
   if (m == nullptr || stats_out == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "null argument");
   if (m->cfg.weights_quantized)
     return fail(ESMCU_ERR_INVALID_ARGUMENT, "calibration runs on the unquantised model");
-  return forward_packed_host(m, ids, nullptr, T, cu, B, nullptr, pctile, stats_out);
+  Observer obs;
+  TRY(forward_packed_host(m, ids, nullptr, T, cu, B, nullptr, &obs));
+  static const char* kSites[4] = {"attn_ln_output", "attn_out", "ffn_ln_output", "inter_gelu"};
+  for (int li = 0; li < m->cfg.num_layers; ++li)
+    for (int j = 0; j < 4; ++j) {
+      const Observer::Reservoir* r = obs.find("layer" + std::to_string(li) + "." + kSites[j]);
+      stats_out[li * 4 + j] = r ? r->percentile(pctile) : 0.0f;
+    }
+  return ESMCU_OK;
 }
 
 int esmcu_model_forward_scheduled(esmcu_model* m, const int32_t* ids_concat, const int32_t* lens,

@@ -109,6 +109,15 @@ _SIGS = {
     "esmcu_forward_scheduled_multi": (C.c_int, [_VP, C.c_int, _VP, _VP, _VP, C.c_int, C.c_float,
                                                 C.c_int, _VP]),
     "esmcu_model_observe_packed": (C.c_int, [_VP, _VP, C.c_int, _VP, C.c_int, C.c_float, _VP]),
+    "esmcu_model_forward_observed": (C.c_int, [_VP, _VP, _VP, C.c_int, _VP, C.c_int, _VP]),
+    "esmcu_observer_create": (C.c_int, [C.POINTER(_VP)]),
+    "esmcu_observer_destroy": (C.c_int, [_VP]),
+    "esmcu_observer_clear": (C.c_int, [_VP]),
+    "esmcu_observer_observe": (C.c_int, [_VP, C.c_char_p, _VP, C.c_size_t]),
+    "esmcu_observer_num_sites": (C.c_int, [_VP]),
+    "esmcu_observer_site": (C.c_int, [_VP, C.c_int, C.c_float, C.POINTER(C.c_char_p),
+                                      C.POINTER(C.c_float), C.POINTER(C.c_size_t)]),
+    "esmcu_observer_percentile": (C.c_int, [_VP, C.c_char_p, C.c_float, C.POINTER(C.c_float)]),
     "esmcu_model_set_profiling": (C.c_int, [_VP, C.c_int]),
     "esmcu_model_profile": (C.c_int, [_VP, C.POINTER(C.c_char_p), _VP, C.c_int]),
     "esmcu_model_last_launch_count": (C.c_int, [_VP]),

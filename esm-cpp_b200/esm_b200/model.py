@@ -83,25 +83,46 @@ _HF_HEAD = {
 
 
 class ActivationObserver:
-    """observer.h ActivationObserver: collects calibration sequences; the
-    percentile of |X| per site is computed over every activation of all
-    collected sequences in one packed GPU forward."""
+    """observer.h ActivationObserver over the native esmcu_observer: per-site
+    reservoirs of at most 65536 |values| (Algorithm R, std::mt19937 seeded
+    0xc1b1ce), fed by Model.forward_with_observer / Model.calibrate in the
+    order the reference's ForwardWithObserver calls would feed them."""
 
     def __init__(self):
-        self._model = None
-        self._seqs: list[np.ndarray] = []
+        h = C.c_void_p()
+        _lib.call("esmcu_observer_create", C.byref(h))
+        self._h = h
 
-    def _add(self, model, ids):
-        self._model = model
-        self._seqs.append(np.asarray(ids, np.int32))
+    @property
+    def handle(self):
+        return self._h
+
+    def observe(self, site_key: str, values) -> None:
+        """ActivationObserver::Observe on host values."""
+        v = np.ascontiguousarray(values, F32).ravel()
+        _lib.call("esmcu_observer_observe", self._h, site_key.encode(), v.ctypes.data, v.size)
 
     def percentile(self, pctile: float) -> dict:
-        if not self._seqs:
-            return {}
-        return self._model._observe(self._seqs, pctile)
+        """ActivationObserver::Percentile: {site key: pctile-th percentile}."""
+        out = {}
+        n = _lib.lib().esmcu_observer_num_sites(self._h)
+        key, val = C.c_char_p(), C.c_float()
+        for i in range(max(n, 0)):
+            _lib.call("esmcu_observer_site", self._h, i, float(pctile), C.byref(key), C.byref(val),
+                      None)
+            out[key.value.decode()] = float(val.value)
+        return out
 
-    def clear(self):
-        self._seqs.clear()
+    def clear(self) -> None:
+        _lib.call("esmcu_observer_clear", self._h)
+
+    def __del__(self):
+        try:
+            if self._h is not None:
+                _lib.lib().esmcu_observer_destroy(self._h)
+                self._h = None
+        except Exception:
+            pass
 
 
 class Model:
@@ -279,17 +300,35 @@ class Model:
         self._dirty = True
 
     def calibrate(self, sequences, pctile: float = 99.9) -> dict:
-        """Observer statistics of a list of id arrays (one packed forward)."""
+        """quantize.py calibrate (python/esm_cpp/quantize.py:35-47): every
+        sequence observed through ForwardWithObserver, then Percentile.  The
+        sequences run as one packed forward, which observes the same values
+        in the same order as one call per sequence."""
         obs = ActivationObserver()
-        for s in sequences:
-            obs._add(self, s)
+        seqs = [np.ascontiguousarray(s, np.int32) for s in sequences]
+        if seqs:
+            ids, cu = np.concatenate(seqs), np.concatenate(
+                [[0], np.cumsum([len(s) for s in seqs])]).astype(np.int32)
+            self._forward_observed(ids, cu, obs, None)
         return obs.percentile(pctile)
 
     def forward_with_observer(self, input_ids, attention_mask, observer: ActivationObserver):
-        if attention_mask is not None:
+        """Model::ForwardWithObserver (model.cpp:1084-1090): logits [L, V] of one
+        sequence, its four Linear inputs per layer fed to `observer`."""
+        if attention_mask is not None and not np.all(np.asarray(attention_mask) == 1):
             raise NotImplementedError("calibration takes unpadded sequences")
-        observer._add(self, input_ids)
-        return self.forward(input_ids)
+        ids = np.ascontiguousarray(input_ids, np.int32)
+        logits = np.empty((ids.shape[0], self._cfg.vocab_size), F32)
+        self._forward_observed(ids, np.array([0, ids.shape[0]], np.int32), observer, logits)
+        return logits
+
+    def _forward_observed(self, ids, cu, observer, logits):
+        if self._cfg.weights_quantized:
+            raise RuntimeError("calibrate before quantize_weights")
+        self._ensure_device()
+        _lib.call("esmcu_model_forward_observed", self._dev, observer.handle, ids.ctypes.data,
+                  ids.shape[0], cu.ctypes.data, cu.shape[0] - 1,
+                  None if logits is None else logits.ctypes.data)
 
     # ------------------------------------------------------------- device
     def _ensure_device(self):
@@ -502,18 +541,6 @@ class Model:
                   None if masks is None else masks.ctypes.data, r.ctypes.data, n,
                   float(imbalance_threshold), int(max_batch_size), out.ctypes.data)
         return out
-
-    def _observe(self, seqs, pctile) -> dict:
-        if self._cfg.weights_quantized:
-            raise RuntimeError("calibrate before quantize_weights")
-        self._ensure_device()
-        ids = np.concatenate(seqs).astype(np.int32)
-        cu = np.concatenate([[0], np.cumsum([len(s) for s in seqs])]).astype(np.int32)
-        n = self._cfg.num_hidden_layers
-        stats = np.zeros(n * 4, F32)
-        _lib.call("esmcu_model_observe_packed", self._dev, ids.ctypes.data, ids.shape[0],
-                  cu.ctypes.data, len(seqs), float(pctile), stats.ctypes.data)
-        return {f"layer{i}.{SITES[j]}": float(stats[i * 4 + j]) for i in range(n) for j in range(4)}
 
 
 def forward_scheduled_multi(models, input_ids, imbalance_threshold: float = 1.2,

@@ -261,11 +261,41 @@ int esmcu_model_forward_packed_device(esmcu_model* m, const int32_t* d_ids,
 int esmcu_forward_scheduled_multi(esmcu_model** models, int n_models, const int32_t* ids_concat,
                                   const int32_t* lens, const int32_t* masks_concat, int n,
                                   float imbalance_threshold, int max_batch_size, float* logits);
-/* Calibration observer for SmoothQuant (Model::ForwardWithObserver,
- * model.cpp:952-1050): runs the packed forward of an unquantised model and
- * returns, per layer, the pctile-th percentile of |X| at the four Linear
- * inputs (attn_ln_output, attn_out, ffn_ln_output, inter_gelu) in
- * stats_out[num_layers * 4]. */
+/* ---- calibration (ActivationObserver, observer.h:14-44) ----------------
+ * esmcu_observer is the reference's per-site reservoir observer: each site
+ * keeps at most 65536 |values| by Algorithm R with its own std::mt19937
+ * seeded 0xc1b1ce (observer.cpp:8-31), so the same values observed in the
+ * same order keep the same sample as the reference; percentiles index the
+ * sorted sample as observer.cpp:33-51 does.  Sites are listed in the order
+ * they were first observed. */
+typedef struct esmcu_observer esmcu_observer;
+int esmcu_observer_create(esmcu_observer** out);
+int esmcu_observer_destroy(esmcu_observer* obs);
+/* ActivationObserver::Clear (observer.cpp:53). */
+int esmcu_observer_clear(esmcu_observer* obs);
+/* ActivationObserver::Observe (observer.cpp:8-31) on n host values. */
+int esmcu_observer_observe(esmcu_observer* obs, const char* site_key, const float* values,
+                           size_t n);
+int esmcu_observer_num_sites(const esmcu_observer* obs);
+/* Site i: its key (valid until the observer changes), its pctile-th
+ * percentile and how many values it has seen (each nullable). */
+int esmcu_observer_site(esmcu_observer* obs, int i, float pctile, const char** key,
+                        float* value, size_t* total_seen);
+/* ActivationObserver::Percentile (observer.cpp:33-51) of one site;
+ * ESMCU_ERR_NOT_FOUND when the site was never observed. */
+int esmcu_observer_percentile(esmcu_observer* obs, const char* site_key, float pctile,
+                              float* value);
+/* Model::ForwardWithObserver (model.cpp:1084-1090) on a packed batch of an
+ * unquantised model: the four Linear inputs of layer i are observed under
+ * "layer<i>.attn_ln_output", ".attn_out", ".ffn_ln_output", ".inter_gelu"
+ * (model.cpp:952-1050), in packed row-major order -- the same stream of
+ * values as one reference call per sequence, in sequence order.  logits
+ * (host, [T, V]) is nullable. */
+int esmcu_model_forward_observed(esmcu_model* m, esmcu_observer* obs, const int32_t* ids, int T,
+                                 const int32_t* cu_seqlens, int batch_size, float* logits);
+/* esmcu_model_forward_observed with a fresh observer, then the pctile-th
+ * percentile of each site into stats_out[num_layers * 4] (layer-major, sites
+ * in the order above). */
 int esmcu_model_observe_packed(esmcu_model* m, const int32_t* ids, int T,
                                const int32_t* cu_seqlens, int batch_size, float pctile,
                                float* stats_out);

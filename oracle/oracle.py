@@ -114,6 +114,12 @@ _REF_SIGS = {
     "ref_model_calibrate_smoothquant": (_I, [_VP, _VP, _VP, _I, _F, _F]),
     "ref_model_quantize": (_I, [_VP]),
     "ref_model_save_gguf": (_I, [_VP, C.c_char_p]),
+    "ref_observer_new": (_VP, []),
+    "ref_observer_free": (None, [_VP]),
+    "ref_observer_observe": (_I, [_VP, C.c_char_p, _VP, _SZ]),
+    "ref_observer_percentile": (_I, [_VP, C.c_char_p, _F, _VP]),
+    "ref_model_observe": (_I, [_VP, _VP, _VP, _I, _F, _VP]),
+    "ref_model_apply_smoothquant": (_I, [_VP, _VP, _F]),
 }
 
 
@@ -452,6 +458,23 @@ class RefModel:
         ref_check(ref().ref_model_calibrate_smoothquant(C.c_void_p(self.h), ids.ctypes.data,
                                                         lens.ctypes.data, len(seqs), pctile, alpha),
                   "calibrate")
+
+    def observe(self, seqs, pctile=99.9):
+        """quantize.py calibrate: ForwardWithObserver per sequence, then
+        Percentile -> [layers * 4] (sites attn_ln_output, attn_out,
+        ffn_ln_output, inter_gelu per layer)."""
+        lens = np.array([len(s) for s in seqs], np.int32)
+        ids = np.concatenate(seqs).astype(np.int32)
+        out = np.zeros(self.layers * 4, F32)
+        ref_check(ref().ref_model_observe(C.c_void_p(self.h), ids.ctypes.data, lens.ctypes.data,
+                                          len(seqs), C.c_float(pctile), out.ctypes.data), "observe")
+        return out
+
+    def apply_smoothquant(self, stats, alpha=0.5):
+        """Model::ApplySmoothQuant with stats [layers * 4] as from observe()."""
+        st = _a(stats)
+        ref_check(ref().ref_model_apply_smoothquant(C.c_void_p(self.h), st.ctypes.data,
+                                                    C.c_float(alpha)), "apply_smoothquant")
 
     def quantize(self):
         ref_check(ref().ref_model_quantize(C.c_void_p(self.h)), "quantize")

@@ -14,6 +14,7 @@
 #include <exception>
 #include <memory>
 #include <span>
+#include <stdexcept>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -341,6 +342,62 @@ int ref_model_calibrate_smoothquant(void* m, const int* ids_concat,
       off += static_cast<std::size_t>(lens[i]);
     }
     model->ApplySmoothQuant(obs.Percentile(pctile), alpha);
+  });
+}
+
+// ActivationObserver (observer.h:14-44, observer.cpp:8-51) as a handle.
+void* ref_observer_new() { return new esm::ActivationObserver(); }
+void ref_observer_free(void* o) { delete static_cast<esm::ActivationObserver*>(o); }
+int ref_observer_observe(void* o, const char* key, const float* values, std::size_t n) {
+  return Guard([&] { static_cast<esm::ActivationObserver*>(o)->Observe(key, values, n); });
+}
+// Percentile of one site; -1 with an error when the site was never observed.
+int ref_observer_percentile(void* o, const char* key, float pctile, float* out) {
+  return Guard([&] {
+    auto p = static_cast<esm::ActivationObserver*>(o)->Percentile(pctile);
+    auto it = p.find(key);
+    if (it == p.end()) throw std::runtime_error(std::string("no site ") + key);
+    *out = it->second;
+  });
+}
+
+// python/esm_cpp/quantize.py:35-47 (calibrate): ForwardWithObserver over each
+// sequence, then Percentile(pctile); stats_out[layer * 4 + site] with sites
+// attn_ln_output, attn_out, ffn_ln_output, inter_gelu (model.cpp:952-1050).
+int ref_model_observe(void* m, const int* ids_concat, const int* lens, int n, float pctile,
+                      float* stats_out) {
+  return Guard([&] {
+    auto* model = static_cast<esm::Model*>(m);
+    esm::ActivationObserver obs;
+    std::size_t off = 0;
+    for (int i = 0; i < n; ++i) {
+      model->ForwardWithObserver(
+          std::span<const std::int32_t>(ids_concat + off, static_cast<std::size_t>(lens[i])),
+          {}, &obs);
+      off += static_cast<std::size_t>(lens[i]);
+    }
+    auto p = obs.Percentile(pctile);
+    static const char* kSites[4] = {"attn_ln_output", "attn_out", "ffn_ln_output", "inter_gelu"};
+    const int L = model->config().num_hidden_layers;
+    for (int li = 0; li < L; ++li)
+      for (int j = 0; j < 4; ++j) {
+        auto it = p.find("layer" + std::to_string(li) + "." + kSites[j]);
+        stats_out[li * 4 + j] = it == p.end() ? 0.0f : it->second;
+      }
+  });
+}
+
+// Model::ApplySmoothQuant (model.cpp:1462-1468 -> smoothquant.cpp:100-185)
+// with the statistics given as stats[layer * 4 + site] (sites as above).
+int ref_model_apply_smoothquant(void* m, const float* stats, float alpha) {
+  return Guard([&] {
+    auto* model = static_cast<esm::Model*>(m);
+    static const char* kSites[4] = {"attn_ln_output", "attn_out", "ffn_ln_output", "inter_gelu"};
+    std::unordered_map<std::string, float> act;
+    const int L = model->config().num_hidden_layers;
+    for (int li = 0; li < L; ++li)
+      for (int j = 0; j < 4; ++j) act["layer" + std::to_string(li) + "." + kSites[j]] = stats[li * 4 + j];
+    model->ApplySmoothQuant(act, alpha);
   });
 }
 
