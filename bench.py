@@ -1,25 +1,40 @@
 """Headline benchmark: packed residues/s of the ESM-2 650M W8A8 varlen packed
-forward (BASELINE config 3a) on 1..8 B200s.
+forward (BASELINE config 3a) on 1..8 B200s, plus the other BASELINE configs
+as separate workloads.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload config3a|config3b|attn|gemm|dms3b]
 
-A step = ForwardScheduled over 256 synthetic sequences (residues ~ N(120,30)
-clipped to [90,250], + CLS/EOS; seed per rank) on random-init 650M weights
-(N(0,0.02), LN gamma 1 / beta 0) calibrated on the GPU (99.9th percentile),
-SmoothQuant-migrated (alpha 0.5) and quantised to per-channel int8.  With N
-GPUs (torchrun, one process per GPU) every rank runs its own 256 sequences on
-its own weight replica: weak scaling, no collective on the data path.
+config3a (default): one global workload of 256 * N synthetic sequences
+(residues ~ N(120,30) clipped to [90,250], + CLS/EOS; the first 256 are the
+same at every N) on random-init 650M weights (N(0,0.02), LN gamma 1 / beta 0)
+calibrated on the GPU (99.9th percentile), SmoothQuant-migrated (alpha 0.5)
+and quantised to per-channel int8.  PlanBatches cuts the whole set into
+packed groups and LPT assigns the groups to the N ranks (torchrun, one
+process per GPU, a weight replica each); no collective on the forward.
 
-  value  device-resident: inputs already in HBM, CUDA events on the model's
-         stream around each step, L2 flushed between steps (256 MB write;
-         the 0.8 GB of int8 weights streamed per step also exceed L2);
-         aggregate over ranks = sum of residues / max over ranks of the time.
-  e2e    the public API Model.forward_scheduled with host arrays in (pinned)
-         and host logits out, same events on the same stream.
+  value  device-resident: each rank's groups already in HBM, CUDA events on
+         the forward's stream, L2 flushed between steps (256 MB write; the
+         0.8 GB of int8 weights streamed per step also exceed L2); total
+         tokens / max over ranks of the step time.
+  e2e    the public API, host ids in and host logits out: Model.forward_scheduled
+         at N = 1, distributed.forward_scheduled_sharded_device at N > 1
+         (logits gathered to rank 0 over NCCL, then read back to its host).
   roofline  the INT8 GEMM family (tcgen05 kernels), algorithmic 2*M*N*K ops per
-         launch over their CUDA-event time inside the timed steps.
+         launch over their CUDA-event time inside one profiled step.
   cpu_baseline  the reference esm.cpp (compiled from its sources into
          oracle/_ref) on a bounded sample of the same workload, rank 0, N=1.
+
+The other workloads (run by hand; one JSON line each, rank 0):
+  config3b  a uniform batch of 8 x 256 tokens per GPU, the same weights.
+  attn      BASELINE config 1: varlen attention at 650M shape, 4096
+            sequences (about 490k tokens) per GPU, FP32 and the reference's
+            BF16 mode; achieved HBM GB/s.
+  gemm      BASELINE config 2: LinearInt8 (activation quantisation, int8
+            GEMM, dequant + bias) at M = 32768 for the four 650M shapes.
+  dms3b     BASELINE config 4: ESM-2 3B W8A8 (random init), the 400-residue
+            wild type and its 7600 substitutions (402 tokens each), sharded
+            over the N ranks by LPT.
 
 --impl reference times that reference CPU path alone (rank 0; other ranks
 exit 0) on a bounded sample per step, through its own API.
@@ -55,11 +70,49 @@ def _peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
-def _workload(rank: int):
+def _workload(world: int):
+    """256 sequences per GPU of one global workload (the first 256 are the
+    same at every N)."""
     from esm_b200 import synth
 
-    lens = synth.varlen_lengths(N_SEQS, seed=1000 + rank)
-    return synth.residue_ids(lens, seed=2000 + rank)
+    lens = synth.varlen_lengths(N_SEQS * world, seed=1000)
+    return synth.residue_ids(lens, seed=2000)
+
+
+def _workload_uniform(world: int):
+    """BASELINE config 3b: 8 sequences of 256 tokens per GPU."""
+    from esm_b200 import synth
+
+    return synth.residue_ids([254] * (8 * world), seed=7)
+
+
+def _workload_dms(world: int):
+    """the 400-residue wild type and all 7600 single-site
+    substitutions, 402 tokens each (the same set at every N)."""
+    from esm_b200 import synth
+
+    return synth.dms_sequences(seed=4)
+
+
+def _dms_max_batch(n_seqs: int, world: int) -> int:
+    """Groups of at most 256 sequences whose count is a multiple of the GPU
+    count (so LPT gives every GPU the same number of equal groups):
+    max_batch = ceil(n / (k * G)), k = ceil(n / (256 * G))."""
+    k = -(-n_seqs // (256 * world))
+    return -(-n_seqs // (k * world))
+
+
+WORKLOADS = {
+    "config3a": dict(name="esm2_650m_w8a8_varlen (BASELINE config 3a)", seqs=_workload,
+                     per_gpu="256 sequences", arch="esm2_650m", metric=METRIC),
+    "config3b": dict(name="esm2_650m_w8a8_uniform_8x256 (BASELINE config 3b)",
+                     seqs=_workload_uniform, per_gpu="8 sequences of 256 tokens", arch="esm2_650m",
+                     metric="residues/sec, ESM-2-650M W8A8 uniform 8x256 batch per B200"),
+    "dms3b": dict(name="esm2_3b_w8a8_dms (BASELINE config 4)", seqs=_workload_dms,
+                  per_gpu="7601 sequences of 402 tokens in total, sharded", arch="esm2_3b",
+                  metric="residues/sec, ESM-2-3B W8A8 deep-mutational-scan forward sharded over B200s",
+                  max_batch=_dms_max_batch, strong=True),
+}
 
 
 class ClockSampler:
@@ -111,11 +164,12 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def build_model(device: int, seed: int = 0):
+def build_model(device: int, seed: int = 0, arch: str = "esm2_650m"):
+    """Random init -> calibration on the GPU -> SmoothQuant -> int8."""
     from esm_b200 import synth
 
     t0 = time.time()
-    m = synth.quantized_650m(seed=seed, device=device)
+    m = synth.quantized_model(arch, seed=seed, device=device)
     m._ensure_device()
     return m, time.time() - t0
 
@@ -126,6 +180,9 @@ def build_model(device: int, seed: int = 0):
 # out-proj 97.0 MB, fc1 247.7 MB, fc2 253.2 MB).  Traffic grows with the
 # tokens of a launch (activations and outputs; the weights are ~3% of it).
 GEMM_DRAM_BYTES_PER_TOKEN_LAYER = 774.30e6 / 13305
+GEMM_TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of the layer case "
+                       "(profiles/gemm_i8_esm2_650m_group0.md), per token, scaled by this "
+                       "rank's tokens per GEMM launch")
 
 
 def gemm_ops_per_step(groups_T, cfg) -> float:
@@ -134,48 +191,15 @@ def gemm_ops_per_step(groups_T, cfg) -> float:
     return per_token * sum(groups_T)
 
 
-def run_ours(args, rank: int, world: int, local_rank: int, dist):
-    import ctypes as C
-
+def _timer(stream):
+    """CUDA-event timing of fn() on `stream` (the stream the model's kernels
+    run on), L2 flushed before each call; returns (ms list, launches)."""
     import torch
 
-    from esm_b200 import _lib, ops
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=stream.device)
 
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    model, init_s = build_model(local_rank)
-    cfg = model.config
-    seqs = _workload(rank)
-    lens = np.array([len(s) for s in seqs], np.int32)
-    tokens = int(lens.sum())
-
-    # Pre-plan and pre-pack the groups (the host part of ForwardScheduled) and
-    # place the inputs in HBM for the device-resident measurement.
-    plan = ops.plan_batches(lens, 1.2, 256)
-    groups = []
-    for g in plan:
-        ids = np.concatenate([seqs[i] for i in g]).astype(np.int32)
-        cu = np.concatenate([[0], np.cumsum(lens[g])]).astype(np.int32)
-        d_ids = torch.from_numpy(ids).to(dev)
-        d_logits = torch.empty((ids.size, cfg.vocab_size), dtype=torch.float32, device=dev)
-        groups.append((d_ids, cu, d_logits))
-    L = _lib.lib()
-    stream = torch.cuda.ExternalStream(L.esmcu_get_stream(model._ctx), device=dev)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-
-    def step_device():
-        n = 0
-        for d_ids, cu, d_logits in groups:
-            _lib.call("esmcu_model_forward_packed_device", model._dev, C.c_void_p(d_ids.data_ptr()),
-                      None, int(d_ids.numel()), cu.ctypes.data, int(cu.size - 1),
-                      C.c_void_p(d_logits.data_ptr()))
-            n += L.esmcu_model_last_launch_count(model._dev)
-        return n
-
-    def timed(fn, k, profile=False):
+    def timed(fn, k):
         ms, launches = [], 0
-        if profile:
-            model.set_profiling(True)
         for _ in range(k):
             with torch.cuda.stream(stream):
                 flush.zero_()
@@ -185,10 +209,64 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
             e1.record(stream)
             e1.synchronize()
             ms.append(e0.elapsed_time(e1))
-        prof = model.profile() if profile else None
-        if profile:
-            model.set_profiling(False)
-        return ms, launches, prof
+        return ms, launches
+
+    return timed
+
+
+def _reduce(dist, dev, vals, op):
+    """Max (or sum) over ranks of a list of floats."""
+    import torch
+
+    t = torch.tensor(vals, dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
+    return [float(x) for x in t]
+
+
+def run_ours(args, rank: int, world: int, local_rank: int, dist, wl: dict):
+    """BASELINE config 3a: one global workload of 256 * N sequences, planned
+    by PlanBatches and split over the N ranks by LPT; every rank runs its
+    groups on its own replica (no collective on the forward).
+
+    value: device-resident inputs, each rank's groups timed with CUDA events
+           on the forward's stream; total tokens / max over ranks.
+    e2e:   forward_scheduled_sharded_device (the multi-GPU public API): host
+           ids in (pinned staging), forward, logits gathered to rank 0 over
+           NCCL and read back to rank 0's host in caller order.  At N = 1 it
+           is Model.forward_scheduled (host ids in, host logits out)."""
+    import torch
+
+    from esm_b200 import distributed as D
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    stream = torch.cuda.current_stream(dev)
+    model, init_s = build_model(local_rank, arch=wl["arch"])
+    cfg = model.config
+    seqs = wl["seqs"](world)
+    lens = [len(s) for s in seqs]
+    max_batch = wl["max_batch"](len(seqs), world) if "max_batch" in wl else 256
+    sp = D.plan_shards(lens, world, cfg.hidden_size, 1.2, max_batch)
+    tokens_all = sum(lens)
+
+    # This rank's groups, packed and placed in HBM once.
+    mine = []
+    off = 0
+    local = torch.zeros((max(sp.max_tokens, 1), cfg.vocab_size), dtype=torch.float32, device=dev)
+    for gi in sp.assign[rank]:
+        ids, cu = D.pack_group(seqs, sp.plan, gi, sp.lens)
+        mine.append((torch.from_numpy(ids).to(dev), cu, off))
+        off += ids.shape[0]
+
+    def step_device():
+        n = 0
+        for d_ids, cu, o in mine:
+            model.forward_packed_device(d_ids, cu, local[o:o + d_ids.numel()])
+            n += model.last_launch_count()
+        return n
+
+    timed = _timer(stream)
 
     def barrier():
         torch.cuda.synchronize()
@@ -199,72 +277,77 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
     # ---- warmup, then K device-resident steps
     for _ in range(args.warmup):
         step_device()
-    _lib.call("esmcu_synchronize", model._ctx)
     barrier()
     with ClockSampler(local_rank) as clk:
-        dev_ms, launches, _ = timed(step_device, args.steps)
+        dev_ms, launches = timed(step_device, args.steps)
         barrier()
     clocks = clk.summary()
-    _lib.call("esmcu_synchronize", model._ctx)
-    # Per-section times from one more, untimed step with the model's
-    # section events on (the events would otherwise sit inside the timed steps).
-    _, _, prof = timed(step_device, 1, profile=True)
-    _lib.call("esmcu_synchronize", model._ctx)
+    # Per-section times from one more, untimed step with the model's section
+    # events on (the events would otherwise sit inside the timed steps).
+    model.set_profiling(True)
+    timed(step_device, 1)
+    prof = model.profile()
+    model.set_profiling(False)
 
-    # ---- e2e through the public API (host ids in, host logits out)
+    # ---- e2e through the public API (host ids in, host logits out on rank 0)
     pinned_seqs = [torch.from_numpy(s).pin_memory().numpy() for s in seqs]
+    if world == 1:
+        def step_e2e():
+            model.forward_scheduled(pinned_seqs, max_batch_size=max_batch)
+    else:
+        def step_e2e():
+            D.forward_scheduled_sharded_device(model, pinned_seqs, rank, world,
+                                               max_batch_size=max_batch)
     for _ in range(max(1, args.warmup)):
-        model.forward_scheduled(pinned_seqs)
+        step_e2e()
     barrier()
-    e2e_ms, _, _ = timed(lambda: model.forward_scheduled(pinned_seqs) and 0, args.steps)
+    e2e_ms, _ = timed(lambda: step_e2e() and 0, args.steps)
     barrier()
 
+    my_tokens = float(sp.tokens[rank])
     step_ms = sum(dev_ms) / len(dev_ms)
     e2e_step_ms = sum(e2e_ms) / len(e2e_ms)
-    vals = torch.tensor([step_ms, e2e_step_ms, float(tokens)], dtype=torch.float64, device=dev)
-    if dist is not None:
-        mx = vals.clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        sm = vals.clone()
-        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
-        step_ms_max, e2e_ms_max, tok_sum = float(mx[0]), float(mx[1]), float(sm[2])
-    else:
-        step_ms_max, e2e_ms_max, tok_sum = step_ms, e2e_step_ms, float(tokens)
-
+    step_ms_max, e2e_ms_max = _reduce(dist, dev, [step_ms, e2e_step_ms], "max")
+    launches_all, = _reduce(dist, dev, [float(launches)], "sum")
     if rank != 0:
         return None
 
     peaks, peak_kind = _peaks()
     gemm_sections = ("qkv_proj", "attn_out_proj", "fc1", "fc2")
-    gemm_ms = sum(prof.get(k, 0.0) for k in gemm_sections)  # one profiled step
-    ops_step = gemm_ops_per_step([int(g[0].numel()) for g in groups], cfg)
+    gemm_ms = sum(prof.get(k, 0.0) for k in gemm_sections)  # one profiled step, rank 0
+    ops_step = gemm_ops_per_step([int(g[0].numel()) for g in mine], cfg)
     achieved = ops_step / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else 0.0
     int8_peak = 2.0 * float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops", 1400.0)))
     sections = {k: round(v, 4) for k, v in sorted(prof.items(), key=lambda kv: -kv[1])}
 
     out = {
-        "metric": METRIC,
-        "value": round(tok_sum / (step_ms_max * 1e-3), 1),
+        "metric": wl["metric"],
+        "value": round(tokens_all / (step_ms_max * 1e-3), 1),
         "unit": "residues/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(step_ms_max, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int8", "data": "synthetic",
-        "config": {"workload": "esm2_650m_w8a8_varlen (BASELINE config 3a)",
-                   "seqs_per_gpu": N_SEQS, "tokens_per_gpu": tokens, "groups": len(groups),
-                   "act_quant": "per_tensor", "parallelism": f"replicas x{world}",
+        "higher_is_better": True, "scaling": "strong" if wl.get("strong") else "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": wl["name"], "per_gpu": wl["per_gpu"],
+                   "seqs": len(seqs), "tokens": tokens_all, "max_batch_size": max_batch,
+                   "groups": len(sp.plan), "groups_per_rank": [len(a) for a in sp.assign],
+                   "tokens_per_rank": sp.tokens, "lpt_imbalance": round(sp.imbalance, 4),
+                   "act_quant": "per_tensor",
+                   "parallelism": f"dp{world}: PlanBatches groups of one global workload, LPT over ranks",
                    "l2": "flushed between steps (256 MB write); 0.8 GB int8 weights per step > L2"},
-        "e2e": {"value": round(tok_sum / (e2e_ms_max * 1e-3), 1), "unit": "residues/s",
-                "h2d_bytes_per_step": int(sum(4 * s.size for s in seqs) + 4 * (len(seqs) + len(plan))),
-                "d2h_bytes_per_step": int(tokens * cfg.vocab_size * 4)},
-        "gpu_launches": int(launches),
+        "e2e": {"value": round(tokens_all / (e2e_ms_max * 1e-3), 1), "unit": "residues/s",
+                "h2d_bytes_per_step": int(4 * tokens_all + 4 * (len(seqs) + len(sp.plan))),
+                "d2h_bytes_per_step": int(tokens_all * cfg.vocab_size * 4),
+                "path": ("Model.forward_scheduled" if world == 1 else
+                         "distributed.forward_scheduled_sharded_device (NCCL gather of logits to rank 0)")},
+        "gpu_launches": int(launches_all),
         "roofline": {"kernel": "gemm_i8 (tcgen05 kind::i8; QKV/out/fc1/fc2)", "bound": "tensor",
                      "achieved": round(achieved, 1), "peak": round(int8_peak, 1), "unit": "TOP/s",
                      "frac": round(achieved / int8_peak, 4),
                      "peak_source": f"2 x bf16_tflops_sustained ({peak_kind}); dense INT8 = 2 x dense BF16",
-                     "traffic": round(GEMM_DRAM_BYTES_PER_TOKEN_LAYER * tokens / (4 * len(groups))),
+                     "traffic": round(GEMM_DRAM_BYTES_PER_TOKEN_LAYER * my_tokens / (4 * max(len(mine), 1))),
                      "traffic_unit": "bytes per launch (mean over the step's GEMM launches)",
-                     "traffic_source": "ncu capture of the first config-3a group, scaled by tokens"},
+                     "traffic_source": GEMM_TRAFFIC_SOURCE},
         "sections_ms_per_step": sections,
         "init_s": round(init_s, 1),
     }
@@ -272,10 +355,173 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
         out["clocks"] = clocks
     if world == 1 and not args.no_cpu_baseline:
         try:
-            out["cpu_baseline"] = cpu_baseline(model, seqs)
+            out["cpu_baseline"] = cpu_baseline(model, seqs, max_batch)
         except Exception as e:  # the baseline is reported, never required
             out["cpu_baseline"] = {"unavailable": str(e)[:200]}
     return out
+
+
+def _clocked(local_rank, fn):
+    with ClockSampler(local_rank) as clk:
+        r = fn()
+    return r, clk.summary()
+
+
+def run_attn(args, rank: int, world: int, local_rank: int, dist):
+    """AttentionVarlen at 650M shape (20 heads x 64) over
+    4096 sequences per GPU, lengths ~ N(120, 30) clipped to [90, 250] (about
+    490k tokens), Q/K/V drawn N(0, 1) on the device, Q scaled by 1/8 and
+    RoPE'd once before timing (the op's prologue).  Timed: the attention
+    kernel alone, FP32 and with ESM_AMX_ATTENTION=on (the reference's BF16
+    scores; the op-level entry first writes bf16-rounded copies of Q and K).
+    HBM roofline: algorithmic bytes = 4 * T * 1280 * 4 (Q, K, V read once,
+    O written once); the inputs (7.5 GB) exceed L2, so no flush is needed."""
+    import torch
+
+    from esm_b200 import ops, synth
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    H, DH = 20, 64
+    lens = synth.varlen_lengths(4096, seed=101 + rank)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    T = int(cu[-1])
+    g = torch.Generator(device=dev).manual_seed(102 + rank)
+    qkv = torch.randn((3, T, H, DH), generator=g, device=dev, dtype=torch.float32)
+    q, k, v = qkv[0], qkv[1], qkv[2]
+    cos_t, sin_t = ops.rope_build_tables(int(lens.max()), DH)
+    dcos, dsin, dcu = (torch.from_numpy(x).to(dev) for x in (cos_t, sin_t, cu))
+    ops.scale_inplace(q, 1.0 / 8.0)
+    ops.rope_apply_varlen(q, dcos, dsin, dcu, H, DH)
+    ops.rope_apply_varlen(k, dcos, dsin, dcu, H, DH)
+    out = torch.empty_like(q)
+    stream = torch.cuda.current_stream(dev)
+    res = {}
+    clocks = None
+    for mode in ("fp32", "bf16"):
+        if mode == "bf16":
+            os.environ["ESM_AMX_ATTENTION"] = "on"
+        else:
+            os.environ.pop("ESM_AMX_ATTENTION", None)
+        B = len(lens)
+
+        def step():
+            from esm_b200 import _lib
+            import ctypes as C
+            _lib.call("esmcu_attention_varlen", ops.context(local_rank), C.c_void_p(q.data_ptr()),
+                      C.c_void_p(k.data_ptr()), C.c_void_p(v.data_ptr()), C.c_void_p(dcu.data_ptr()),
+                      B, H, DH, C.c_void_p(out.data_ptr()))
+            return 1
+        for _ in range(max(args.warmup, 3)):
+            step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+        def run():
+            e0.record(stream)
+            for _ in range(args.steps):
+                step()
+            e1.record(stream)
+            e1.synchronize()
+            return e0.elapsed_time(e1) / args.steps
+        ms, clk = _clocked(local_rank, run)
+        clocks = clocks or clk
+        ms_max, = _reduce(dist, dev, [ms], "max")
+        res[mode] = ms_max
+    os.environ.pop("ESM_AMX_ATTENTION", None)
+    if rank != 0:
+        return None
+    peaks, peak_kind = _peaks()
+    tot = T * world
+    bytes_ = 4.0 * T * H * DH * 4
+    ach = bytes_ / (res["fp32"] * 1e-3) / 1e9
+    return {"metric": "tokens/sec, varlen attention op at 650M shape (BASELINE config 1)",
+            "value": round(tot / (res["fp32"] * 1e-3), 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(res["fp32"], 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": "attention_varlen_650m (BASELINE config 1)", "seqs_per_gpu": 4096,
+                       "tokens_per_gpu": T, "heads": H, "head_dim": DH,
+                       "l2": "inputs 7.5 GB per GPU > L2; not flushed"},
+            "bf16_mode": {"ms_per_step": round(res["bf16"], 4),
+                          "value": round(tot / (res["bf16"] * 1e-3), 1),
+                          "note": "ESM_AMX_ATTENTION=on: bf16-rounded Q/K scores, fp32 softmax and P.V; "
+                                  "the op-level entry writes rounded copies of Q and K first"},
+            "roofline": {"kernel": "attention_tma (tcgen05 kind::tf32, 3xTF32)", "bound": "hbm",
+                         "achieved": round(ach, 1), "peak": float(peaks["hbm_gbs"]), "unit": "GB/s",
+                         "frac": round(ach / float(peaks["hbm_gbs"]), 4),
+                         "peak_source": f"hbm_gbs ({peak_kind})",
+                         "algorithmic_bytes": bytes_, "traffic": None},
+            "clocks": clocks}
+
+
+def run_gemm(args, rank: int, world: int, local_rank: int, dist):
+    """LinearInt8 (per-tensor activation quantisation,
+    int8 tensor-core GEMM with int32 accumulation, fp32 dequant + bias) at
+    M = 32768 for the four 650M shapes.  A is fp32 N(0,1) with 1% of its
+    channels x20 (outliers), SmoothQuant-smoothed (alpha 0.5, the 99.9th
+    percentile of |A| as P_X) into the weights N(0,0.02), which are then
+    quantised per channel.  Timed per call (activation quantisation
+    included); inputs of 168-671 MB plus a 256 MB flush between calls."""
+    import torch
+
+    from esm_b200 import ops, prep
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    stream = torch.cuda.current_stream(dev)
+    timed = _timer(stream)
+    M = 32768
+    shapes = [("qkv", 1280, 3840), ("out", 1280, 1280), ("fc1", 1280, 5120), ("fc2", 5120, 1280)]
+    rng = np.random.default_rng(7 + rank)
+    per = {}
+    tot_ops = tot_ms = 0.0
+    clocks = None
+    for name, K, N in shapes:
+        A = rng.standard_normal((M, K), dtype=np.float32)
+        A[:, rng.choice(K, K // 100, replace=False)] *= np.float32(20.0)
+        W = (rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02))
+        p_x = np.float32(np.percentile(np.abs(A[::16]), 99.9))
+        s = prep.smoothquant_scales(np.full(K, p_x, np.float32), np.max(np.abs(W), axis=0), 0.5)
+        A = (A / s).astype(np.float32)
+        Wq, ws = prep.quantize_weight((W * s).astype(np.float32))
+        bias = (rng.standard_normal(N, dtype=np.float32) * np.float32(0.02))
+        dA, dW, dws, db = (torch.from_numpy(x).to(dev) for x in (A, Wq, ws, bias))
+
+        def step():
+            ops.linear_int8(dA, dW, dws, db)
+            return 4  # absmax, quantise, GEMM (+ the scale memset)
+        for _ in range(max(args.warmup, 3)):
+            step()
+        torch.cuda.synchronize()
+        (ms, _), clk = _clocked(local_rank, lambda: timed(step, args.steps))
+        clocks = clocks or clk
+        t, = _reduce(dist, dev, [sum(ms) / len(ms)], "max")
+        ops_ = 2.0 * M * N * K
+        per[name] = {"M": M, "K": K, "N": N, "ms": round(t, 4), "top_s": round(ops_ / t / 1e9, 1),
+                     "hbm_bytes": 4 * M * K + N * K + 4 * M * N}
+        tot_ops += ops_
+        tot_ms += t
+        del dA, dW, dws, db
+    if rank != 0:
+        return None
+    peaks, peak_kind = _peaks()
+    int8_peak = 2.0 * float(peaks["bf16_tflops"])
+    ach = tot_ops * world / (tot_ms * 1e-3) / 1e12
+    for v in per.values():
+        v["hbm_gbs"] = round(v["hbm_bytes"] / (v["ms"] * 1e-3) / 1e9, 1)
+    return {"metric": "TOP/s, W8A8 LinearInt8 sweep at 650M shapes, M=32768 (BASELINE config 2)",
+            "value": round(ach, 1), "unit": "TOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": round(tot_ms, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "linear_int8_sweep_650m (BASELINE config 2)", "shapes": per,
+                       "act_quant": "per_tensor", "l2": "flushed between calls (256 MB write)"},
+            "roofline": {"kernel": "gemm_i8 (tcgen05 kind::i8) + activation quantisation",
+                         "bound": "tensor", "achieved": round(ach / world, 1), "peak": round(int8_peak, 1),
+                         "unit": "TOP/s", "frac": round(ach / world / int8_peak, 4),
+                         "peak_source": f"2 x bf16_tflops burst ({peak_kind}); dense INT8 = 2 x dense BF16",
+                         "traffic": None},
+            "clocks": clocks}
 
 
 def _ref_threads():
@@ -284,7 +530,7 @@ def _ref_threads():
     return int(os.environ["ESM_NUM_THREADS"])
 
 
-def cpu_baseline(model, seqs):
+def cpu_baseline(model, seqs, max_batch: int = 256):
     """The reference's ForwardScheduled on a bounded sample of the same
     workload, same quantised weights (via GGUF), all host threads."""
     threads = _ref_threads()
@@ -308,7 +554,7 @@ def cpu_baseline(model, seqs):
     t = statistics.median(times)
     return {"value": round(toks / t, 1), "unit": "residues/s", "cores": threads, "kind": "reference",
             "isa": O.ref().ref_current_isa().decode(),
-            "sample": f"{len(sample)} of the {N_SEQS} sequences ({toks} tokens), ForwardScheduled, "
+            "sample": f"{len(sample)} of the {len(seqs)} sequences ({toks} tokens), ForwardScheduled, "
                       f"median of {len(times)}"}
 
 
@@ -332,7 +578,7 @@ def run_reference(args, rank: int):
         ref = O.RefModel(p)
     ref.calibrate_smoothquant(synth.residue_ids(synth.varlen_lengths(4, seed=1), seed=2), 99.9, 0.5)
     ref.quantize()
-    seqs = _workload(0)
+    seqs = _workload(1)
     sample = seqs[:CPU_SAMPLE_SEQS]
     toks = sum(len(s) for s in sample)
     for _ in range(args.warmup):
@@ -363,6 +609,8 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["config3a", "config3b", "attn", "gemm", "dms3b"],
+                    default="config3a")
     args = ap.parse_args(argv)
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -383,11 +631,16 @@ def main(argv=None):
         import torch.distributed as td
 
         torch.cuda.set_device(local_rank)
-        td.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+        td.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                               device_id=torch.device("cuda", local_rank))
         dist = td
     try:
-        out = run_ours(args, rank, world, local_rank, dist)
+        if args.workload == "attn":
+            out = run_attn(args, rank, world, local_rank, dist)
+        elif args.workload == "gemm":
+            out = run_gemm(args, rank, world, local_rank, dist)
+        else:
+            out = run_ours(args, rank, world, local_rank, dist, WORKLOADS[args.workload])
     finally:
         if dist is not None:
             dist.barrier()

@@ -437,6 +437,28 @@ class Model:
             return out
         return [logits[cu[b]:cu[b + 1]] for b in range(B)]
 
+    def forward_packed_device(self, d_ids, cu_seqlens, d_logits, d_masks=None):
+        """Model::ForwardPacked on device tensors (esmcu_model_forward_packed_device):
+        d_ids int32 [T] and d_logits float32 [T, V] (contiguous, on this model's
+        GPU), cu_seqlens host int32 [B + 1].  Runs on torch's current stream
+        of the device, so torch copies before and after it are ordered with
+        it; nothing is synchronised."""
+        import torch
+
+        self._ensure_device()
+        cu = np.ascontiguousarray(cu_seqlens, np.int32)
+        T, V = int(cu[-1]), self._cfg.vocab_size
+        if d_ids.dtype != torch.int32 or d_ids.numel() != T or not d_ids.is_contiguous():
+            raise ValueError("d_ids must be a contiguous int32 tensor of cu_seqlens[-1] elements")
+        if d_logits.dtype != torch.float32 or tuple(d_logits.shape) != (T, V) or not d_logits.is_contiguous():
+            raise ValueError("d_logits must be a contiguous float32 tensor [T, vocab]")
+        _lib.call("esmcu_set_stream", self._ctx,
+                  C.c_void_p(torch.cuda.current_stream(self.device).cuda_stream))
+        _lib.call("esmcu_model_forward_packed_device", self._dev, C.c_void_p(d_ids.data_ptr()),
+                  None if d_masks is None else C.c_void_p(d_masks.data_ptr()), T, cu.ctypes.data,
+                  cu.shape[0] - 1, C.c_void_p(d_logits.data_ptr()))
+        return d_logits
+
     def forward(self, input_ids, attention_mask=None):
         ids = np.ascontiguousarray(input_ids, np.int32)
         if ids.ndim != 1:

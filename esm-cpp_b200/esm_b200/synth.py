@@ -100,13 +100,19 @@ def pack(seqs):
     return np.concatenate(seqs).astype(np.int32), cu
 
 
-def quantized_650m(seed: int = 0, device: int = 0, calib_seqs: int = 32, alpha: float = 0.5,
-                   num_layers: int | None = None) -> Model:
-    """Config 3 weights: random init -> seeded calibration on the GPU
+def quantized_model(arch="esm2_650m", seed: int = 0, device: int = 0, calib_seqs: int = 32,
+                    alpha: float = 0.5, num_layers: int | None = None) -> Model:
+    """Config 3 / 4 weights: random init -> seeded calibration on the GPU
     (percentile 99.9) -> SmoothQuant(alpha) -> per-channel int8."""
-    m = random_model("esm2_650m", seed=seed, device=device, num_layers=num_layers)
+    m = random_model(arch, seed=seed, device=device, num_layers=num_layers)
     calib = residue_ids(varlen_lengths(calib_seqs, seed + 1), seed + 2)
     stats = m.calibrate(calib, 99.9)
     m.apply_smoothquant(stats, alpha)
     m.quantize_weights()
     return m
+
+
+def quantized_650m(seed: int = 0, device: int = 0, calib_seqs: int = 32, alpha: float = 0.5,
+                   num_layers: int | None = None) -> Model:
+    """BASELINE config 3 weights (ESM-2 650M)."""
+    return quantized_model("esm2_650m", seed, device, calib_seqs, alpha, num_layers)

@@ -31,7 +31,7 @@ def _workload():
     return synth.residue_ids(synth.varlen_lengths(23, seed=3, mean=40, sd=25, lo=1, hi=90), seed=4)
 
 
-def _worker(rank, world, port, outdir, fail_rank):
+def _worker(rank, world, port, outdir, fail_rank, max_batch=5, threshold=1.2):
     import datetime
 
     for p in (str(ROOT / "esm-cpp_b200"), str(ROOT / "oracle")):
@@ -57,7 +57,8 @@ def _worker(rank, world, port, outdir, fail_rank):
 
         try:
             out = forward_scheduled_sharded(run_group, _workload(), rank, world, d=64,
-                                            max_batch_size=5)
+                                            imbalance_threshold=threshold,
+                                            max_batch_size=max_batch)
             status = "ok"
         except Exception as e:  # noqa: BLE001
             out, status = None, f"error: {type(e).__name__}"
@@ -71,19 +72,27 @@ def _worker(rank, world, port, outdir, fail_rank):
             pass
 
 
-def _spawn(tmp_path, fail_rank=-1, world=2):
+def _spawn(tmp_path, fail_rank=-1, world=2, max_batch=5, threshold=1.2):
     import torch.multiprocessing as mp
 
-    mp.start_processes(_worker, args=(world, _port(), str(tmp_path), fail_rank), nprocs=world,
-                       join=True, start_method="spawn")
+    mp.start_processes(_worker, args=(world, _port(), str(tmp_path), fail_rank, max_batch, threshold),
+                       nprocs=world, join=True, start_method="spawn")
 
 
-def test_sharded_scheduled_forward_equals_single_process(tmp_path, O):
+@pytest.mark.parametrize("world,max_batch,threshold", [(2, 5, 1.2), (3, 12, 1000.0)])
+def test_sharded_scheduled_forward_equals_single_process(tmp_path, O, world, max_batch, threshold):
+    """(3, 12, no split): 23 sequences make two groups, so rank 2 runs none
+    and sends only padding; the two others hold different token counts."""
     from esm_b200 import synth
+    from esm_b200.distributed import plan_shards
 
-    _spawn(tmp_path)
-    assert (tmp_path / "status0.txt").read_text() == "ok"
-    assert (tmp_path / "status1.txt").read_text() == "ok"
+    _spawn(tmp_path, world=world, max_batch=max_batch, threshold=threshold)
+    for r in range(world):
+        assert (tmp_path / f"status{r}.txt").read_text() == "ok"
+    sp = plan_shards([len(s) for s in _workload()], world, 64, threshold, max_batch)
+    if world == 3:
+        assert sorted(len(a) for a in sp.assign) == [0, 1, 1]
+        assert len(set(sp.tokens)) == 3
     got = np.load(tmp_path / "out.npz")
     seqs = _workload()
     m = synth.random_model(TINY, seed=9)
@@ -91,7 +100,7 @@ def test_sharded_scheduled_forward_equals_single_process(tmp_path, O):
     from esm_b200.ops import plan_batches
 
     lens = [len(s) for s in seqs]
-    for g in plan_batches(np.array(lens, np.int32), 1.2, 5):  # same groups -> same numerics
+    for g in plan_batches(np.array(lens, np.int32), threshold, max_batch):  # same groups, same numerics
         ids = np.concatenate([seqs[i] for i in g])
         cu = np.concatenate([[0], np.cumsum([lens[i] for i in g])]).astype(np.int32)
         want = O.forward_packed(m, ids, cu)
