@@ -169,6 +169,20 @@ int esmcu_set_stream(esmcu_context* ctx, void* stream) {
 
 void* esmcu_get_stream(esmcu_context* ctx) { return ctx ? ctx->stream : nullptr; }
 
+int esmcu_set_math_mode(esmcu_context* ctx, int mode) {
+  if (ctx == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "null context");
+  if (mode != ESMCU_MATH_DEFAULT && mode != ESMCU_MATH_AVX512)
+    return fail(ESMCU_ERR_INVALID_ARGUMENT, "bad math mode");
+  ctx->math_mode = mode;
+  return ESMCU_OK;
+}
+
+int esmcu_get_math_mode(const esmcu_context* ctx, int* mode) {
+  if (ctx == nullptr || mode == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "null argument");
+  *mode = ctx->math_mode;
+  return ESMCU_OK;
+}
+
 int esmcu_synchronize(esmcu_context* ctx) {
   ESMCU_TRY(use_device(ctx));
   ESMCU_CUDA(cudaStreamSynchronize(ctx->stream));
@@ -389,6 +403,12 @@ int esmcu_layernorm(esmcu_context* ctx, const float* x, const float* gamma, cons
   ESMCU_TRY(check_ptr(gamma, "gamma"));
   ESMCU_TRY(check_ptr(beta, "beta"));
   ESMCU_TRY(check_ptr(out, "out"));
+  if (ctx->math_mode == ESMCU_MATH_AVX512) {
+    if (d % 16 != 0)
+      return fail(ESMCU_ERR_INVALID_ARGUMENT, "the AVX-512 math mode needs d % 16 == 0");
+    ESMCU_CUDA(launch_layernorm_avx(x, gamma, beta, eps, out, num_rows, d, nullptr, ctx->stream));
+    return ESMCU_OK;
+  }
   ESMCU_CUDA(launch_layernorm(x, gamma, beta, eps, out, num_rows, d, nullptr, nullptr, 0, nullptr,
                               ctx->stream));
   return ESMCU_OK;
@@ -399,6 +419,10 @@ int esmcu_gelu(esmcu_context* ctx, const float* x, float* out, size_t n) {
   if (n == 0) return ESMCU_OK;
   ESMCU_TRY(check_ptr(x, "x"));
   ESMCU_TRY(check_ptr(out, "out"));
+  if (ctx->math_mode == ESMCU_MATH_AVX512) {
+    ESMCU_CUDA(launch_gelu_avx(x, out, static_cast<long>(n), nullptr, ctx->stream));
+    return ESMCU_OK;
+  }
   ESMCU_CUDA(launch_gelu(x, out, static_cast<long>(n), ctx->stream));
   return ESMCU_OK;
 }
@@ -453,6 +477,14 @@ int esmcu_attention_varlen(esmcu_context* ctx, const float* q, const float* k, c
   for (int b = 0; b < B; ++b) {
     max_len = std::max(max_len, cu_h[b + 1] - cu_h[b]);
     min_len = std::min(min_len, cu_h[b + 1] - cu_h[b]);
+  }
+  if (ctx->math_mode == ESMCU_MATH_AVX512) {
+    if (dh != 16 && dh != 32 && dh != 64)
+      return fail(ESMCU_ERR_INVALID_ARGUMENT, "the AVX-512 math mode needs head_dim 16, 32 or 64");
+    if (max_len == 0) return ESMCU_OK;
+    ESMCU_CUDA(launch_attention_avx(q, k, v, cu, B, H, dh, cu_h[B], max_len, out, nullptr,
+                                    ctx->stream));
+    return ESMCU_OK;
   }
   const bool qk_bf16 = attention_bf16_enabled(dh);
   if (qk_bf16) {

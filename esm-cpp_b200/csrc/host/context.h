@@ -19,6 +19,7 @@ struct esmcu_context {
   // absmax, scales, padded weights).  Grows between calls, never shrinks.
   void* scratch = nullptr;
   size_t scratch_bytes = 0;
+  int math_mode = 0;  // esmcu_math_mode
 };
 
 namespace esmb200 {

@@ -338,9 +338,12 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
   float2* lnstat = reinterpret_cast<float2*>(base + a.lnstat);
   // LayerNorm + per-tensor quantisation in one kernel (no fp32 LN output)
   // unless an observer needs that output.
-  const bool ln_fused = quant && !per_token && obs == nullptr && d % 128 == 0 &&
+  // Reference-rounding mode: LayerNorm, GELU and attention reproduce the
+  // reference's default x86 kernels (refmath.cu), unfused.
+  const bool avx = ctx->math_mode == ESMCU_MATH_AVX512;
+  const bool ln_fused = quant && !per_token && obs == nullptr && !avx && d % 128 == 0 &&
                         (d <= 2048 || d == 2560);
-  const bool qk_bf16 = attention_bf16_enabled(c.head_dim);
+  const bool qk_bf16 = !avx && attention_bf16_enabled(c.head_dim);
   LAUNCH(m, launch_positions(cu, B, pos, s));
   sec.begin("embed");
   LAUNCH(m, launch_embed(m->embed, d, ids, mk, cu, B, c.mask_token_id, hidden, s));
@@ -404,6 +407,9 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
     if (ln_fused) {
       LAUNCH(m, launch_layernorm_quant(hidden, L.ln1_w, L.ln1_b, c.layer_norm_eps, T, d, am, lnstat,
                                        ln_sync + 2 * li, q8, m->ldk_d, ascale, ctx->d_status, s));
+    } else if (avx) {
+      LAUNCH(m, launch_layernorm_avx(hidden, L.ln1_w, L.ln1_b, c.layer_norm_eps, ln, T, d,
+                                     quant && !per_token ? am : nullptr, s));
     } else if (quant && per_token) {
       LAUNCH(m, launch_layernorm(hidden, L.ln1_w, L.ln1_b, c.layer_norm_eps, nullptr, T, d, nullptr,
                                  q8, m->ldk_d, ascale, s));
@@ -413,7 +419,7 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
     }
     sec.end();
     TRY(observe(li, 0, ln, Td));
-    if (quant && !per_token && !ln_fused) {
+    if (quant && (avx || !per_token) && !ln_fused) {
       sec.begin("quantize");
       TRY(quantize(ln, d, m->ldk_d, am));
       sec.end();
@@ -455,9 +461,14 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
     sec.begin("attention");
     // With ESM_AMX_ATTENTION, q and k arrive rounded to bf16 from the QKV
     // epilogue or the split kernel.
-    LAUNCH(m, launch_attention_varlen(q, k, v, cu, B, H, dh, T, a.min_len, max_len, attn,
-                                      (quant && !per_token) ? am + 1 * kAmaxSlots : nullptr,
-                                      ctx->d_status, ctx->num_sms, s, qk_bf16));
+    if (avx) {
+      LAUNCH(m, launch_attention_avx(q, k, v, cu, B, H, dh, T, max_len, attn,
+                                     (quant && !per_token) ? am + 1 * kAmaxSlots : nullptr, s));
+    } else {
+      LAUNCH(m, launch_attention_varlen(q, k, v, cu, B, H, dh, T, a.min_len, max_len, attn,
+                                        (quant && !per_token) ? am + 1 * kAmaxSlots : nullptr,
+                                        ctx->d_status, ctx->num_sms, s, qk_bf16));
+    }
     sec.end();
     TRY(observe(li, 1, attn, Td));
     if (quant) {
@@ -487,6 +498,10 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
       LAUNCH(m, launch_layernorm_quant(hidden, L.ln2_w, L.ln2_b, c.layer_norm_eps, T, d,
                                        am + 2 * kAmaxSlots, lnstat, ln_sync + 2 * li + 1, q8,
                                        m->ldk_d, ascale, ctx->d_status, s));
+    } else if (avx) {
+      LAUNCH(m, launch_layernorm_avx(hidden, L.ln2_w, L.ln2_b, c.layer_norm_eps, ln, T, d,
+                                     quant && !per_token && !round0 ? am + 2 * kAmaxSlots : nullptr,
+                                     s));
     } else if (quant && per_token && !round0) {
       LAUNCH(m, launch_layernorm(hidden, L.ln2_w, L.ln2_b, c.layer_norm_eps, nullptr, T, d, nullptr,
                                  q8, m->ldk_d, ascale, s));
@@ -500,7 +515,7 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
     if (round0)
       LAUNCH(m, launch_round_fp16(ln, static_cast<long>(Td), quant && !per_token ? am + 2 * kAmaxSlots : nullptr,
                                   s));
-    if (quant && (round0 || (!per_token && !ln_fused))) {
+    if (quant && (round0 || avx || (!per_token && !ln_fused))) {
       sec.begin("quantize");
       TRY(quantize(ln, d, m->ldk_d, am + 2 * kAmaxSlots));
       sec.end();
@@ -508,15 +523,18 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
     sec.begin("fc1");
     {
       EpiParams e;
-      e.kind = kEpiGelu;  // fc1 -> GELU (model.cpp:1036-1046)
+      e.kind = avx ? kEpiStore : kEpiGelu;  // fc1 -> GELU (model.cpp:1036-1046)
       e.C = inter;
       e.ldc = ffn;
       if (quant) {
-        e.amax = per_token ? nullptr : am + 3 * kAmaxSlots;
+        e.amax = per_token || avx ? nullptr : am + 3 * kAmaxSlots;
         TRY(gemm_i8(L.w1, m->ldk_d, ffn, L.s1, L.b1, e));
       } else {
         TRY(gemm_f32(ln, d, L.f1, ffn, L.b1, e));
       }
+      if (avx)
+        LAUNCH(m, launch_gelu_avx(inter, inter, static_cast<long>(T) * ffn,
+                                  quant && !per_token ? am + 3 * kAmaxSlots : nullptr, s));
     }
     sec.end();
     TRY(observe(li, 3, inter, static_cast<size_t>(T) * ffn));
@@ -550,8 +568,12 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
   const bool lm_int8 = m->lm_wq != nullptr;
   uint32_t* am_lm = amax + 4 * c.num_layers * kAmaxSlots;
   sec.begin("final_ln");
-  LAUNCH(m, launch_layernorm(hidden, m->final_ln_w, m->final_ln_b, c.layer_norm_eps, ln, T, d,
-                             lm_int8 && !per_token ? am_lm : nullptr, nullptr, 0, nullptr, s));
+  if (avx)
+    LAUNCH(m, launch_layernorm_avx(hidden, m->final_ln_w, m->final_ln_b, c.layer_norm_eps, ln, T,
+                                   d, lm_int8 && !per_token ? am_lm : nullptr, s));
+  else
+    LAUNCH(m, launch_layernorm(hidden, m->final_ln_w, m->final_ln_b, c.layer_norm_eps, ln, T, d,
+                               lm_int8 && !per_token ? am_lm : nullptr, nullptr, 0, nullptr, s));
   sec.end();
   if (hidden_out)  // the last entry is the final LayerNorm's output
     ESMCU_CUDA(cudaMemcpyAsync(hidden_out + static_cast<size_t>(c.num_layers) * Tdh, ln, Tdh * 4,
@@ -568,7 +590,7 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
   sec.begin("lm_dense");
   {
     EpiParams e;
-    e.kind = kEpiGelu;  // dense -> GELU (model.cpp:1192-1223)
+    e.kind = avx ? kEpiStore : kEpiGelu;  // dense -> GELU (model.cpp:1192-1223)
     e.C = attn;
     e.ldc = d;
     if (lm_int8) {  // LinearInt8 (model.cpp:1209-1211)
@@ -596,11 +618,15 @@ int forward_device(esmcu_model* m, const Arena& a, const int* ids, const int* mk
     } else {
       TRY(gemm_f32(head_in, d, m->lm_w, d, m->lm_b, e, TH));
     }
+    if (avx) LAUNCH(m, launch_gelu_avx(attn, attn, static_cast<long>(TH) * d, nullptr, s));
   }
   sec.end();
   sec.begin("lm_ln");
-  LAUNCH(m, launch_layernorm(attn, m->lm_ln_w, m->lm_ln_b, c.layer_norm_eps, q, TH, d, nullptr,
-                             nullptr, 0, nullptr, s));
+  if (avx)
+    LAUNCH(m, launch_layernorm_avx(attn, m->lm_ln_w, m->lm_ln_b, c.layer_norm_eps, q, TH, d, nullptr, s));
+  else
+    LAUNCH(m, launch_layernorm(attn, m->lm_ln_w, m->lm_ln_b, c.layer_norm_eps, q, TH, d, nullptr,
+                               nullptr, 0, nullptr, s));
   sec.end();
   sec.begin("lm_decoder");
   {

@@ -182,4 +182,17 @@ cudaError_t launch_log_softmax_rows(float* x, int R, int V, cudaStream_t s);
 cudaError_t launch_embed(const float* embed_w, int d, const int* ids, const int* masks,
                          const int* cu, int B, int mask_id, float* out, cudaStream_t s);
 
+// ---------------------------------------------- reference-rounding mode
+// The reference's default x86 kernels bit for bit (refmath.cu).
+// LayerNormAvx512: d % 16 == 0; amax (nullable) gets max|y|.
+cudaError_t launch_layernorm_avx(const float* x, const float* g, const float* b, float eps,
+                                 float* out, int rows, int d, uint32_t* amax, cudaStream_t s);
+// GeluAvx512 over n values (in place allowed); amax (nullable) gets max|y|.
+cudaError_t launch_gelu_avx(const float* x, float* y, long n, uint32_t* amax, cudaStream_t s);
+// AttentionVarlenAvx512, q/k/v/out [T, H, dh], dh in {16, 32, 64}; max_len
+// = the longest sequence; amax (nullable) gets max|out|.
+cudaError_t launch_attention_avx(const float* q, const float* k, const float* v, const int* cu,
+                                 int B, int H, int dh, int T, int max_len, float* out,
+                                 uint32_t* amax, cudaStream_t s);
+
 }  // namespace esmb200

@@ -57,6 +57,9 @@ class LayerWeights(C.Structure):
 _lib = None
 
 _VP = C.c_void_p
+MATH_DEFAULT, MATH_AVX512 = 0, 1  # esmcu_math_mode
+MATH_MODES = {"default": MATH_DEFAULT, "avx512": MATH_AVX512}
+
 _SIGS = {
     "esmcu_last_error": (C.c_char_p, []),
     "esmcu_version": (C.c_char_p, []),
@@ -67,6 +70,8 @@ _SIGS = {
     "esmcu_get_stream": (_VP, [_VP]),
     "esmcu_synchronize": (C.c_int, [_VP]),
     "esmcu_bounded_wait_selftest": (C.c_int, [_VP, C.c_int, C.POINTER(C.c_int)]),
+    "esmcu_set_math_mode": (C.c_int, [_VP, C.c_int]),
+    "esmcu_get_math_mode": (C.c_int, [_VP, C.POINTER(C.c_int)]),
     "esmcu_malloc": (C.c_int, [_VP, C.c_size_t, C.POINTER(_VP)]),
     "esmcu_free": (C.c_int, [_VP, _VP]),
     "esmcu_memcpy_h2d": (C.c_int, [_VP, _VP, _VP, C.c_size_t]),

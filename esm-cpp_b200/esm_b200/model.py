@@ -253,6 +253,14 @@ class Model:
         self.act_quant = mode
         self._dirty = True
 
+    def set_math_mode(self, mode: str) -> None:
+        """"default" or "avx512": with "avx512" this model's forwards run
+        LayerNorm, GELU and attention with the reference's default x86
+        arithmetic bit for bit (esmcu_math_mode ESMCU_MATH_AVX512), so a W8A8
+        forward reproduces the reference's default path layer by layer."""
+        self._ensure_device()
+        _lib.call("esmcu_set_math_mode", self._ctx, _lib.MATH_MODES[mode])
+
     def set_first_block_fc1_fp16(self, enabled: bool) -> None:
         """Config::first_block_fc1_fp16: round layer 0's fc1 input to fp16
         precision (model.cpp:1031-1033); saved as esm.first_block_fc1_fp16."""

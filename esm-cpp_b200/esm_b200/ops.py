@@ -37,6 +37,13 @@ def _dev(t):
     return t.device.index or 0
 
 
+def set_math_mode(mode: str, device: int = 0) -> None:
+    """esmcu_set_math_mode on the facade's context of `device`: "default"
+    (tensor-core / fused kernels) or "avx512" (LayerNorm, GELU and attention
+    reproduce the reference's default x86 kernels bit for bit)."""
+    _lib.call("esmcu_set_math_mode", context(device), _lib.MATH_MODES[mode])
+
+
 def synchronize(device: int = 0):
     _lib.call("esmcu_synchronize", context(device))
 

@@ -69,6 +69,23 @@ int esmcu_set_stream(esmcu_context* ctx, void* cuda_stream);
 void* esmcu_get_stream(esmcu_context* ctx);
 /* Waits for the stream and reports device-side failures (timeouts). */
 int esmcu_synchronize(esmcu_context* ctx);
+/* Arithmetic of the LayerNorm, GELU and attention kernels (facade calls and
+ * the forwards of models on this context).
+ *   ESMCU_MATH_DEFAULT  the tensor-core / fused kernels, within the FP32
+ *                       class of the reference's scalar twins.
+ *   ESMCU_MATH_AVX512   the reference's default x86 kernels bit for bit:
+ *                       LayerNormAvx512 (layernorm.cpp:59-149), GeluAvx512
+ *                       (gelu.cpp:48-148) and AttentionVarlenAvx512
+ *                       (attention.cpp:230-437, 770-811) as its release build
+ *                       rounds them; with the INT8 GEMMs already exact, a W8A8
+ *                       forward then reproduces the reference's default path
+ *                       layer by layer.  SIMT kernels, several times slower;
+ *                       needs hidden and head dims that are multiples of 16
+ *                       (head_dim 16, 32 or 64); the FP32 attention form
+ *                       (ESM_AMX_ATTENTION is not applied in this mode). */
+typedef enum { ESMCU_MATH_DEFAULT = 0, ESMCU_MATH_AVX512 = 1 } esmcu_math_mode;
+int esmcu_set_math_mode(esmcu_context* ctx, int mode);
+int esmcu_get_math_mode(const esmcu_context* ctx, int* mode);
 /* Failure-detection self-test; no counterpart in the reference, which has no
  * device waits.  Runs one small kernel whose mbarrier waits can never
  * complete (one of two expected arrivals is made) and must give up after

@@ -63,6 +63,19 @@ void orc_embed(const float* embed_w, int d, const int* ids, const int* masks,
 int orc_plan_batches(const int* lengths, int n, float threshold, int max_batch,
                      int* order_out, int* group_sizes_out);
 
+/* The reference's default x86 kernels, bit for bit (esm_oracle_avx.c). */
+/* layernorm.cpp:59-149 LayerNormAvx512, d % 16 == 0 */
+void orc_layernorm_avx(const float* x, const float* g, const float* b, float eps, float* out,
+                       int rows, int d);
+/* gelu.cpp:48-148 GeluAvx512 */
+void orc_gelu_avx(const float* x, float* out, size_t n);
+/* the C library's expf (used by AttentionVarlenAvx512 past whole 16-key blocks) */
+float orc_expf_libc(float x);
+/* attention.cpp:230-437, 770-811 AttentionVarlenAvx512, head_dim % 16 == 0,
+ * scratch of max_len floats */
+void orc_attention_avx(const float* q, const float* k, const float* v, const int* cu, int B,
+                       int H, int dh, float* out, float* scratch);
+
 #ifdef __cplusplus
 }
 #endif

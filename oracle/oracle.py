@@ -75,6 +75,10 @@ _ORC_SIGS = {
     "orc_attention_varlen": (None, [_VP, _VP, _VP, _VP, _I, _I, _I, _VP]),
     "orc_embed": (None, [_VP, _I, _VP, _VP, _VP, _I, _I, _VP]),
     "orc_plan_batches": (_I, [_VP, _I, _F, _I, _VP, _VP]),
+    "orc_layernorm_avx": (None, [_VP, _VP, _VP, _F, _VP, _I, _I]),
+    "orc_gelu_avx": (None, [_VP, _VP, _SZ]),
+    "orc_expf_libc": (_F, [_F]),
+    "orc_attention_avx": (None, [_VP, _VP, _VP, _VP, _I, _I, _I, _VP, _VP]),
 }
 _REF_SIGS = {
     "ref_last_error": (C.c_char_p, []),
@@ -251,6 +255,43 @@ def gelu(x):
     x = _a(x)
     out = np.zeros_like(x)
     orc().orc_gelu(x.ctypes.data, out.ctypes.data, x.size)
+    return out
+
+
+def layernorm_avx(x, g, b, eps=1e-5):
+    """LayerNormAvx512 (layernorm.cpp:59-149) bit for bit, d % 16 == 0."""
+    x = _a(x)
+    out = np.zeros_like(x)
+    rows, d = x.shape
+    orc().orc_layernorm_avx(x.ctypes.data, _a(g).ctypes.data, _a(b).ctypes.data, C.c_float(eps),
+                            out.ctypes.data, rows, d)
+    return out
+
+
+def gelu_avx(x):
+    """GeluAvx512 (gelu.cpp:48-148) bit for bit."""
+    x = _a(x)
+    out = np.zeros_like(x)
+    orc().orc_gelu_avx(x.ctypes.data, out.ctypes.data, x.size)
+    return out
+
+
+def expf_libc(x) -> np.ndarray:
+    """The C library's expf, restated (orc_expf_libc), elementwise."""
+    x = _a(x).ravel()
+    f = orc().orc_expf_libc
+    return np.array([f(float(v)) for v in x], F32)
+
+
+def attention_avx(q, k, v, cu, H, dh):
+    """AttentionVarlenAvx512 (attention.cpp:230-437, 770-811) bit for bit."""
+    q, k, v = _a(q), _a(k), _a(v)
+    cu = _a(cu, np.int32)
+    out = np.zeros_like(q)
+    maxL = int(np.max(np.diff(cu))) if cu.size > 1 else 1
+    scratch = np.zeros(max(maxL, 1) + 16, F32)
+    orc().orc_attention_avx(q.ctypes.data, k.ctypes.data, v.ctypes.data, cu.ctypes.data,
+                            cu.size - 1, H, dh, out.ctypes.data, scratch.ctypes.data)
     return out
 
 

@@ -126,3 +126,28 @@ def test_3b_w8a8_dms_scheduled_matches_reference(q8, O, record):
     record("3b_w8a8_dms_scheduled", pearson_min=min(ps), max_abs_err=err)
     assert min(ps) >= PEARSON_W8A8, ps
     assert err <= ATOL_W8A8 + 1e-3 * max(float(np.abs(w).max()) for w in want)
+
+
+def test_3b_w8a8_avx512_mode_reproduces_reference_layer_by_layer(q8, O, record):
+    """ESMCU_MATH_AVX512 at 3B width: every hidden state bit-identical to
+    the reference's default path (VNNI), including the 402-token DMS length;
+    logits to the FP32 class (the LM head's GEMMs sum in another order)."""
+    from esm_b200 import synth
+
+    m, ref = q8
+    m.set_math_mode("avx512")
+    try:
+        O.ref_force_isa("avx512vnni")
+        try:
+            for s in [synth.dms_sequences(seed=4)[1]] + synth.residue_ids([93], seed=5):
+                logits, hs = m.forward_with_hidden_states(s)
+                rlogits, rh = ref.forward_hidden(s)
+                for li in range(len(hs)):
+                    assert np.array_equal(hs[li].view(np.uint32), rh[li].view(np.uint32)), li
+                rel = float((np.abs(logits - rlogits) / (1 + np.abs(rlogits))).max())
+                assert rel <= 1e-4, rel
+        finally:
+            O.ref_force_isa(None)
+        record("3b_w8a8_avx512_mode", hidden_states_bit_exact=True, max_rel_err=rel)
+    finally:
+        m.set_math_mode("default")

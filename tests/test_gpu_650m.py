@@ -152,3 +152,44 @@ def test_650m_w8a8_int8_code_flips_per_layer(q8, O, record):
            logits_pearson=pears)
     assert frac[0] == 0.0  # the embedding output is bit-identical
     assert min(pears) >= W8A8_PEARSON_650M, pears
+
+
+def test_650m_w8a8_avx512_mode_reproduces_reference_layer_by_layer(q8, O, record):
+    """esmcu_math_mode ESMCU_MATH_AVX512: LayerNorm, GELU and attention take
+    the reference's default x86 arithmetic, the INT8 GEMMs are exact, so
+    every hidden state of a W8A8 forward -- all 33 layers and the final
+    LayerNorm -- equals the reference's default path (VNNI) bit for bit.
+    Only the FP32 LM head's two GEMMs sum in a different order, so the
+    logits agree to the FP32 class (1e-4 * (1 + |ref|), Pearson 0.99999);
+    the per-tensor scale of every layer, hence every int8 code, is the
+    reference's.  The packed config-3a group is checked the same way."""
+    from esm_b200 import synth
+
+    m, ref = q8
+    m.set_math_mode("avx512")
+    try:
+        seqs = synth.residue_ids(synth.varlen_lengths(3, seed=31), seed=32)
+        O.ref_force_isa("avx512vnni")
+        try:
+            for s in seqs:
+                logits, hs = m.forward_with_hidden_states(s)
+                rlogits, rh = ref.forward_hidden(s)
+                for li in range(len(hs)):
+                    assert np.array_equal(hs[li].view(np.uint32), rh[li].view(np.uint32)), (
+                        f"hidden state {li}: {np.count_nonzero(hs[li] != rh[li])} values differ")
+                rel = float((np.abs(logits - rlogits) / (1 + np.abs(rlogits))).max())
+                assert rel <= 1e-4, rel
+                assert np.corrcoef(logits.ravel(), rlogits.ravel())[0, 1] >= 0.99999
+            ids, cu = _config_input("config3a")
+            got = m.forward_packed(ids, cu, out=np.empty((ids.size, 33), np.float32))
+            want = ref.forward_packed(ids, cu)
+        finally:
+            O.ref_force_isa(None)
+        rel = float((np.abs(got - want) / (1 + np.abs(want))).max())
+        ps = _pearsons(got, want, cu)
+        record("650m_w8a8_avx512_mode", hidden_states_bit_exact=True, max_rel_err=rel,
+               pearson_min=min(ps))
+        assert rel <= 1e-4, rel
+        assert min(ps) >= 0.99999, ps
+    finally:
+        m.set_math_mode("default")
