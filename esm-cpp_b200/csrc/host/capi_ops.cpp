@@ -304,7 +304,7 @@ int esmcu_quantize_weights(esmcu_context* ctx, const float* W, int N, int K, int
   }
   ESMCU_TRY(check_ptr(W, "W"));
   ESMCU_TRY(check_ptr(q, "q"));
-  ESMCU_CUDA(launch_quantize_weights(W, N, K, q, scales, ctx->stream));
+  ESMCU_CUDA(launch_quantize_weights(W, N, K, q, K, scales, ctx->stream));
   return ESMCU_OK;
 }
 

@@ -1061,6 +1061,206 @@ int esmcu_model_set_layer(esmcu_model* m, int layer, const esmcu_layer_weights* 
   return ESMCU_OK;
 }
 
+// ---- on-device weight preparation
+
+namespace {
+
+// SmoothQuantScales (smoothquant.cpp:49-74) for one channel, with the same
+// float arithmetic and C library powf as the reference.
+float smooth_scale(float px, float pw, float alpha) {
+  if (px <= 0.0f || pw <= 0.0f) return 1.0f;
+  const float num = std::pow(px, alpha);
+  const float den = std::pow(pw, 1.0f - alpha);
+  float val = num / den;
+  if (!std::isfinite(val) || val <= 0.0f) return 1.0f;
+  if (val < 1e-3f) val = 1e-3f;
+  if (val > 1e3f) val = 1e3f;
+  return val;
+}
+
+// Column absmax of a device [N, K] matrix, to the host.
+int col_absmax_host(esmcu_model* m, const float* W, int N, int K, uint32_t* d_tmp,
+                    std::vector<float>* out) {
+  cudaStream_t s = m->ctx->stream;
+  ESMCU_CUDA(launch_col_absmax(W, N, K, d_tmp, s));
+  out->resize(static_cast<size_t>(K));
+  ESMCU_CUDA(cudaMemcpyAsync(out->data(), d_tmp, static_cast<size_t>(K) * 4, cudaMemcpyDeviceToHost, s));
+  ESMCU_CUDA(cudaStreamSynchronize(s));
+  return ESMCU_OK;
+}
+
+void release(esmcu_model* m, void* p) {
+  if (p == nullptr) return;
+  cudaFree(p);
+  m->owned.erase(std::remove(m->owned.begin(), m->owned.end(), p), m->owned.end());
+}
+
+// Quantize (pack.cpp:149-177) of a device FP32 [N, K] matrix into freshly
+// allocated int8 rows of stride ldk (zero padding) and [N] scales.
+int quantize_device(esmcu_model* m, const float* W, int N, int K, long ldk, int8_t** q,
+                    float** scales) {
+  cudaStream_t s = m->ctx->stream;
+  void* pq = nullptr;
+  void* ps = nullptr;
+  ESMCU_CUDA(cudaMalloc(&pq, static_cast<size_t>(N) * ldk));
+  m->owned.push_back(pq);
+  ESMCU_CUDA(cudaMalloc(&ps, static_cast<size_t>(N) * 4));
+  m->owned.push_back(ps);
+  ESMCU_CUDA(cudaMemsetAsync(pq, 0, static_cast<size_t>(N) * ldk, s));
+  ESMCU_CUDA(launch_quantize_weights(W, N, K, static_cast<int8_t*>(pq), ldk, static_cast<float*>(ps), s));
+  *q = static_cast<int8_t*>(pq);
+  *scales = static_cast<float*>(ps);
+  return ESMCU_OK;
+}
+
+int copy_out(void* dst, const void* src, size_t bytes) {
+  if (dst == nullptr) return ESMCU_OK;
+  if (src == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "the model holds no such tensor");
+  ESMCU_CUDA(cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost));
+  return ESMCU_OK;
+}
+
+// Rows [r0, r0 + n) of a device int8 matrix with row stride ldk, K bytes each,
+// to dense host rows.
+int copy_out_i8(int8_t* dst, const int8_t* src, long r0, int n, int K, long ldk) {
+  if (dst == nullptr) return ESMCU_OK;
+  if (src == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "the model holds no int8 weights");
+  ESMCU_CUDA(cudaMemcpy2D(dst, static_cast<size_t>(K), src + r0 * ldk, static_cast<size_t>(ldk),
+                          static_cast<size_t>(K), static_cast<size_t>(n), cudaMemcpyDeviceToHost));
+  return ESMCU_OK;
+}
+
+}  // namespace
+
+int esmcu_model_apply_smoothquant(esmcu_model* m, const float* stats, float alpha) {
+  if (m == nullptr || stats == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "null argument");
+  TRY(use_device(m->ctx));
+  if (!model_ready(m)) return fail(ESMCU_ERR_INVALID_ARGUMENT, "model weights are not fully set");
+  if (m->cfg.weights_quantized)
+    return fail(ESMCU_ERR_INVALID_ARGUMENT, "apply_smoothquant runs on FP32 weights, before quantize");
+  const int d = m->cfg.hidden_size, ffn = m->cfg.intermediate_size;
+  cudaStream_t s = m->ctx->stream;
+  void* tmp = nullptr;  // column maxima, then the scales
+  ESMCU_CUDA(cudaMalloc(&tmp, static_cast<size_t>(std::max(d, ffn)) * 8));
+  uint32_t* d_cmax = static_cast<uint32_t*>(tmp);
+  float* d_s = reinterpret_cast<float*>(d_cmax + std::max(d, ffn));
+  auto scales = [&](float px, const std::vector<float>& pw) {
+    std::vector<float> sc(pw.size());
+    for (size_t k = 0; k < pw.size(); ++k) sc[k] = smooth_scale(px, pw[k], alpha);
+    return sc;
+  };
+  auto upload_s = [&](const std::vector<float>& sc) -> int {
+    ESMCU_CUDA(cudaMemcpyAsync(d_s, sc.data(), sc.size() * 4, cudaMemcpyHostToDevice, s));
+    return ESMCU_OK;
+  };
+  int rc = ESMCU_OK;
+  std::vector<float> pw;
+  for (int li = 0; li < m->cfg.num_layers && rc == ESMCU_OK; ++li) {
+    DevLayer& L = m->layers[static_cast<size_t>(li)];
+    auto step = [&]() -> int {
+      // Site 1: attn_ln_output -> Q, K, V (smoothquant.cpp:110-138).  Wq|Wk|Wv
+      // are one [3d, d] matrix, so its column max is the max over the three.
+      TRY(col_absmax_host(m, L.fqkv, 3 * d, d, d_cmax, &pw));
+      TRY(upload_s(scales(stats[li * 4 + 0], pw)));
+      ESMCU_CUDA(launch_div_vec2(L.ln1_w, L.ln1_b, d, d_s, s));
+      ESMCU_CUDA(launch_mul_cols(L.fqkv, 3L * d, d, d_s, s));
+      // Site 2: attn_out -> out_proj; V's rows and bias divided
+      // (smoothquant.cpp:140-166).
+      TRY(col_absmax_host(m, L.fo, d, d, d_cmax, &pw));
+      TRY(upload_s(scales(stats[li * 4 + 1], pw)));
+      ESMCU_CUDA(launch_div_rows(L.fqkv + 2L * d * d, d, d, L.bqkv + 2L * d, d_s, s));
+      ESMCU_CUDA(launch_mul_cols(L.fo, d, d, d_s, s));
+      // Site 3: ffn_ln_output -> fc1 (smoothquant.cpp:168-180).  fc2 is not
+      // migrated.
+      TRY(col_absmax_host(m, L.f1, ffn, d, d_cmax, &pw));
+      TRY(upload_s(scales(stats[li * 4 + 2], pw)));
+      ESMCU_CUDA(launch_div_vec2(L.ln2_w, L.ln2_b, d, d_s, s));
+      ESMCU_CUDA(launch_mul_cols(L.f1, ffn, d, d_s, s));
+      ESMCU_CUDA(cudaStreamSynchronize(s));
+      return ESMCU_OK;
+    };
+    rc = step();
+  }
+  cudaFree(tmp);
+  return rc;
+}
+
+int esmcu_model_quantize_weights(esmcu_model* m, int quantize_lm_head) {
+  if (m == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "null model");
+  TRY(use_device(m->ctx));
+  if (!model_ready(m)) return fail(ESMCU_ERR_INVALID_ARGUMENT, "model weights are not fully set");
+  if (m->cfg.weights_quantized) return ESMCU_OK;  // model.cpp:1471
+  const int d = m->cfg.hidden_size, ffn = m->cfg.intermediate_size;
+  for (auto& L : m->layers) {
+    TRY(quantize_device(m, L.fqkv, 3 * d, d, m->ldk_d, &L.wqkv, &L.sqkv));
+    TRY(quantize_device(m, L.fo, d, d, m->ldk_d, &L.wo, &L.so));
+    TRY(quantize_device(m, L.f1, ffn, d, m->ldk_d, &L.w1, &L.s1));
+    TRY(quantize_device(m, L.f2, d, ffn, m->ldk_ffn, &L.w2, &L.s2));
+  }
+  if (quantize_lm_head) TRY(quantize_device(m, m->lm_w, d, d, m->ldk_d, &m->lm_wq, &m->lm_ws));
+  ESMCU_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  for (auto& L : m->layers) {  // the FP32 copies are no longer read
+    release(m, L.fqkv);
+    release(m, L.fo);
+    release(m, L.f1);
+    release(m, L.f2);
+    L.fqkv = L.fo = L.f1 = L.f2 = nullptr;
+  }
+  m->cfg.weights_quantized = 1;
+  return ESMCU_OK;
+}
+
+int esmcu_model_get_layer(esmcu_model* m, int layer, const esmcu_layer_buffers* out) {
+  if (m == nullptr || out == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "null argument");
+  if (layer < 0 || layer >= m->cfg.num_layers)
+    return fail(ESMCU_ERR_OUT_OF_RANGE, "layer index out of range");
+  TRY(use_device(m->ctx));
+  ESMCU_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  const DevLayer& L = m->layers[static_cast<size_t>(layer)];
+  if (!L.set) return fail(ESMCU_ERR_INVALID_ARGUMENT, "layer weights are not set");
+  const size_t d = static_cast<size_t>(m->cfg.hidden_size), f = static_cast<size_t>(m->cfg.intermediate_size);
+  const int di = m->cfg.hidden_size, fi = m->cfg.intermediate_size;
+  TRY(copy_out(out->attn_ln_w, L.ln1_w, d * 4));
+  TRY(copy_out(out->attn_ln_b, L.ln1_b, d * 4));
+  TRY(copy_out(out->ffn_ln_w, L.ln2_w, d * 4));
+  TRY(copy_out(out->ffn_ln_b, L.ln2_b, d * 4));
+  TRY(copy_out(out->q_b, L.bqkv, d * 4));
+  TRY(copy_out(out->k_b, L.bqkv ? L.bqkv + d : nullptr, d * 4));
+  TRY(copy_out(out->v_b, L.bqkv ? L.bqkv + 2 * d : nullptr, d * 4));
+  TRY(copy_out(out->out_b, L.bo, d * 4));
+  TRY(copy_out(out->fc1_b, L.b1, f * 4));
+  TRY(copy_out(out->fc2_b, L.b2, d * 4));
+  TRY(copy_out(out->q_w, L.fqkv, d * d * 4));
+  TRY(copy_out(out->k_w, L.fqkv ? L.fqkv + d * d : nullptr, d * d * 4));
+  TRY(copy_out(out->v_w, L.fqkv ? L.fqkv + 2 * d * d : nullptr, d * d * 4));
+  TRY(copy_out(out->out_w, L.fo, d * d * 4));
+  TRY(copy_out(out->fc1_w, L.f1, f * d * 4));
+  TRY(copy_out(out->fc2_w, L.f2, d * f * 4));
+  TRY(copy_out_i8(out->q_wq, L.wqkv, 0, di, di, m->ldk_d));
+  TRY(copy_out_i8(out->k_wq, L.wqkv, di, di, di, m->ldk_d));
+  TRY(copy_out_i8(out->v_wq, L.wqkv, 2L * di, di, di, m->ldk_d));
+  TRY(copy_out_i8(out->out_wq, L.wo, 0, di, di, m->ldk_d));
+  TRY(copy_out_i8(out->fc1_wq, L.w1, 0, fi, di, m->ldk_d));
+  TRY(copy_out_i8(out->fc2_wq, L.w2, 0, di, fi, m->ldk_ffn));
+  TRY(copy_out(out->q_ws, L.sqkv, d * 4));
+  TRY(copy_out(out->k_ws, L.sqkv ? L.sqkv + d : nullptr, d * 4));
+  TRY(copy_out(out->v_ws, L.sqkv ? L.sqkv + 2 * d : nullptr, d * 4));
+  TRY(copy_out(out->out_ws, L.so, d * 4));
+  TRY(copy_out(out->fc1_ws, L.s1, f * 4));
+  TRY(copy_out(out->fc2_ws, L.s2, d * 4));
+  return ESMCU_OK;
+}
+
+int esmcu_model_get_head_int8(esmcu_model* m, int8_t* lm_dense_wq, float* lm_dense_ws) {
+  if (m == nullptr) return fail(ESMCU_ERR_INVALID_ARGUMENT, "null model");
+  TRY(use_device(m->ctx));
+  if (m->lm_wq == nullptr) return fail(ESMCU_ERR_NOT_FOUND, "the LM head is FP32");
+  const int d = m->cfg.hidden_size;
+  TRY(copy_out_i8(lm_dense_wq, m->lm_wq, 0, d, d, m->ldk_d));
+  TRY(copy_out(lm_dense_ws, m->lm_ws, static_cast<size_t>(d) * 4));
+  return ESMCU_OK;
+}
+
 int esmcu_model_forward_packed(esmcu_model* m, const int32_t* ids, const int32_t* masks, int T,
                                const int32_t* cu, int B, float* logits) {
   return forward_packed_host(m, ids, masks, T, cu, B, logits, nullptr);

@@ -115,10 +115,10 @@ cudaError_t launch_quantize_per_tensor(const float* x, long ldx, int M, int K,
 cudaError_t launch_quantize_per_token(const float* x, long ldx, int M, int K, int8_t* q,
                                       long ldq, float* row_scales, cudaStream_t s);
 cudaError_t launch_absmax(const float* x, long n, uint32_t* amax_bits, cudaStream_t s);
-// quant::Quantize of weights W [N, K] (dense rows) -> q [N, K] int8 and
-// per-row scales [N].
-cudaError_t launch_quantize_weights(const float* W, int N, int K, int8_t* q, float* scale,
-                                    cudaStream_t s);
+// quant::Quantize of weights W [N, K] (dense rows) -> q [N, K] int8 in rows
+// of stride ldq >= K bytes (bytes past K untouched) and per-row scales [N].
+cudaError_t launch_quantize_weights(const float* W, int N, int K, int8_t* q, long ldq,
+                                    float* scale, cudaStream_t s);
 // x = float(half(x)) in place (round to nearest even); optional absmax of the
 // rounded values into amax_bits.
 cudaError_t launch_round_fp16(float* x, long n, uint32_t* amax_bits, cudaStream_t s);
@@ -194,5 +194,17 @@ cudaError_t launch_gelu_avx(const float* x, float* y, long n, uint32_t* amax, cu
 cudaError_t launch_attention_avx(const float* q, const float* k, const float* v, const int* cu,
                                  int B, int H, int dh, int T, int max_len, float* out,
                                  uint32_t* amax, cudaStream_t s);
+
+// ---------------------------------------------- on-device weight preparation
+// (prep.cu) The SmoothQuant migration's element steps on FP32 weights.
+// out[k] = max_n |W[n, k]| as float bits (out is zeroed first).
+cudaError_t launch_col_absmax(const float* W, int N, int K, uint32_t* out, cudaStream_t s);
+// W[n, k] *= scales[k].
+cudaError_t launch_mul_cols(float* W, long N, int K, const float* scales, cudaStream_t s);
+// W[n, k] /= scales[n] and bias[n] /= scales[n] (bias nullable).
+cudaError_t launch_div_rows(float* W, long N, int K, float* bias, const float* scales,
+                            cudaStream_t s);
+// x[i] /= scales[i], y[i] /= scales[i].
+cudaError_t launch_div_vec2(float* x, float* y, int n, const float* scales, cudaStream_t s);
 
 }  // namespace esmb200

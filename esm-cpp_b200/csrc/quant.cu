@@ -117,12 +117,13 @@ __global__ void round_fp16_kernel(float* __restrict__ x, long n, uint32_t* amax_
 // per row; the max is order-free, so the codes and scales are bit-identical
 // to the reference's.
 __global__ void quantize_weight_rows_kernel(const float* __restrict__ W, int N, int K,
-                                            int8_t* __restrict__ q, float* __restrict__ scale) {
+                                            int8_t* __restrict__ q, long ldq,
+                                            float* __restrict__ scale) {
   const int warps = static_cast<int>(blockDim.x >> 5), lane = static_cast<int>(threadIdx.x & 31);
   for (long n = static_cast<long>(blockIdx.x) * warps + (threadIdx.x >> 5); n < N;
        n += static_cast<long>(gridDim.x) * warps) {
     const float* row = W + n * K;
-    int8_t* qr = q + n * K;
+    int8_t* qr = q + n * ldq;
     float mx = 0.0f;
     for (int k = lane; k < K; k += 32) mx = fmaxf(mx, fabsf(row[k]));
     mx = warp_max(mx);
@@ -170,11 +171,12 @@ cudaError_t launch_quantize_per_token(const float* x, long ldx, int M, int K, in
   return cudaGetLastError();
 }
 
-cudaError_t launch_quantize_weights(const float* W, int N, int K, int8_t* q, float* scale,
-                                    cudaStream_t s) {
+cudaError_t launch_quantize_weights(const float* W, int N, int K, int8_t* q, long ldq,
+                                    float* scale, cudaStream_t s) {
   if (N <= 0 || K <= 0) return cudaSuccess;
+  if (ldq < K) return cudaErrorInvalidValue;
   quantize_weight_rows_kernel<<<grid_for(static_cast<long>(N) * 32, 256), 256, 0, s>>>(W, N, K, q,
-                                                                                     scale);
+                                                                                     ldq, scale);
   return cudaGetLastError();
 }
 

@@ -54,6 +54,10 @@ class LayerWeights(C.Structure):
     ]
 
 
+class LayerBuffers(LayerWeights):
+    """esmcu_layer_buffers: the same fields, written by esmcu_model_get_layer."""
+
+
 _lib = None
 
 _VP = C.c_void_p
@@ -115,6 +119,10 @@ _SIGS = {
                                                 C.c_int, _VP]),
     "esmcu_model_observe_packed": (C.c_int, [_VP, _VP, C.c_int, _VP, C.c_int, C.c_float, _VP]),
     "esmcu_model_forward_observed": (C.c_int, [_VP, _VP, _VP, C.c_int, _VP, C.c_int, _VP]),
+    "esmcu_model_apply_smoothquant": (C.c_int, [_VP, _VP, C.c_float]),
+    "esmcu_model_quantize_weights": (C.c_int, [_VP, C.c_int]),
+    "esmcu_model_get_layer": (C.c_int, [_VP, C.c_int, C.POINTER(LayerBuffers)]),
+    "esmcu_model_get_head_int8": (C.c_int, [_VP, _VP, _VP]),
     "esmcu_observer_create": (C.c_int, [C.POINTER(_VP)]),
     "esmcu_observer_destroy": (C.c_int, [_VP]),
     "esmcu_observer_clear": (C.c_int, [_VP]),

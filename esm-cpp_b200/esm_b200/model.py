@@ -272,40 +272,81 @@ class Model:
         """model.cpp:1470-1494: per-layer Linears to per-channel int8, and
         lm_head.dense too when ESM_QUANTIZE_LM_HEAD is set to anything but
         "", "0" or "off" (model.cpp:1487-1492; the LM head's LayerNorm and the
-        tied decoder stay FP32).  on_device=True runs quant::Quantize on this
-        model's GPU (esmcu_quantize_weights) instead of numpy; the codes and
-        scales are the same bits."""
+        tied decoder stay FP32).  on_device=True quantises the FP32 replica
+        already in HBM in place (esmcu_model_quantize_weights) and reads the
+        codes back for the host copy; the codes and scales are the same bits
+        as numpy's (and the reference's)."""
         if self._cfg.weights_quantized:
             return
-        quant = quantize_weight
+        env = os.environ.get("ESM_QUANTIZE_LM_HEAD")
+        lm_head = bool(env) and env not in ("0", "off")
         if on_device:
-            import torch
-
-            from . import ops
-
-            dev = torch.device("cuda", self.device)
-
-            def quant(w):
-                q, s = ops.quantize_weights(torch.from_numpy(np.ascontiguousarray(w, F32)).to(dev))
-                return q.cpu().numpy(), s.cpu().numpy()
+            self._ensure_device()
+            _lib.call("esmcu_model_quantize_weights", self._dev, int(lm_head))
+            self._pull_layers(quantized=True)
+            if lm_head:
+                d = self._cfg.hidden_size
+                wq, ws = np.empty((d, d), np.int8), np.empty(d, F32)
+                _lib.call("esmcu_model_get_head_int8", self._dev, wq.ctypes.data, ws.ctypes.data)
+                self.head["lm_dense_wq"], self.head["lm_dense_ws"] = wq, ws
+                self._cfg.lm_head_dense_quantized = True
+            self._cfg.weights_quantized = True
+            return  # the device replica is already the quantised model
         for lw in self.layers:
             for n in LINEARS:
-                q, s = quant(lw[n + "_w"])
+                q, s = quantize_weight(lw[n + "_w"])
                 lw[n + "_wq"], lw[n + "_ws"] = q, s
-        env = os.environ.get("ESM_QUANTIZE_LM_HEAD")
-        if env and env not in ("0", "off"):
-            self.head["lm_dense_wq"], self.head["lm_dense_ws"] = quant(self.head["lm_dense_w"])
+        if lm_head:
+            self.head["lm_dense_wq"], self.head["lm_dense_ws"] = quantize_weight(self.head["lm_dense_w"])
             self._cfg.lm_head_dense_quantized = True
         self._cfg.weights_quantized = True
         self._dirty = True
 
-    def apply_smoothquant(self, act_stats: dict, alpha: float) -> None:
-        """model.cpp:1462-1468 -> smoothquant.cpp:100-185 (FP32 weights)."""
+    def apply_smoothquant(self, act_stats: dict, alpha: float, on_device: bool = False) -> None:
+        """model.cpp:1462-1468 -> smoothquant.cpp:100-185 (FP32 weights).
+        on_device=True migrates the FP32 replica in HBM
+        (esmcu_model_apply_smoothquant) and reads the migrated weights back;
+        the result is the same bits either way."""
         if self._cfg.weights_quantized:
             raise RuntimeError("apply_smoothquant runs on FP32 weights, before quantize_weights")
+        if on_device:
+            self._ensure_device()
+            n = self._cfg.num_hidden_layers
+            st = np.array([act_stats.get(f"layer{i}.{SITES[j]}", 0.0) for i in range(n) for j in range(4)],
+                          F32)
+            _lib.call("esmcu_model_apply_smoothquant", self._dev, st.ctypes.data, float(alpha))
+            self._pull_layers(quantized=False)
+            return
         for i, lw in enumerate(self.layers):
             migrate_smoothquant(lw, act_stats, i, alpha)
         self._dirty = True
+
+    def _pull_layers(self, quantized: bool) -> None:
+        """Copies the device replica's layers into the host arrays (LN,
+        biases, and FP32 or int8 weights)."""
+        c = self._cfg
+        d, f = c.hidden_size, c.intermediate_size
+        shapes = {"q": (d, d), "k": (d, d), "v": (d, d), "out": (d, d), "fc1": (f, d), "fc2": (d, f)}
+        for i, lw in enumerate(self.layers):
+            buf = _lib.LayerBuffers()
+            keep = {}
+
+            def arr(name, shape, dtype, ptr_t):
+                a = np.empty(shape, dtype)
+                keep[name] = a
+                setattr(buf, name, C.cast(a.ctypes.data, ptr_t))
+
+            for name in ("attn_ln_w", "attn_ln_b", "ffn_ln_w", "ffn_ln_b"):
+                arr(name, (d,), F32, _lib._FP)
+            for n, shp in shapes.items():
+                arr(n + "_b", (shp[0],), F32, _lib._FP)
+                if quantized:
+                    arr(n + "_wq", shp, np.int8, _lib._I8P)
+                    arr(n + "_ws", (shp[0],), F32, _lib._FP)
+                else:
+                    arr(n + "_w", shp, F32, _lib._FP)
+            _lib.call("esmcu_model_get_layer", self._dev, i, C.byref(buf))
+            lw.update(keep)
 
     def calibrate(self, sequences, pctile: float = 99.9) -> dict:
         """quantize.py calibrate (python/esm_cpp/quantize.py:35-47): every

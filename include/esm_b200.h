@@ -215,6 +215,18 @@ typedef struct {
   const float *ffn_ln_w, *ffn_ln_b;
 } esmcu_layer_weights;
 
+/* Caller-owned host buffers to read one layer back into
+ * (esmcu_model_get_layer): the same fields as esmcu_layer_weights; null
+ * fields are skipped. */
+typedef struct {
+  float *attn_ln_w, *attn_ln_b;
+  float *q_w, *k_w, *v_w, *out_w, *fc1_w, *fc2_w;
+  int8_t *q_wq, *k_wq, *v_wq, *out_wq, *fc1_wq, *fc2_wq;
+  float *q_ws, *k_ws, *v_ws, *out_ws, *fc1_ws, *fc2_ws;
+  float *q_b, *k_b, *v_b, *out_b, *fc1_b, *fc2_b;
+  float *ffn_ln_w, *ffn_ln_b;
+} esmcu_layer_buffers;
+
 /* Allocates the per-device replica on ctx's device. */
 int esmcu_model_create(esmcu_context* ctx, const esmcu_config* cfg, esmcu_model** out);
 int esmcu_model_destroy(esmcu_model* m);
@@ -316,6 +328,29 @@ int esmcu_model_forward_observed(esmcu_model* m, esmcu_observer* obs, const int3
 int esmcu_model_observe_packed(esmcu_model* m, const int32_t* ids, int T,
                                const int32_t* cu_seqlens, int batch_size, float pctile,
                                float* stats_out);
+
+/* ---- on-device weight preparation --------------------------------------
+ * Model::ApplySmoothQuant (model.cpp:1462-1468 -> MigrateSmoothQuant,
+ * smoothquant.cpp:100-185) on the model's FP32 weights in HBM, with
+ * stats[num_layers * 4] as esmcu_model_observe_packed returns them (the
+ * inter_gelu entries are unused: fc2 is not migrated).  The per-channel
+ * column maxima, the LayerNorm / V / weight rescales run on the device; the
+ * scales s = clamp(P_X^a / P_W^(1-a), 1e-3, 1e3) are formed on the host with
+ * the reference's float arithmetic; the migrated weights are the
+ * reference's bit for bit. */
+int esmcu_model_apply_smoothquant(esmcu_model* m, const float* stats, float alpha);
+/* Model::QuantizeWeights (model.cpp:1470-1494) on the device: every encoder
+ * Linear (and lm_head.dense when quantize_lm_head, the ESM_QUANTIZE_LM_HEAD
+ * case) becomes per-output-channel int8 by quant::Quantize (pack.cpp:149-177)
+ * in place; the FP32 copies are freed.  No-op on a quantised model. */
+int esmcu_model_quantize_weights(esmcu_model* m, int quantize_lm_head);
+/* Reads layer `layer` back into the host buffers of `out` (FP32 weights of
+ * an unquantised model, int8 rows [out, in] and scales of a quantised one;
+ * LN and biases always).  ESMCU_ERR_INVALID_ARGUMENT for a requested tensor
+ * the model does not hold. */
+int esmcu_model_get_layer(esmcu_model* m, int layer, const esmcu_layer_buffers* out);
+/* The INT8 lm_head.dense (ESMCU_ERR_NOT_FOUND when the head is FP32). */
+int esmcu_model_get_head_int8(esmcu_model* m, int8_t* lm_dense_wq, float* lm_dense_ws);
 /* Section times (ms, CUDA events on the model's stream, names as the
  * reference's ESM_PROFILE sections) when profiling is on (ESM_PROFILE=1 or
  * esmcu_model_set_profiling).  esmcu_model_profile sums every forward since
