@@ -103,12 +103,13 @@ def pack(seqs):
 def quantized_model(arch="esm2_650m", seed: int = 0, device: int = 0, calib_seqs: int = 32,
                     alpha: float = 0.5, num_layers: int | None = None) -> Model:
     """Config 3 / 4 weights: random init -> seeded calibration on the GPU
-    (percentile 99.9) -> SmoothQuant(alpha) -> per-channel int8."""
+    (percentile 99.9) -> SmoothQuant(alpha) -> per-channel int8, the last
+    two on the replica in HBM (the same bits as the host path)."""
     m = random_model(arch, seed=seed, device=device, num_layers=num_layers)
     calib = residue_ids(varlen_lengths(calib_seqs, seed + 1), seed + 2)
     stats = m.calibrate(calib, 99.9)
-    m.apply_smoothquant(stats, alpha)
-    m.quantize_weights()
+    m.apply_smoothquant(stats, alpha, on_device=True)
+    m.quantize_weights(on_device=True)
     return m
 
 
