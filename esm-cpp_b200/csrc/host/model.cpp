@@ -84,6 +84,14 @@ struct esmcu_model {
   // here and sent with one async H2D each; logits come back the same way.
   char* pinned = nullptr;
   size_t pinned_bytes = 0;
+  // Pinned ring for the cu_seqlens of esmcu_model_forward_packed_device, so
+  // consecutive device-resident forwards enqueue without a host wait: each
+  // call copies its cu into the next free stretch and sends it with an async
+  // H2D.  When the ring wraps, an event recorded behind the lap's copies is
+  // waited on before the stretches are written again (one wait per lap).
+  char* cu_ring = nullptr;
+  size_t cu_ring_off = 0;
+  cudaEvent_t cu_ring_lap = nullptr;
   // profiling
   bool profiling = false;
   using EventPair = std::pair<std::string, std::pair<cudaEvent_t, cudaEvent_t>>;
@@ -917,6 +925,8 @@ int esmcu_model_destroy(esmcu_model* m) {
   for (void* p : m->owned) cudaFree(p);
   if (m->arena) cudaFree(m->arena);
   if (m->pinned) cudaFreeHost(m->pinned);
+  if (m->cu_ring) cudaFreeHost(m->cu_ring);
+  if (m->cu_ring_lap) cudaEventDestroy(m->cu_ring_lap);
   for (auto& e : m->pending) {
     cudaEventDestroy(e.second.first);
     cudaEventDestroy(e.second.second);
@@ -1283,8 +1293,26 @@ int esmcu_model_forward_packed_device(esmcu_model* m, const int32_t* d_ids,
   if (d_ids == nullptr || d_logits == nullptr)
     return fail(ESMCU_ERR_INVALID_ARGUMENT, "ids/logits is null");
   m->launches = 0;
-  ESMCU_CUDA(cudaMemcpyAsync(m->arena + a.cu, cu, static_cast<size_t>(B + 1) * 4,
-                             cudaMemcpyHostToDevice, m->ctx->stream));
+  cudaStream_t s = m->ctx->stream;
+  constexpr size_t kRing = 1u << 20;
+  const size_t n_cu = static_cast<size_t>(B + 1) * 4;
+  if (n_cu > kRing) {  // a batch beyond the ring: plain (synchronising) copy
+    ESMCU_CUDA(cudaMemcpyAsync(m->arena + a.cu, cu, n_cu, cudaMemcpyHostToDevice, s));
+  } else {
+    if (m->cu_ring == nullptr) {
+      ESMCU_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&m->cu_ring), kRing, cudaHostAllocDefault));
+      ESMCU_CUDA(cudaEventCreateWithFlags(&m->cu_ring_lap, cudaEventDisableTiming));
+    }
+    if (m->cu_ring_off + n_cu > kRing) {  // wrap: the lap's copies must have run
+      ESMCU_CUDA(cudaEventRecord(m->cu_ring_lap, s));
+      ESMCU_CUDA(cudaEventSynchronize(m->cu_ring_lap));
+      m->cu_ring_off = 0;
+    }
+    char* src = m->cu_ring + m->cu_ring_off;
+    m->cu_ring_off = align_up(m->cu_ring_off + n_cu, 256);
+    std::memcpy(src, cu, n_cu);
+    ESMCU_CUDA(cudaMemcpyAsync(m->arena + a.cu, src, n_cu, cudaMemcpyHostToDevice, s));
+  }
   return forward_device(m, a, d_ids, d_masks, d_logits, T, B, max_len, nullptr);
 }
 

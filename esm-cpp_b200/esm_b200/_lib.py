@@ -54,6 +54,18 @@ class LayerWeights(C.Structure):
     ]
 
 
+def torch_stream_handle(device: int) -> C.c_void_p:
+    """The cudaStream_t of torch's current stream on `device` for
+    esmcu_set_stream.  torch's default stream is the legacy default stream,
+    whose handle is 0 -- which esmcu_set_stream reads as "the context's own
+    stream" -- so it is passed as cudaStreamLegacy (0x1), the explicit handle
+    of that same stream."""
+    import torch
+
+    h = torch.cuda.current_stream(device).cuda_stream
+    return C.c_void_p(h if h else 1)
+
+
 class LayerBuffers(LayerWeights):
     """esmcu_layer_buffers: the same fields, written by esmcu_model_get_layer."""
 

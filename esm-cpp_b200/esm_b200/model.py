@@ -501,8 +501,7 @@ class Model:
             raise ValueError("d_ids must be a contiguous int32 tensor of cu_seqlens[-1] elements")
         if d_logits.dtype != torch.float32 or tuple(d_logits.shape) != (T, V) or not d_logits.is_contiguous():
             raise ValueError("d_logits must be a contiguous float32 tensor [T, vocab]")
-        _lib.call("esmcu_set_stream", self._ctx,
-                  C.c_void_p(torch.cuda.current_stream(self.device).cuda_stream))
+        _lib.call("esmcu_set_stream", self._ctx, _lib.torch_stream_handle(self.device))
         _lib.call("esmcu_model_forward_packed_device", self._dev, C.c_void_p(d_ids.data_ptr()),
                   None if d_masks is None else C.c_void_p(d_masks.data_ptr()), T, cu.ctypes.data,
                   cu.shape[0] - 1, C.c_void_p(d_logits.data_ptr()))

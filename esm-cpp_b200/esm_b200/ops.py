@@ -17,15 +17,14 @@ _ctx = {}
 
 
 def context(device: int = 0):
-    """A per-device esmcu_context bound to torch's current stream."""
-    import torch
-
+    """A per-device esmcu_context bound to torch's current stream (so the ops
+    are stream-ordered with the torch work around them)."""
     if device not in _ctx:
         h = C.c_void_p()
         _lib.call("esmcu_open", device, C.byref(h))
         _ctx[device] = h
     h = _ctx[device]
-    _lib.call("esmcu_set_stream", h, C.c_void_p(torch.cuda.current_stream(device).cuda_stream))
+    _lib.call("esmcu_set_stream", h, _lib.torch_stream_handle(device))
     return h
 
 
