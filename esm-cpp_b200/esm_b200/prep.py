@@ -33,15 +33,43 @@ def quantize_weight(w: np.ndarray):
     return q, scale
 
 
+_powf = None
+
+
+def _c_powf():
+    """The C library's powf, the function the reference's std::pow(float,
+    float) calls (numpy's power rounds differently in the last ulp)."""
+    global _powf
+    if _powf is None:
+        import ctypes
+        import ctypes.util
+
+        libm = ctypes.CDLL(ctypes.util.find_library("m") or "libm.so.6")
+        libm.powf.restype = ctypes.c_float
+        libm.powf.argtypes = [ctypes.c_float, ctypes.c_float]
+        _powf = libm.powf
+    return _powf
+
+
 def smoothquant_scales(p_x: np.ndarray, p_w: np.ndarray, alpha: float) -> np.ndarray:
-    p_x = np.asarray(p_x, F32)
-    p_w = np.asarray(p_w, F32)
-    s = np.ones_like(p_x)
-    ok = (p_x > 0) & (p_w > 0)
-    with np.errstate(all="ignore"):
-        val = (np.power(p_x, F32(alpha)) / np.power(p_w, F32(1.0) - F32(alpha))).astype(F32)
-    good = ok & np.isfinite(val) & (val > 0)
-    s[good] = np.clip(val[good], F32(1e-3), F32(1e3))
+    """smoothquant.cpp:49-74 channel by channel: s = powf(P_X, a) / powf(P_W,
+    1 - a) in float, 1 where either input is not positive or s is not a
+    positive finite number, clamped to [1e-3, 1e3]."""
+    p_x = np.asarray(p_x, F32).ravel()
+    p_w = np.asarray(p_w, F32).ravel()
+    powf = _c_powf()
+    a = float(F32(alpha))
+    b = float(F32(1.0) - F32(alpha))
+    s = np.ones(p_x.shape, F32)
+    for k in range(p_x.size):
+        px, pw = float(p_x[k]), float(p_w[k])
+        if not (px > 0.0 and pw > 0.0):
+            continue
+        with np.errstate(all="ignore"):
+            val = F32(powf(px, a)) / F32(powf(pw, b))
+        if not np.isfinite(val) or val <= 0:
+            continue
+        s[k] = min(max(val, F32(1e-3)), F32(1e3))
     return s
 
 

@@ -83,7 +83,8 @@ def test_device_smoothquant_and_quantize_match_reference_bits(prep, O, record):
             assert np.array_equal(m.layers[i][ln + "_wq"], rq.layers[i][ln + "_wq"]), (i, ln)
             assert np.array_equal(m.layers[i][ln + "_ws"].view(np.uint32),
                                   rq.layers[i][ln + "_ws"].view(np.uint32)), (i, ln)
-    record("device_smoothquant_quantize", layers=n, bit_exact=True, numpy_host_path_bit_exact=host_same)
+    record("device_smoothquant_quantize", layers=n, bit_exact=True, host_path_bit_exact=host_same)
+    assert host_same  # the host restatement (prep.py) gives the same bits
     # The replica in HBM is the quantised model: a forward runs on it as is.
     seqs = calib[:3]
     ids = np.concatenate(seqs).astype(np.int32)

@@ -142,3 +142,28 @@ def test_isa_queries():
     import esm_b200
 
     assert esm_b200.current_isa() == esm_b200.host_isa() == "sm_100a"
+
+
+def test_host_smoothquant_migration_matches_reference_bits(O, R, tmp_path):
+    """prep.migrate_smoothquant (the host path of Model.apply_smoothquant)
+    against the compiled reference's ApplySmoothQuant on the same FP32
+    weights and statistics: every migrated tensor bit-identical."""
+    from esm_b200 import Model, synth
+
+    arch = dict(num_hidden_layers=2, hidden_size=320, num_attention_heads=20, head_dim=16,
+                intermediate_size=1280)
+    m = synth.random_model(arch, seed=23)
+    m.save_to_safetensors(tmp_path / "w.safetensors")
+    rng = np.random.default_rng(24)
+    sites = ("attn_ln_output", "attn_out", "ffn_ln_output", "inter_gelu")
+    st = (rng.random(8) * 20 + 0.1).astype(np.float32)
+    st[1] = 0.0  # a site with no statistic: s = 1
+    stats = {f"layer{i}.{sites[j]}": float(st[i * 4 + j]) for i in range(2) for j in range(4)}
+    ref = O.RefModel(tmp_path / "w.safetensors")
+    ref.apply_smoothquant(st, 0.5)
+    ref.save_gguf(tmp_path / "m.gguf")
+    want = Model.load_from_gguf(tmp_path / "m.gguf")
+    m.apply_smoothquant(stats, 0.5)
+    for i in range(2):
+        for name, a in m.layers[i].items():
+            assert np.array_equal(a.view(np.uint32), want.layers[i][name].view(np.uint32)), (i, name)
