@@ -242,6 +242,8 @@ __global__ void __maxnreg__(128)
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + kNumBars);
   volatile uint32_t* abort_flag = tslot + 1;
   uint8_t* vpre = smem + kSVpre;
+  pdl_wait();  // cu and the inputs come from earlier work of the stream
+  pdl_trigger();
 
   const int stride = gridDim.x;
   Item first;
@@ -599,6 +601,8 @@ __global__ void __maxnreg__(128)
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + kPNumBars);
   volatile uint32_t* abort_flag = tslot + 1;
   uint8_t* vbuf = smem + kPVbuf;
+  pdl_wait();  // cu and the inputs come from earlier work of the stream
+  pdl_trigger();
 
   const uint32_t rank = cluster_ctarank();
   const int stride = static_cast<int>(gridDim.x >> 1);
@@ -1026,6 +1030,8 @@ __global__ void __maxnreg__(128)
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kLBarOff);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + kLNumBars);
   volatile uint32_t* abort_flag = tslot + 1;
+  pdl_wait();  // cu and the inputs come from earlier work of the stream
+  pdl_trigger();
 
   const int stride = gridDim.x;
   QTile first;
@@ -1438,10 +1444,8 @@ cudaError_t launch_attention_tma(const float* q, const float* k, const float* v,
   const long n_items = static_cast<long>(B) * H;
   if (n_items > (1L << 30)) return cudaErrorInvalidValue;
   const int grid = static_cast<int>(std::min<long>(n_items, std::max(1, num_sms)));
-  attention_tma_kernel<<<grid, kThreads, kSSmemBytes, s>>>(tmQ, tmK, tmV, cu, H,
-                                                          static_cast<int>(n_items), out, amax,
-                                                          status, qk_bf16 ? 1 : 0);
-  return cudaGetLastError();
+  return launch_pdl(attention_tma_kernel, dim3(grid), dim3(kThreads), kSSmemBytes, s, tmQ, tmK, tmV,
+                    cu, H, static_cast<int>(n_items), out, amax, status, qk_bf16 ? 1 : 0);
 }
 
 // Every sequence of 129..256 tokens, one CTA pair per (sequence, head).
@@ -1474,13 +1478,14 @@ cudaError_t launch_attention_tma_pair(const float* q, const float* k, const floa
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = kPSmemBytes;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1] = pdl_attribute();
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, attention_tma_pair_kernel, tmQ, tmK, tmV, cu, H,
                             static_cast<int>(n_items), out, amax, status, qk_bf16 ? 1 : 0);
 }
@@ -1513,9 +1518,9 @@ cudaError_t launch_attention_tma_long(const float* q, const float* k, const floa
   const long n_items = static_cast<long>(B) * H * qtiles;
   if (n_items > (1L << 30)) return cudaErrorInvalidValue;
   const int grid = static_cast<int>(std::min<long>(n_items, std::max(1, num_sms)));
-  attention_tma_long_kernel<<<grid, kThreads, kLSmemBytes, s>>>(
-      tmQ, tmK, tmV, cu, H, qtiles, static_cast<int>(n_items), out, amax, status, qk_bf16 ? 1 : 0);
-  return cudaGetLastError();
+  return launch_pdl(attention_tma_long_kernel, dim3(grid), dim3(kThreads), kLSmemBytes, s, tmQ, tmK,
+                    tmV, cu, H, qtiles, static_cast<int>(n_items), out, amax, status,
+                    qk_bf16 ? 1 : 0);
 }
 
 }  // namespace esmb200

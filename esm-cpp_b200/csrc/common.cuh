@@ -24,6 +24,17 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
+// Programmatic dependent launch.  The forward's kernels are launched with
+// cudaLaunchAttributeProgrammaticStreamSerialization, so a kernel may start
+// (and run its setup: barrier init, TMEM allocation, tensor-map prefetch)
+// while the previous kernel of its stream is still finishing.  pdl_wait()
+// blocks until that kernel has completed and its memory operations are
+// visible -- every kernel calls it before its first global-memory access,
+// reads and writes alike -- and is a no-op for a kernel launched without the
+// attribute.  pdl_trigger() lets the next kernel of the stream launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -48,6 +48,8 @@ __global__ void round_bf16_kernel(const float* x, float* y, long n) {
 // lo = x - tf32(x): the part of an fp32 operand a tf32 MMA drops (it reads
 // the fp32 word with its low 13 mantissa bits cleared).
 __global__ void tf32_lo_kernel(const float* __restrict__ x, float* __restrict__ lo, long n) {
+  pdl_wait();
+  pdl_trigger();
   for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<long>(gridDim.x) * blockDim.x) {
     const float v = x[i];
@@ -130,6 +132,8 @@ __global__ void split_qkv_rope_kernel(const float* __restrict__ qkv, float* __re
 }
 
 __global__ void positions_kernel(const int* __restrict__ cu, int B, int* __restrict__ pos) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x;
   if (b >= B) return;
   const int s0 = cu[b], s1 = cu[b + 1];
@@ -142,6 +146,8 @@ __global__ void positions_kernel(const int* __restrict__ cu, int B, int* __restr
 __global__ void embed_kernel(const float* __restrict__ embed_w, int d, const int* __restrict__ ids,
                              const int* __restrict__ masks, const int* __restrict__ cu, int B,
                              int mask_id, float* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ int s_counts[2];
   const int b = blockIdx.x;
   if (b >= B) return;
@@ -198,6 +204,8 @@ __global__ void embed_kernel(const float* __restrict__ embed_w, int d, const int
 // of each masked copy).  One block per selected row.
 __global__ void gather_rows_kernel(const float* __restrict__ x, const int* __restrict__ rows, int d,
                                    float* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const float* src = x + static_cast<long>(__ldg(rows + blockIdx.x)) * d;
   float* dst = out + static_cast<long>(blockIdx.x) * d;
   for (int i = threadIdx.x; i < d; i += blockDim.x) dst[i] = src[i];
@@ -206,6 +214,8 @@ __global__ void gather_rows_kernel(const float* __restrict__ x, const int* __res
 // In place, each row of x [R, V]: (x - max) - log(sum(exp(x - max))), the
 // order of eval/proteingym.py:48-50.  One warp per row.
 __global__ void log_softmax_rows_kernel(float* __restrict__ x, int R, int V) {
+  pdl_wait();
+  pdl_trigger();
   const long row = (blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= R) return;
@@ -242,8 +252,7 @@ cudaError_t launch_round_bf16(const float* x, float* y, long n, cudaStream_t s) 
 
 cudaError_t launch_tf32_lo(const float* x, float* lo, long n, cudaStream_t s) {
   if (n <= 0) return cudaSuccess;
-  tf32_lo_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, lo, n);
-  return cudaGetLastError();
+  return launch_pdl(tf32_lo_kernel, dim3(grid_for(n, 256)), dim3(256), 0, s, x, lo, n);
 }
 
 cudaError_t launch_scale(float* x, long n, float sc, cudaStream_t s) {
@@ -273,29 +282,27 @@ cudaError_t launch_split_qkv_rope(const float* qkv, float* q, float* k, float* v
 
 cudaError_t launch_positions(const int* cu, int B, int* pos, cudaStream_t s) {
   if (B <= 0) return cudaSuccess;
-  positions_kernel<<<B, 128, 0, s>>>(cu, B, pos);
-  return cudaGetLastError();
+  return launch_pdl(positions_kernel, dim3(B), dim3(128), 0, s, cu, B, pos);
 }
 
 cudaError_t launch_embed(const float* embed_w, int d, const int* ids, const int* masks,
                          const int* cu, int B, int mask_id, float* out, cudaStream_t s) {
   if (B <= 0) return cudaSuccess;
-  embed_kernel<<<dim3(B, 4), 256, 0, s>>>(embed_w, d, ids, masks, cu, B, mask_id, out);
-  return cudaGetLastError();
+  return launch_pdl(embed_kernel, dim3(B, 4), dim3(256), 0, s, embed_w, d, ids, masks, cu, B, mask_id,
+                    out);
 }
 
 cudaError_t launch_gather_rows(const float* x, const int* rows, int R, int d, float* out,
                                cudaStream_t s) {
   if (R <= 0) return cudaSuccess;
-  gather_rows_kernel<<<R, 128, 0, s>>>(x, rows, d, out);
-  return cudaGetLastError();
+  return launch_pdl(gather_rows_kernel, dim3(R), dim3(128), 0, s, x, rows, d, out);
 }
 
 cudaError_t launch_log_softmax_rows(float* x, int R, int V, cudaStream_t s) {
   if (R <= 0) return cudaSuccess;
   const long threads = static_cast<long>(R) * 32;  // one warp per row
-  log_softmax_rows_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, s>>>(x, R, V);
-  return cudaGetLastError();
+  return launch_pdl(log_softmax_rows_kernel, dim3(static_cast<unsigned>((threads + 255) / 256)),
+                    dim3(256), 0, s, x, R, V);
 }
 
 }  // namespace esmb200

@@ -182,6 +182,10 @@ __global__ void __maxnreg__(EW == 16 ? 96 : 168)
   if (PAIR) cluster_sync();  // CTA 0's barriers exist before CTA 1 signals them
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Setup done; from here on the previous kernel's outputs are read (A, the
+  // activation scale) and buffers it may still read are written (C).
+  pdl_wait();
+  pdl_trigger();
 
   // Tiles: m_units row slabs (128 rows, or 256 per pair) x n_blocks.  A pair
   // shares one tile index; CTA `rank` takes rows [128 rank, 128 rank + 128).
@@ -647,9 +651,8 @@ cudaError_t launch_bn(const GemmI8Args& a, cudaStream_t s) {
   if constexpr (!PAIR) {
     const int tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
     const int grid = tiles < a.num_sms ? tiles : a.num_sms;
-    gemm_i8_kernel<BN, EPI, false, EW, false><<<grid, kThreads, C::SMEM, s>>>(
-        tmA, tmB, tmC[0], tmC[1], tmC[2], tmC[1], tmC[2], p);
-    return cudaGetLastError();
+    return launch_pdl(gemm_i8_kernel<BN, EPI, false, EW, false>, dim3(grid), dim3(kThreads),
+                      C::SMEM, s, tmA, tmB, tmC[0], tmC[1], tmC[2], tmC[1], tmC[2], p);
   } else {
   // CTA pairs: one 2-CTA cluster per pair tile, at most num_sms / 2 pairs.
   const int tiles = ((a.M + 2 * BM - 1) / (2 * BM)) * ((a.N + BN - 1) / BN);
@@ -659,13 +662,14 @@ cudaError_t launch_bn(const GemmI8Args& a, cudaStream_t s) {
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1] = pdl_attribute();
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, gemm_i8_kernel<BN, EPI, true, EW, false>, tmA, tmB, tmC[0],
                             tmC[1], tmC[2], tmC[1], tmC[2], p);
   }
@@ -713,9 +717,8 @@ cudaError_t launch_f32(const GemmTf32Args& a, cudaStream_t s) {
   if constexpr (!PAIR) {
     const int tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
     const int grid = tiles < a.num_sms ? tiles : a.num_sms;
-    gemm_i8_kernel<BN, kEpiStore, false, EW, true><<<grid, kThreads, C::SMEM, s>>>(
-        tmA, tmB, tmC[0], tmC[1], tmC[2], tmAlo, tmBlo, p);
-    return cudaGetLastError();
+    return launch_pdl(gemm_i8_kernel<BN, kEpiStore, false, EW, true>, dim3(grid), dim3(kThreads),
+                      C::SMEM, s, tmA, tmB, tmC[0], tmC[1], tmC[2], tmAlo, tmBlo, p);
   } else {
     const int tiles = ((a.M + 2 * BM - 1) / (2 * BM)) * ((a.N + BN - 1) / BN);
     const int pairs = std::max(1, std::min(tiles, a.num_sms / 2));
@@ -724,13 +727,14 @@ cudaError_t launch_f32(const GemmTf32Args& a, cudaStream_t s) {
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = C::SMEM;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1] = pdl_attribute();
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, gemm_i8_kernel<BN, kEpiStore, true, EW, true>, tmA, tmB,
                               tmC[0], tmC[1], tmC[2], tmAlo, tmBlo, p);
   }

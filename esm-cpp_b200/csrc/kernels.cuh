@@ -7,6 +7,31 @@
 
 namespace esmb200 {
 
+// Launch attribute of the forward's kernels: programmatic stream
+// serialisation (the kernel calls pdl_wait() before touching global memory,
+// common.cuh), so its launch and setup overlap the previous kernel's tail.
+inline cudaLaunchAttribute pdl_attribute() {
+  cudaLaunchAttribute a;
+  a.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  a.val.programmaticStreamSerializationAllowed = 1;
+  return a;
+}
+
+// kernel<<<grid, block, smem, s>>>(args...) with the PDL attribute.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1] = {pdl_attribute()};
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // A per-tensor absmax lives in kAmaxSlots uint32 slots (float bits): each
 // producer block folds its maximum into slot (blockIdx.x % kAmaxSlots) and the
 // consumer takes the max over the slots.  Spreading the atomics over 64

@@ -53,6 +53,8 @@ __global__ void __launch_bounds__(kLnThreads)
                      const float* __restrict__ b, float eps, float* __restrict__ out, int rows,
                      int d, uint32_t* amax, int8_t* __restrict__ q, long ldq,
                      float* __restrict__ row_scales) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ double red_d[kLnThreads / 32];
   __shared__ float red_f[kLnThreads / 32];
   float tmax = 0.0f;
@@ -366,14 +368,13 @@ cudaError_t launch_layernorm(const float* x, const float* g, const float* b, flo
   const int grid = rows < 148 * 16 ? rows : 148 * 16;
   if (vec && nv4 <= 8) {
     switch (nv4) {
-      case 1: layernorm_kernel<1><<<grid, kLnThreads, 0, s>>>(x, g, b, eps, out, rows, d, amax, q, ldq, row_scales); break;
-      case 2: layernorm_kernel<2><<<grid, kLnThreads, 0, s>>>(x, g, b, eps, out, rows, d, amax, q, ldq, row_scales); break;
-      case 3: layernorm_kernel<3><<<grid, kLnThreads, 0, s>>>(x, g, b, eps, out, rows, d, amax, q, ldq, row_scales); break;
-      case 4: layernorm_kernel<4><<<grid, kLnThreads, 0, s>>>(x, g, b, eps, out, rows, d, amax, q, ldq, row_scales); break;
-      case 5: layernorm_kernel<5><<<grid, kLnThreads, 0, s>>>(x, g, b, eps, out, rows, d, amax, q, ldq, row_scales); break;
-      default: layernorm_kernel<8><<<grid, kLnThreads, 0, s>>>(x, g, b, eps, out, rows, d, amax, q, ldq, row_scales); break;
+      case 1: return launch_pdl(layernorm_kernel<1>, dim3(grid), dim3(kLnThreads), 0, s, x, g, b, eps, out, rows, d, amax, q, ldq, row_scales);
+      case 2: return launch_pdl(layernorm_kernel<2>, dim3(grid), dim3(kLnThreads), 0, s, x, g, b, eps, out, rows, d, amax, q, ldq, row_scales);
+      case 3: return launch_pdl(layernorm_kernel<3>, dim3(grid), dim3(kLnThreads), 0, s, x, g, b, eps, out, rows, d, amax, q, ldq, row_scales);
+      case 4: return launch_pdl(layernorm_kernel<4>, dim3(grid), dim3(kLnThreads), 0, s, x, g, b, eps, out, rows, d, amax, q, ldq, row_scales);
+      case 5: return launch_pdl(layernorm_kernel<5>, dim3(grid), dim3(kLnThreads), 0, s, x, g, b, eps, out, rows, d, amax, q, ldq, row_scales);
+      default: return launch_pdl(layernorm_kernel<8>, dim3(grid), dim3(kLnThreads), 0, s, x, g, b, eps, out, rows, d, amax, q, ldq, row_scales);
     }
-    return cudaGetLastError();
   }
   if (q != nullptr || out == nullptr) return cudaErrorInvalidValue;
   const long threads = static_cast<long>(rows) * 32;

@@ -35,6 +35,8 @@ __global__ void quantize_per_tensor_kernel(const float* __restrict__ x, long ldx
                                            const uint32_t* __restrict__ amax_bits,
                                            int8_t* __restrict__ q, long ldq,
                                            float* __restrict__ scale_out) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float s_amax;
   if (threadIdx.x < 32) {
     const uint32_t m = max(__ldg(amax_bits + threadIdx.x), __ldg(amax_bits + 32 + threadIdx.x));
@@ -75,6 +77,8 @@ __global__ void quantize_per_tensor_kernel(const float* __restrict__ x, long ldx
 __global__ void quantize_per_token_kernel(const float* __restrict__ x, long ldx, int M, int K,
                                           int8_t* __restrict__ q, long ldq,
                                           float* __restrict__ row_scales) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const long m = (blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x) >> 5;
   if (m >= M) return;
@@ -156,9 +160,8 @@ cudaError_t launch_quantize_per_tensor(const float* x, long ldx, int M, int K,
   if (M <= 0) return cudaSuccess;
   if ((ldq & 15) || ldq < K || (reinterpret_cast<uintptr_t>(q) & 15)) return cudaErrorInvalidValue;
   const long work = static_cast<long>(M) * (ldq / 16);
-  quantize_per_tensor_kernel<<<grid_for(work, 256), 256, 0, s>>>(x, ldx, M, K, amax_bits, q,
-                                                                  ldq, scale_out);
-  return cudaGetLastError();
+  return launch_pdl(quantize_per_tensor_kernel, dim3(grid_for(work, 256)), dim3(256), 0, s, x, ldx,
+                    M, K, amax_bits, q, ldq, scale_out);
 }
 
 cudaError_t launch_quantize_per_token(const float* x, long ldx, int M, int K, int8_t* q,
@@ -166,9 +169,8 @@ cudaError_t launch_quantize_per_token(const float* x, long ldx, int M, int K, in
   if (M <= 0) return cudaSuccess;
   if (ldq < K) return cudaErrorInvalidValue;
   const long threads = static_cast<long>(M) * 32;
-  quantize_per_token_kernel<<<static_cast<int>((threads + 255) / 256), 256, 0, s>>>(
-      x, ldx, M, K, q, ldq, row_scales);
-  return cudaGetLastError();
+  return launch_pdl(quantize_per_token_kernel, dim3(static_cast<unsigned>((threads + 255) / 256)),
+                    dim3(256), 0, s, x, ldx, M, K, q, ldq, row_scales);
 }
 
 cudaError_t launch_quantize_weights(const float* W, int N, int K, int8_t* q, long ldq,

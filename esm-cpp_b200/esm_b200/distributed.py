@@ -141,14 +141,43 @@ def forward_scheduled_sharded(run_group, input_ids, rank: int, world: int, d: in
     return gather_logits(local, sp, rank, world, len(seqs), dst, group)
 
 
+class _Staging:
+    """Per-device pinned host buffer for the rank's packed ids, reused across
+    calls: grown when too small, and rewritten only after the event recorded
+    behind the previous call's host-to-device copies has completed."""
+
+    def __init__(self):
+        self.buf = None
+        self.done = None
+
+    def take(self, n: int, dev):
+        import torch
+
+        if self.done is not None:
+            self.done.synchronize()
+        if self.buf is None or self.buf.numel() < n:
+            self.buf = torch.empty(max(n, 1), dtype=torch.int32, pin_memory=True)
+        return self.buf
+
+    def mark(self, dev):
+        import torch
+
+        self.done = torch.cuda.Event()
+        self.done.record(torch.cuda.current_stream(dev))
+
+
+_staging = {}
+
+
 def forward_scheduled_sharded_device(model, input_ids, rank: int, world: int,
                                      imbalance_threshold: float = 1.2, max_batch_size: int = 256,
                                      dst: int = 0, group=None):
     """forward_scheduled_sharded on this rank's GPU model (esm_b200.Model):
-    the rank's packed ids go to the device (one host-to-device copy per
-    group), each group runs on the device into one packed logits buffer,
-    and the buffer is gathered to rank `dst` over NCCL.  Returns the logits
-    per sequence in input order on rank `dst`, None elsewhere."""
+    the rank's packed ids go to the device through a pinned staging buffer
+    (one asynchronous host-to-device copy per group), each group runs on the
+    device into one packed logits buffer, and the buffer is gathered to rank
+    `dst` over NCCL.  Returns the logits per sequence in input order on rank
+    `dst`, None elsewhere."""
     import torch
 
     seqs = [np.ascontiguousarray(s, np.int32) for s in input_ids]
@@ -157,12 +186,19 @@ def forward_scheduled_sharded_device(model, input_ids, rank: int, world: int,
     dev = torch.device("cuda", model.device)
     V = model.config.vocab_size
     local = torch.zeros((max(sp.max_tokens, 1), V), dtype=torch.float32, device=dev)
+    st = _staging.setdefault(model.device, _Staging())
+    host = st.take(sp.tokens[rank], dev)
+    d_ids_all = torch.empty(max(sp.tokens[rank], 1), dtype=torch.int32, device=dev)
     off = 0
     for gi in sp.assign[rank]:
         ids, cu = pack_group(seqs, sp.plan, gi, sp.lens)
-        d_ids = torch.from_numpy(ids).pin_memory().to(dev, non_blocking=True)
-        model.forward_packed_device(d_ids, cu, local[off:off + ids.shape[0]])
-        off += ids.shape[0]
+        n = ids.shape[0]
+        host[off:off + n].numpy()[:] = ids
+        d_ids = d_ids_all[off:off + n]
+        d_ids.copy_(host[off:off + n], non_blocking=True)
+        model.forward_packed_device(d_ids, cu, local[off:off + n])
+        off += n
+    st.mark(dev)
     if sp.max_tokens == 0:
         return [np.zeros((0, V), np.float32) for _ in seqs] if rank == dst else None
     return gather_logits(local, sp, rank, world, len(seqs), dst, group)
