@@ -126,3 +126,26 @@ def test_lpt_assignment_balances_and_covers():
         loads = [sum(group_cost([lens[i] for i in plan[g]], 1280) for g in r) for r in a]
         biggest = max(group_cost([lens[i] for i in g], 1280) for g in plan)
         assert max(loads) - min(loads) <= biggest
+
+
+def test_dms_sharding_gives_every_gpu_equal_groups():
+    """Config 4: 7,601 sequences of 402 tokens, groups of at most 256; the
+    bench's max_batch rule makes the group count a multiple of the GPU count,
+    so LPT gives every GPU the same number of groups and tokens within one
+    group's worth."""
+    import importlib.util
+
+    from esm_b200.distributed import plan_shards
+
+    spec = importlib.util.spec_from_file_location("bench_mod", ROOT / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    lens = [402] * 7601
+    for world in (1, 2, 4, 8):
+        mb = bench._dms_max_batch(len(lens), world)
+        assert mb <= 256
+        sp = plan_shards(lens, world, 2560, 1.2, mb)
+        counts = [len(a) for a in sp.assign]
+        assert len(sp.plan) % world == 0 and len(set(counts)) == 1, (world, counts)
+        assert max(sp.tokens) - min(sp.tokens) <= mb * 402
+        assert sp.imbalance < 1.01
