@@ -335,50 +335,82 @@ __global__ void __maxnreg__(EW == 16 ? 96 : 168)
     int acc = 0;
     uint32_t acc_phase = 0;
     float amax = 0.0f;
+    static_assert(BN <= EW * 32, "one vector column per epilogue thread");
+    const bool has_col = p.acc_out == nullptr && etid < BN;
+    // Per-tensor scale: ws[n]*as is the same for every row, so the rounded
+    // product (the reference rounds it before the fma) is formed once per
+    // column; the raw-accumulator mode carries no activation scale.
+    const bool scaled = !F32 && p.acc_out == nullptr;
+    const float as_col = (scaled && !p.per_token) ? __ldg(p.a_scale) : 1.0f;
+    // The per-tile inputs of the epilogue -- this thread's w_scale / bias
+    // column, its row's per-token scale, and (RoPE) its row's position and
+    // cos / sin table entries -- are fetched one tile ahead (the position two
+    // tiles ahead, as the table rows depend on it), so their global-memory
+    // latency overlaps the current tile's work instead of preceding the
+    // accumulator wait.
+    auto fetch_cols = [&](int t, float& ws, float& b, float& as_row) {
+      const long mm = static_cast<long>(tile_m_base(t)) + row_in_tile;
+      as_row = (scaled && p.per_token && mm < p.M) ? __ldg(p.a_scale + mm) : 1.0f;
+      ws = 0.0f;
+      b = 0.0f;
+      if (has_col) {  // tail columns read the last valid column
+        const int n = min((t / m_units) * BN + etid, p.N - 1);
+        if (!F32) ws = __ldg(p.w_scale + n);
+        b = p.bias ? __ldg(p.bias + n) : 0.0f;
+      }
+    };
+    constexpr bool kRope = EPI == kEpiQkvRope;
+    // RoPE: the quadrant's 32 rows' cos (warp sub 0) or sin (sub 1) table
+    // entries 0..31, 8 lanes per 128-byte row (coalesced): lane l holds
+    // entry chunk l & 7 of rows (l >> 3) + 4 i.
+    auto fetch_pos = [&](int t) {
+      const long mm = static_cast<long>(tile_m_base(t)) + row_in_tile;
+      return (kRope && p.tma && t < num_tiles && mm < p.M) ? __ldg(p.epi.pos + mm) : 0;
+    };
+    float4 rope_v[kRope ? 8 : 1];
+    auto fetch_rope = [&](int pos_m) {
+      if constexpr (kRope) {
+        const float* tab = sub == 0 ? p.epi.cos_t : p.epi.sin_t;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int pr = __shfl_sync(0xffffffffu, pos_m, i * 4 + (lane >> 3));
+          rope_v[i] = __ldg(reinterpret_cast<const float4*>(tab + static_cast<long>(pr) * 64) + (lane & 7));
+        }
+      }
+    };
+    float ws_nx = 0.0f, b_nx = 0.0f, as_nx = 1.0f;
+    fetch_cols(first_tile, ws_nx, b_nx, as_nx);
+    int pos_nx = 0;
+    if constexpr (kRope) {
+      if (p.tma) {
+        fetch_rope(fetch_pos(first_tile));
+        pos_nx = fetch_pos(first_tile + tile_stride);
+      }
+    }
     for (int tile = first_tile; tile < num_tiles; tile += tile_stride) {
       const int m_base = tile_m_base(tile);
       const int n_blk = tile / m_units;
-      // RoPE: the quadrant's 32 rows' cos (warp sub 0) or sin (sub 1) table
-      // entries 0..31 into shared memory while the accumulator is still being
-      // computed, 8 lanes per 128-byte row (coalesced); row r's 16-byte chunk
-      // k goes to position k ^ (r & 7) so the per-row reads are conflict-free.
-      // The previous tile's readers are past the tile-end barrier; this
-      // tile's read after the vectors-filled barrier.
-      if constexpr (EPI == kEpiQkvRope) {
+      // This tile's RoPE rows into shared memory (row r's 16-byte chunk k at
+      // position k ^ (r & 7), so the per-row reads are conflict-free); the
+      // previous tile's readers are past the tile-end barrier, this tile's
+      // read after the vectors-filled barrier.  Then the next tile's rows.
+      if constexpr (kRope) {
         static_assert(EW / 4 == 2, "two epilogue warps per TMEM lane quadrant");
         if (p.tma) {
-          const long mm = static_cast<long>(m_base) + row_in_tile;
-          const int pos_m = mm < p.M ? __ldg(p.epi.pos + mm) : 0;
-          const float* tab = sub == 0 ? p.epi.cos_t : p.epi.sin_t;
           uint8_t* qreg = rope_cs + quad * 32 * 256 + sub * 128;
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const int r = i * 4 + (lane >> 3), k = lane & 7;
-            const int pr = __shfl_sync(0xffffffffu, pos_m, r);
-            const float4 v = __ldg(reinterpret_cast<const float4*>(tab + static_cast<long>(pr) * 64) + k);
-            sts128(smem_u32(qreg + r * 256 + ((k ^ (r & 7)) << 4)), v);
+            sts128(smem_u32(qreg + r * 256 + ((k ^ (r & 7)) << 4)), rope_v[i]);
           }
+          fetch_rope(pos_nx);
+          pos_nx = fetch_pos(tile + 2 * tile_stride);
         }
       }
-      // The tile's scales and bias are loaded before the accumulator wait so
-      // their latency overlaps it: the activation scale, and this thread's
-      // column (at most one) of the w_scale / bias vectors.
-      static_assert(BN <= EW * 32, "one vector column per epilogue thread");
       const long m = static_cast<long>(m_base) + row_in_tile;
       const bool row_ok = m < p.M;
-      float as = 1.0f;  // the raw-accumulator mode carries no activation scale
-      if (!F32 && row_ok && p.acc_out == nullptr)
-        as = p.per_token ? __ldg(p.a_scale + m) : __ldg(p.a_scale);
-      // Per-tensor scale: ws[n]*as is the same for every row, so the rounded
-      // product (the reference rounds it before the fma) is formed once.
-      const float as_col = (F32 || p.per_token || p.acc_out) ? 1.0f : __ldg(p.a_scale);
-      const bool has_col = p.acc_out == nullptr && etid < BN;
-      float ws_col = 0.0f, b_col = 0.0f;
-      if (has_col) {  // tail columns read the last valid column
-        const int n = min(n_blk * BN + etid, p.N - 1);
-        if (!F32) ws_col = __ldg(p.w_scale + n);
-        b_col = p.bias ? __ldg(p.bias + n) : 0.0f;
-      }
+      const float as = as_nx, ws_col = ws_nx, b_col = b_nx;
+      if (tile + tile_stride < num_tiles) fetch_cols(tile + tile_stride, ws_nx, b_nx, as_nx);
       if (!epi_all<EW>(mbar_wait(&tfull[acc], acc_phase, p.status))) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
