@@ -86,6 +86,7 @@ struct Params {
   uint32_t* status;
   int32_t* acc_out;
   int tma;  // epilogue stores through TMA (tensor maps tmC0..2 valid)
+  int band;  // row slabs per tile band (0: all of them, row-slab-fastest order)
 };
 
 // Named barrier 1 across the EW epilogue warps only.
@@ -189,6 +190,11 @@ __global__ void __maxnreg__(EW == 16 ? 96 : 168)
 
   // Tiles: m_units row slabs (128 rows, or 256 per pair) x n_blocks.  A pair
   // shares one tile index; CTA `rank` takes rows [128 rank, 128 rank + 128).
+  // Tile order: bands of `band` row slabs, each band's tiles (row slab
+  // fastest) before the next band's, so the tiles in flight share one band
+  // of A -- which stays in L2 across the column blocks -- where A is too
+  // large to stay in L2 whole; band = m_units is row-slab-fastest over all
+  // of A.
   const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
   const int first_tile = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
   const int tile_stride = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
@@ -197,8 +203,19 @@ __global__ void __maxnreg__(EW == 16 ? 96 : 168)
   const int num_tiles = m_units * n_blocks;
   const int kpb = F32 ? BK / 4 : BK;  // K elements per stage
   const int num_kb = (p.K + kpb - 1) / kpb;
+  const int band = p.band > 0 && p.band < m_units ? p.band : m_units;
+  auto tile_mu = [&](int tile) {
+    const int b0 = (tile / (band * n_blocks)) * band;
+    const int rows_b = min(band, m_units - b0);
+    return b0 + (tile - b0 * n_blocks) % rows_b;
+  };
+  auto tile_nb = [&](int tile) {
+    const int b0 = (tile / (band * n_blocks)) * band;
+    const int rows_b = min(band, m_units - b0);
+    return (tile - b0 * n_blocks) / rows_b;
+  };
   auto tile_m_base = [&](int tile) {
-    const int mu = tile % m_units;
+    const int mu = tile_mu(tile);
     return PAIR ? mu * 2 * BM + static_cast<int>(rank) * BM : mu * BM;
   };
 
@@ -210,7 +227,7 @@ __global__ void __maxnreg__(EW == 16 ? 96 : 168)
       bool ok = true;
       for (int tile = first_tile; tile < num_tiles && ok; tile += tile_stride) {
         const int m_base = tile_m_base(tile);
-        const int n_blk = tile / m_units;
+        const int n_blk = tile_nb(tile);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.status)) {
             ok = false;
@@ -354,7 +371,7 @@ __global__ void __maxnreg__(EW == 16 ? 96 : 168)
       ws = 0.0f;
       b = 0.0f;
       if (has_col) {  // tail columns read the last valid column
-        const int n = min((t / m_units) * BN + etid, p.N - 1);
+        const int n = min(tile_nb(t) * BN + etid, p.N - 1);
         if (!F32) ws = __ldg(p.w_scale + n);
         b = p.bias ? __ldg(p.bias + n) : 0.0f;
       }
@@ -389,7 +406,7 @@ __global__ void __maxnreg__(EW == 16 ? 96 : 168)
     }
     for (int tile = first_tile; tile < num_tiles; tile += tile_stride) {
       const int m_base = tile_m_base(tile);
-      const int n_blk = tile / m_units;
+      const int n_blk = tile_nb(tile);
       // This tile's RoPE rows into shared memory (row r's 16-byte chunk k at
       // position k ^ (r & 7), so the per-row reads are conflict-free); the
       // previous tile's readers are past the tile-end barrier, this tile's
@@ -680,6 +697,14 @@ cudaError_t launch_bn(const GemmI8Args& a, cudaStream_t s) {
   p.status = a.status;
   p.acc_out = a.acc_out;
   p.tma = tma ? 1 : 0;
+  // Where A is too large to stay in L2 across the column blocks (long K),
+  // bands of row slabs just wide enough for the tiles in flight.
+  p.band = 0;
+  if (static_cast<long>(a.M) * a.K > (32l << 20)) {
+    const int nb = (a.N + BN - 1) / BN;
+    const int in_flight = PAIR ? a.num_sms / 2 : a.num_sms;
+    p.band = std::max(1, (in_flight + nb - 1) / nb);
+  }
   if constexpr (!PAIR) {
     const int tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
     const int grid = tiles < a.num_sms ? tiles : a.num_sms;
@@ -746,6 +771,7 @@ cudaError_t launch_f32(const GemmTf32Args& a, cudaStream_t s) {
   p.status = a.status;
   p.acc_out = nullptr;
   p.tma = tma ? 1 : 0;
+  p.band = 0;
   if constexpr (!PAIR) {
     const int tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
     const int grid = tiles < a.num_sms ? tiles : a.num_sms;
