@@ -222,6 +222,10 @@ __global__ void __launch_bounds__(kLqThreads, NV <= 16 ? 2 : 1)
     s_gb[i] = __ldg(g + i);
     s_gb[128 * NV + i] = __ldg(b + i);
   }
+  // x, the absmax slots and the barrier counter come from earlier work of
+  // the stream (the weights above do not).
+  pdl_wait();
+  pdl_trigger();
   __syncthreads();
   const uint32_t sg = smem_u32(s_gb), sb = sg + 128u * NV * 4u;
   auto load_row = [&](long r, float4 (&v)[NV]) {
@@ -324,9 +328,22 @@ cudaError_t launch_lq(const float* x, const float* g, const float* b, float eps,
   }
   const long want = (static_cast<long>(rows) + kLqThreads / 32 - 1) / (kLqThreads / 32);
   const int grid = static_cast<int>(std::max(1L, std::min<long>(want, static_cast<long>(per_sm) * sms)));
-  void* args[] = {&x, &g, &b, &eps, &rows, &d, &amax, &stats, &counter, &q, &ldq, &scale_out, &status};
-  return cudaLaunchCooperativeKernel(reinterpret_cast<void*>(ln_quant_kernel<NV>), dim3(grid),
-                                     dim3(kLqThreads), args, 0, s);
+  // Cooperative (for the grid barrier) and with programmatic dependent
+  // launch, so the launch and the gamma / beta loads overlap the previous
+  // kernel's tail.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kLqThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  attr[1] = pdl_attribute();
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, ln_quant_kernel<NV>, x, g, b, eps, rows, d, amax, stats, counter, q,
+                            ldq, scale_out, status);
 }
 
 }  // namespace
