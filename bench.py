@@ -179,7 +179,7 @@ def build_model(device: int, seed: int = 0, arch: str = "esm2_650m"):
 # kernel_cases.py on this build (first config-3a group, 13,305 tokens; QKV
 # 174.1 MB, out-proj 97.5 MB, fc1 245.2 MB, fc2 251.8 MB).  Traffic grows with
 # the tokens of a launch (activations and outputs; the weights are ~3% of it).
-GEMM_DRAM_BYTES_PER_TOKEN_LAYER = 768.59e6 / 13305
+GEMM_DRAM_BYTES_PER_TOKEN_LAYER = 680.93e6 / 13305
 GEMM_TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of the layer case "
                        "(profiles/gemm_i8_esm2_650m_group0.md), per token, scaled by this "
                        "rank's tokens per GEMM launch")
