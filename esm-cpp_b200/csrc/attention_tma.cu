@@ -935,11 +935,21 @@ __global__ void __maxnreg__(128)
 // tile), one CTA each on a persistent grid, keys in blocks of 128.  The
 // softmax keeps the exact form -- the row max over all keys first, then
 // exponentials, sum and P.V -- in two passes over the key blocks:
-//   pass 1  S_j = Q K_j^T (3xTF32) for the row max m;
-//   pass 2  the same S_j again (the same MMAs, so the same values), P =
-//           2^((S - m) log2 e) chunk by chunk into TMEM as in the short
-//           kernel, O += P V_j (3xTF32), row sums summed over the blocks.
-// O is never rescaled; the price is S computed twice.
+//   pass 1  S'_j = Q K_j^T with one tf32 MMA per 8 dh (the raw words, no lo
+//           terms) for a row max m' raised by the bound of its error;
+//   pass 2  S_j in 3xTF32, P = 2^((S - m') log2 e) chunk by chunk into TMEM
+//           as in the short kernel, O += P V_j (3xTF32), row sums summed
+//           over the blocks.
+// O is never rescaled.  m' is an upper bound of the exact row max m, at
+// most 2 B above it: tf32 truncation leaves each of q_i, k_i within 2^-10
+// relative, so |S - S'| <= 2^-9 ||q|| ||k|| (plus the fp32 accumulation,
+// taken care of by a factor 2), ||k|| <= 8 max|k| at dh = 64, hence
+// B = 2^-5 ||q|| max|k| with max|k| over the sequence's keys, capped at 16
+// so that P stays a normal float.  exp(S - m') / sum exp(S - m') equals exp(S - m) / sum
+// exp(S - m); the shift changes results at the rounding level only.  Q and
+// K holding bf16 values (qk_bf16) are exact in tf32: there S' = S, B = 0.
+// Pass 1 needs no lo parts, so the prep warps only scan its K tiles for
+// max|k|.
 // Two S buffers: S_{j+1} runs on the tensor cores while the softmax warps
 // read or convert S_j.  Pass 2 issues S_0, S_1, P.V_0, S_2, P.V_1, ...; P_lo
 // has two 32-column slots, chunk c reusing slot c & 1 once the P.V that read
@@ -968,7 +978,8 @@ enum : int {
   kLODone = 16,   // the item's P.V done
   kLLoFree = 17,  // [2] the P.V that read P_lo slot s is done
   kLChunk = 19,   // [4] P chunk c written (4 softmax warps)
-  kLNumBars = 23
+  kLBound = 23,   // the item's pass-1 max|k| published (4 prep warps)
+  kLNumBars = 24
 };
 // Ring stage and phase parity of tile t.
 __device__ __forceinline__ int ring_stage(uint32_t t) { return static_cast<int>(t % kLNst); }
@@ -1030,6 +1041,9 @@ __global__ void __maxnreg__(128)
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kLBarOff);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + kLNumBars);
   volatile uint32_t* abort_flag = tslot + 1;
+  // max|k| of the item's pass-1 K tiles, one slot per prep warp, by item
+  // parity (item n + 2's prep starts after item n's softmax has read them).
+  float (*kmax_slot)[4] = reinterpret_cast<float (*)[4]>(tslot + 2);
   pdl_wait();  // cu and the inputs come from earlier work of the stream
   pdl_trigger();
 
@@ -1057,6 +1071,7 @@ __global__ void __maxnreg__(128)
     mbar_init(&bar[kLQFree], 1);
     mbar_init(&bar[kLODone], 1);
     for (int c = 0; c < 4; ++c) mbar_init(&bar[kLChunk + c], 4);
+    mbar_init(&bar[kLBound], 4);
     *abort_flag = 0u;
     fence_barrier_init();
   }
@@ -1124,10 +1139,10 @@ __global__ void __maxnreg__(128)
       const uint32_t idO2 = idesc_tf32_bmn(QB, 2 * DH);
       const uint32_t q_s = smem_u32(smem + kLQ);
 
-      // S = Q_raw K_raw^T + Q_raw K_lo^T + Q_lo K_raw^T for the K tile at
-      // ring index t into the next S buffer (identical in both passes);
+      // S = Q_raw K_raw^T + Q_raw K_lo^T + Q_lo K_raw^T (exact) or Q_raw K_raw^T
+      // (pass 1) for the K tile at ring index t into the next S buffer;
       // returns false on a failed wait.
-      auto issue_s = [&](uint32_t t) -> bool {
+      auto issue_s = [&](uint32_t t, bool exact) -> bool {
         const int s = ring_stage(t);
         if (!mbar_wait_abort(&bar[kLReady + s], ring_parity(t), status, abort_flag)) return false;
         const uint32_t b = ns & 1;
@@ -1141,7 +1156,7 @@ __global__ void __maxnreg__(128)
           const uint32_t o = static_cast<uint32_t>((kk >> 2) * 16384 + (kk & 3) * 32);
           const uint64_t a_raw = sw128_kmajor_desc(q_s + o);
           mma_tf32(tS, a_raw, sw128_kmajor_desc(st + o), idS, kk > 0 ? 1u : 0u);
-          if (!qk_bf16) {  // bf16-valued Q and K are exact in tf32: no lo terms
+          if (exact && !qk_bf16) {  // bf16-valued Q and K are exact in tf32: no lo terms
             mma_tf32(tS, a_raw, sw128_kmajor_desc(st + 32768u + o), idS, 1u);
             mma_tf32_ts(tS, tmem + kColQlo + 8u * kk, sw128_kmajor_desc(st + o), idS, 1u);
           }
@@ -1154,16 +1169,16 @@ __global__ void __maxnreg__(128)
         const int L = cur.L, nkb = (L + QB - 1) / QB;
         if (!(ok = mbar_wait_abort(&bar[kLQReady], n & 1, status, abort_flag))) break;
         // ---- pass 1: S_j for the row max
-        for (int j = 0; j < nkb && ok; ++j) ok = issue_s(tb + static_cast<uint32_t>(j));
+        for (int j = 0; j < nkb && ok; ++j) ok = issue_s(tb + static_cast<uint32_t>(j), false);
         if (!ok) break;
         // ---- pass 2: S_0, S_1, P.V_0, S_2, P.V_1, ...
         const uint32_t t2 = tb + static_cast<uint32_t>(nkb);
         const uint32_t b0 = ns & 1;  // S buffer of pass 2's S_0
-        if (!(ok = issue_s(t2))) break;
+        if (!(ok = issue_s(t2, true))) break;
         if (nkb == 1) mma_commit(&bar[kLQFree]);
         for (int j = 0; j < nkb && ok; ++j) {
           if (j + 1 < nkb) {
-            if (!(ok = issue_s(t2 + static_cast<uint32_t>(pass2_k(j + 1))))) break;
+            if (!(ok = issue_s(t2 + static_cast<uint32_t>(pass2_k(j + 1)), true))) break;
             if (j + 2 == nkb) mma_commit(&bar[kLQFree]);  // the item's last S
           }
           const uint32_t t = t2 + static_cast<uint32_t>(pass2_v(j, nkb));
@@ -1232,6 +1247,7 @@ __global__ void __maxnreg__(128)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[kLQReady]);
+      float kmax = 0.0f;  // this thread's max|k| over the pass-1 tiles
       for (int i = 0; i < 3 * nkb; ++i) {
         const uint32_t t = tb + static_cast<uint32_t>(i);
         const int s = ring_stage(t);
@@ -1240,8 +1256,27 @@ __global__ void __maxnreg__(128)
         int j = i;
         if (i >= nkb) pass2_tile(i - nkb, nkb, is_v, j);
         const uint32_t raw = smem_u32(smem + kLRing + s * kLStage), lo = raw + 32768u;
-        if (!is_v) {
-          tile_lo_32k(raw, lo, ptid);  // K_j (either pass)
+        if (i < nkb) {
+          // K_j of pass 1: no lo part; max|k| over the sequence's own keys
+          // (rows < L - 128 j) for the error bound, so that the result does
+          // not depend on the next sequence's data.
+          const int kvalid = L - QB * j;
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const uint32_t o = static_cast<uint32_t>((ptid + e * 128) * 16);
+            const float4 x = lds128(raw + o);
+            if (static_cast<int>((o & 16383u) >> 7) < kvalid)
+              kmax = fmaxf(kmax, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+          }
+          if (i == nkb - 1) {
+            kmax = warp_max(kmax);
+            if (lane == 0) {
+              kmax_slot[n & 1][warp - kPrepWarp0] = kmax;
+              mbar_arrive(&bar[kLBound]);  // release: the slot write precedes it
+            }
+          }
+        } else if (!is_v) {
+          tile_lo_32k(raw, lo, ptid);  // K_j of pass 2
         } else {
           // V_j: lo, with keys (rows) past L zeroed in both parts.
           const int kvalid = L - QB * j;
@@ -1316,8 +1351,24 @@ __global__ void __maxnreg__(128)
         release_s(b);
       }
       red[par][row] = mx;
+      // The error bound of the 1xTF32 row max: ||q|| of this row (the item's
+      // Q tile is in shared memory until its last S) and the prep warps'
+      // max|k|.
+      float qn2 = 0.0f;
+#pragma unroll
+      for (int blk = 0; blk < 2; ++blk)
+#pragma unroll
+        for (int c4 = 0; c4 < 8; ++c4) {
+          const float4 x = lds128(smem_u32(smem + kLQ + blk * 16384 + row * 128) +
+                                  static_cast<uint32_t>((c4 ^ (row & 7)) << 4));
+          qn2 = fmaf(x.x, x.x, fmaf(x.y, x.y, fmaf(x.z, x.z, fmaf(x.w, x.w, qn2))));
+        }
+      if (good) good = mbar_wait_abort(&bar[kLBound], n & 1, status, abort_flag);
+      const float kmax = fmaxf(fmaxf(kmax_slot[n & 1][0], kmax_slot[n & 1][1]),
+                               fmaxf(kmax_slot[n & 1][2], kmax_slot[n & 1][3]));
+      const float bound = qk_bf16 ? 0.0f : fminf(0.03125f * sqrtf(qn2) * kmax * 1.0001f, 16.0f);
       if (!soft_all(good)) break;
-      mx = fmaxf(red[0][row], red[1][row]);
+      mx = fmaxf(red[0][row], red[1][row]) + bound;
       soft_sync();
       // ---- pass 2: P chunks (P_hi over S, P_lo into slot c & 1), row sums
       float sum = 0.0f;
