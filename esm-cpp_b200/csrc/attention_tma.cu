@@ -932,32 +932,25 @@ __global__ void __maxnreg__(128)
 
 // ============================================================ long sequences
 // Sequences of more than 256 tokens: items = (sequence, head, 128-row query
-// tile), one CTA each on a persistent grid, keys in blocks of 128.  The
-// softmax keeps the exact form -- the row max over all keys first, then
-// exponentials, sum and P.V -- in two passes over the key blocks:
-//   pass 1  S'_j = Q K_j^T with one tf32 MMA per 8 dh (the raw words, no lo
-//           terms) for a row max m' raised by the bound of its error;
-//   pass 2  S_j in 3xTF32, P = 2^((S - m') log2 e) chunk by chunk into TMEM
-//           as in the short kernel, O += P V_j (3xTF32), row sums summed
-//           over the blocks.
-// O is never rescaled.  m' is an upper bound of the exact row max m, at
-// most 2 B above it: tf32 truncation leaves each of q_i, k_i within 2^-10
-// relative, so |S - S'| <= 2^-9 ||q|| ||k|| (plus the fp32 accumulation,
-// taken care of by a factor 2), ||k|| <= 8 max|k| at dh = 64, hence
-// B = 2^-5 ||q|| max|k| with max|k| over the sequence's keys, capped at 16
-// so that P stays a normal float.  exp(S - m') / sum exp(S - m') equals exp(S - m) / sum
-// exp(S - m); the shift changes results at the rounding level only.  Q and
-// K holding bf16 values (qk_bf16) are exact in tf32: there S' = S, B = 0.
-// Pass 1 needs no lo parts, so the prep warps only scan its K tiles for
-// max|k|.
+// tile), one CTA each on a persistent grid, keys in blocks of 128, one
+// pass: S_j = Q K_j^T (3xTF32), P_j = 2^((S_j - m) log2 e) chunk by chunk
+// into TMEM as in the short kernel, O += P_j V_j (3xTF32), row sums summed
+// over the blocks, O / sum at the end.  The reference point m of a row is
+// the max of its first block, kept while later blocks' maxima stay within
+// 2^8 of P above it; a block whose max exceeds that moves m to the new max
+// and rescales O and the row sum by 2^((m_old - m_new) log2 e) first (after
+// the previous block's P.V is done).  The normalised result is the same
+// function of S as with the global max (the reference's form), at the
+// rounding level; rescaling, rare after the first block, is the only step
+// the max-first form does not have.
 // Two S buffers: S_{j+1} runs on the tensor cores while the softmax warps
-// read or convert S_j.  Pass 2 issues S_0, S_1, P.V_0, S_2, P.V_1, ...; P_lo
+// read or convert S_j: the MMAs go S_0, S_1, P.V_0, S_2, P.V_1, ...; P_lo
 // has two 32-column slots, chunk c reusing slot c & 1 once the P.V that read
 // it last is done.  Tiles flow through a ring of three 64 KB stages (raw |
-// lo, the short kernel's slot layout) in the order the MMAs take them: pass
-// 1's K_0 .. K_{n-1}, then K_0, K_1, V_0, K_2, V_1, ..., V_{n-1}; the prep
-// warps form each tile's lo part and zero V rows past L.  A tile's load and
-// lo take about two S computations, hence three stages.
+// lo, the short kernel's slot layout) in the order the MMAs take them: K_0,
+// K_1, V_0, K_2, V_1, ..., V_{n-1}; the prep warps form each tile's lo part
+// and zero V rows past L.  A tile's load and lo take about two S
+// computations, hence three stages.
 // TMEM: S0 [0,128) S1 [128,256) O [256,384) P_lo [384,448) Q_lo [448,512).
 constexpr uint32_t kLNst = 3;  // ring stages
 constexpr uint32_t kLQ = 0, kLRing = 32768, kLStage = 65536;
@@ -978,7 +971,7 @@ enum : int {
   kLODone = 16,   // the item's P.V done
   kLLoFree = 17,  // [2] the P.V that read P_lo slot s is done
   kLChunk = 19,   // [4] P chunk c written (4 softmax warps)
-  kLBound = 23,   // the item's pass-1 max|k| published (4 prep warps)
+  kLPVDone = 23,  // a key block's P.V done (once per block, all items)
   kLNumBars = 24
 };
 // Ring stage and phase parity of tile t.
@@ -1041,9 +1034,6 @@ __global__ void __maxnreg__(128)
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kLBarOff);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + kLNumBars);
   volatile uint32_t* abort_flag = tslot + 1;
-  // max|k| of the item's pass-1 K tiles, one slot per prep warp, by item
-  // parity (item n + 2's prep starts after item n's softmax has read them).
-  float (*kmax_slot)[4] = reinterpret_cast<float (*)[4]>(tslot + 2);
   pdl_wait();  // cu and the inputs come from earlier work of the stream
   pdl_trigger();
 
@@ -1071,7 +1061,7 @@ __global__ void __maxnreg__(128)
     mbar_init(&bar[kLQFree], 1);
     mbar_init(&bar[kLODone], 1);
     for (int c = 0; c < 4; ++c) mbar_init(&bar[kLChunk + c], 4);
-    mbar_init(&bar[kLBound], 4);
+    mbar_init(&bar[kLPVDone], 1);
     *abort_flag = 0u;
     fence_barrier_init();
   }
@@ -1104,15 +1094,15 @@ __global__ void __maxnreg__(128)
         for (int blk = 0; blk < 2; ++blk)
           tma_load_2d(smem + kLQ + blk * 16384, &tmQ, &bar[kLQFull], cur.h * DH + 32 * blk,
                       cur.s0 + cur.q0);
-        for (int i = 0; i < 3 * nkb; ++i) {
+        for (int i = 0; i < 2 * nkb; ++i) {
           const uint32_t t = tb + static_cast<uint32_t>(i);
           const int s = ring_stage(t);
           // The stage's previous tile, t - kLNst, must be consumed.
           if (t >= kLNst && !(ok = mbar_wait_abort(&bar[kLFree + s], ring_parity(t - kLNst), status, abort_flag)))
             break;
           bool is_v = false;
-          int j = i;
-          if (i >= nkb) pass2_tile(i - nkb, nkb, is_v, j);
+          int j = 0;
+          pass2_tile(i, nkb, is_v, j);
           uint8_t* st = smem + kLRing + s * kLStage;
           mbar_arrive_expect_tx(&bar[kLFull + s], 2 * 16384);
           for (int blk = 0; blk < 2; ++blk)
@@ -1120,7 +1110,7 @@ __global__ void __maxnreg__(128)
                         cur.s0 + QB * j);
         }
         if (!ok) break;
-        tb += 3u * static_cast<uint32_t>(nkb);
+        tb += 2u * static_cast<uint32_t>(nkb);
         QTile nxt;
         const int itn = next_qtile(it + stride, stride, n_items, H, qtiles, cu, nxt);
         if (itn >= n_items) break;
@@ -1139,10 +1129,9 @@ __global__ void __maxnreg__(128)
       const uint32_t idO2 = idesc_tf32_bmn(QB, 2 * DH);
       const uint32_t q_s = smem_u32(smem + kLQ);
 
-      // S = Q_raw K_raw^T + Q_raw K_lo^T + Q_lo K_raw^T (exact) or Q_raw K_raw^T
-      // (pass 1) for the K tile at ring index t into the next S buffer;
-      // returns false on a failed wait.
-      auto issue_s = [&](uint32_t t, bool exact) -> bool {
+      // S = Q_raw K_raw^T + Q_raw K_lo^T + Q_lo K_raw^T for the K tile at
+      // ring index t into the next S buffer; returns false on a failed wait.
+      auto issue_s = [&](uint32_t t) -> bool {
         const int s = ring_stage(t);
         if (!mbar_wait_abort(&bar[kLReady + s], ring_parity(t), status, abort_flag)) return false;
         const uint32_t b = ns & 1;
@@ -1156,7 +1145,7 @@ __global__ void __maxnreg__(128)
           const uint32_t o = static_cast<uint32_t>((kk >> 2) * 16384 + (kk & 3) * 32);
           const uint64_t a_raw = sw128_kmajor_desc(q_s + o);
           mma_tf32(tS, a_raw, sw128_kmajor_desc(st + o), idS, kk > 0 ? 1u : 0u);
-          if (exact && !qk_bf16) {  // bf16-valued Q and K are exact in tf32: no lo terms
+          if (!qk_bf16) {  // bf16-valued Q and K are exact in tf32: no lo terms
             mma_tf32(tS, a_raw, sw128_kmajor_desc(st + 32768u + o), idS, 1u);
             mma_tf32_ts(tS, tmem + kColQlo + 8u * kk, sw128_kmajor_desc(st + o), idS, 1u);
           }
@@ -1168,17 +1157,14 @@ __global__ void __maxnreg__(128)
       while (ok) {
         const int L = cur.L, nkb = (L + QB - 1) / QB;
         if (!(ok = mbar_wait_abort(&bar[kLQReady], n & 1, status, abort_flag))) break;
-        // ---- pass 1: S_j for the row max
-        for (int j = 0; j < nkb && ok; ++j) ok = issue_s(tb + static_cast<uint32_t>(j), false);
-        if (!ok) break;
-        // ---- pass 2: S_0, S_1, P.V_0, S_2, P.V_1, ...
-        const uint32_t t2 = tb + static_cast<uint32_t>(nkb);
-        const uint32_t b0 = ns & 1;  // S buffer of pass 2's S_0
-        if (!(ok = issue_s(t2, true))) break;
+        // ---- S_0, S_1, P.V_0, S_2, P.V_1, ...
+        const uint32_t t2 = tb;
+        const uint32_t b0 = ns & 1;  // S buffer of the item's S_0
+        if (!(ok = issue_s(t2))) break;
         if (nkb == 1) mma_commit(&bar[kLQFree]);
         for (int j = 0; j < nkb && ok; ++j) {
           if (j + 1 < nkb) {
-            if (!(ok = issue_s(t2 + static_cast<uint32_t>(pass2_k(j + 1)), true))) break;
+            if (!(ok = issue_s(t2 + static_cast<uint32_t>(pass2_k(j + 1))))) break;
             if (j + 2 == nkb) mma_commit(&bar[kLQFree]);  // the item's last S
           }
           const uint32_t t = t2 + static_cast<uint32_t>(pass2_v(j, nkb));
@@ -1203,10 +1189,11 @@ __global__ void __maxnreg__(128)
           }
           if (!ok) break;
           mma_commit(&bar[kLFree + s]);
+          mma_commit(&bar[kLPVDone]);
         }
         if (!ok) break;
         mma_commit(&bar[kLODone]);
-        tb += 3u * static_cast<uint32_t>(nkb);
+        tb += 2u * static_cast<uint32_t>(nkb);
         QTile nxt;
         const int itn = next_qtile(it + stride, stride, n_items, H, qtiles, cu, nxt);
         if (itn >= n_items) break;
@@ -1247,36 +1234,16 @@ __global__ void __maxnreg__(128)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[kLQReady]);
-      float kmax = 0.0f;  // this thread's max|k| over the pass-1 tiles
-      for (int i = 0; i < 3 * nkb; ++i) {
+      for (int i = 0; i < 2 * nkb; ++i) {
         const uint32_t t = tb + static_cast<uint32_t>(i);
         const int s = ring_stage(t);
         if (!(ok = mbar_wait_abort(&bar[kLFull + s], ring_parity(t), status, abort_flag))) break;
         bool is_v = false;
-        int j = i;
-        if (i >= nkb) pass2_tile(i - nkb, nkb, is_v, j);
+        int j = 0;
+        pass2_tile(i, nkb, is_v, j);
         const uint32_t raw = smem_u32(smem + kLRing + s * kLStage), lo = raw + 32768u;
-        if (i < nkb) {
-          // K_j of pass 1: no lo part; max|k| over the sequence's own keys
-          // (rows < L - 128 j) for the error bound, so that the result does
-          // not depend on the next sequence's data.
-          const int kvalid = L - QB * j;
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const uint32_t o = static_cast<uint32_t>((ptid + e * 128) * 16);
-            const float4 x = lds128(raw + o);
-            if (static_cast<int>((o & 16383u) >> 7) < kvalid)
-              kmax = fmaxf(kmax, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
-          }
-          if (i == nkb - 1) {
-            kmax = warp_max(kmax);
-            if (lane == 0) {
-              kmax_slot[n & 1][warp - kPrepWarp0] = kmax;
-              mbar_arrive(&bar[kLBound]);  // release: the slot write precedes it
-            }
-          }
-        } else if (!is_v) {
-          tile_lo_32k(raw, lo, ptid);  // K_j of pass 2
+        if (!is_v) {
+          tile_lo_32k(raw, lo, ptid);  // K_j
         } else {
           // V_j: lo, with keys (rows) past L zeroed in both parts.
           const int kvalid = L - QB * j;
@@ -1302,7 +1269,7 @@ __global__ void __maxnreg__(128)
         if (lane == 0) mbar_arrive(&bar[kLReady + s]);
       }
       if (!ok) break;
-      tb += 3u * static_cast<uint32_t>(nkb);
+      tb += 2u * static_cast<uint32_t>(nkb);
       QTile nxt;
       const int itn = next_qtile(it + stride, stride, n_items, H, qtiles, cu, nxt);
       if (itn >= n_items) break;
@@ -1325,6 +1292,7 @@ __global__ void __maxnreg__(128)
     float (*red)[QB] = reinterpret_cast<float (*)[QB]>(smem + kLRed);
     uint32_t ns = 0;       // S computations consumed (S buffer ns & 1)
     uint32_t lo_uses = 0;  // this warp's writes of P_lo slot par (chunks c with c & 1 == par)
+    uint32_t gblk = 0;     // key blocks before this one, all items: kLPVDone completions
     bool good = ok;
     // Waits for S number ns; returns its TMEM address (this warp's lanes).
     auto next_s = [&](uint32_t& b) -> bool {
@@ -1341,43 +1309,54 @@ __global__ void __maxnreg__(128)
     };
     while (true) {
       const int L = cur.L, nkb = (L + QB - 1) / QB;
-      // ---- pass 1: the row max over all keys
-      float mx = -INFINITY;
-      for (int j = 0; j < nkb && good; ++j) {
-        uint32_t b;
-        if (!(good = next_s(b))) break;
-        const int kv = L - QB * j;
-        mx = fmaxf(mx, s_row_max(tmem + 128u * b + lane_off, par, min(QB / KC, (kv + KC - 1) / KC), kv));
-        release_s(b);
-      }
-      red[par][row] = mx;
-      // The error bound of the 1xTF32 row max: ||q|| of this row (the item's
-      // Q tile is in shared memory until its last S) and the prep warps'
-      // max|k|.
-      float qn2 = 0.0f;
-#pragma unroll
-      for (int blk = 0; blk < 2; ++blk)
-#pragma unroll
-        for (int c4 = 0; c4 < 8; ++c4) {
-          const float4 x = lds128(smem_u32(smem + kLQ + blk * 16384 + row * 128) +
-                                  static_cast<uint32_t>((c4 ^ (row & 7)) << 4));
-          qn2 = fmaf(x.x, x.x, fmaf(x.y, x.y, fmaf(x.z, x.z, fmaf(x.w, x.w, qn2))));
+      // ---- one pass over the key blocks: row max of the block, then the
+      // reference point m (and, rarely, a rescale of O and the sum), then P
+      // chunks and row sums.  The two warps of a row exchange their halves
+      // of the block max through `red` at the same points (AND-votes).
+      const float kLog2e = 1.4426950408889634f;
+      float m = -INFINITY, sum = 0.0f;
+      for (int j = 0; j < nkb; ++j) {
+        uint32_t b = 0;
+        const bool w = good && next_s(b);
+        const int kv = L - QB * j, nch = min(QB / KC, (kv + KC - 1) / KC);
+        const uint32_t tS = tmem + 128u * b + lane_off;
+        red[par][row] = w ? s_row_max(tS, par, nch, kv) : -INFINITY;
+        if (!soft_all(w)) {
+          good = false;
+          break;
         }
-      if (good) good = mbar_wait_abort(&bar[kLBound], n & 1, status, abort_flag);
-      const float kmax = fmaxf(fmaxf(kmax_slot[n & 1][0], kmax_slot[n & 1][1]),
-                               fmaxf(kmax_slot[n & 1][2], kmax_slot[n & 1][3]));
-      const float bound = qk_bf16 ? 0.0f : fminf(0.03125f * sqrtf(qn2) * kmax * 1.0001f, 16.0f);
-      if (!soft_all(good)) break;
-      mx = fmaxf(red[0][row], red[1][row]) + bound;
-      soft_sync();
-      // ---- pass 2: P chunks (P_hi over S, P_lo into slot c & 1), row sums
-      float sum = 0.0f;
-      for (int j = 0; j < nkb && good; ++j) {
-        uint32_t b;
-        if (!(good = next_s(b))) break;
-        const int kv = L - QB * j;
-        sum = __fadd_rn(sum, p_chunks(tmem + 128u * b + lane_off, tmem + kColPlo + lane_off, 1u, par,
-                                      min(QB / KC, (kv + KC - 1) / KC), kv, mx,
+        const float mb = fmaxf(red[0][row], red[1][row]);
+        soft_sync();
+        float alpha = 1.0f;
+        if (j == 0) {
+          m = mb;
+        } else if (__fmul_rn(__fsub_rn(mb, m), kLog2e) > 8.0f) {
+          alpha = ex2_ftz(__fmul_rn(__fsub_rn(m, mb), kLog2e));
+          m = mb;
+        }
+        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+          // O holds P.V of blocks 0 .. j-1 against the old m: once the last
+          // of them is done, scale this warp's rows of O (its 32 dh columns of
+          // both halves) and their sums.  P.V of block j is issued only after
+          // this warp's chunks below, which follow the store.
+          if (good) good = mbar_wait_abort(&bar[kLPVDone], (gblk - 1) & 1, status, abort_flag);
+          tc_fence_after();
+          uint32_t o[32], ob[32];
+          tmem_ld32(tmem + kColO + lane_off + 32u * par, o);
+          tmem_ld32(tmem + kColO + 64u + lane_off + 32u * par, ob);
+          tmem_ld_wait();
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            o[jj] = __float_as_uint(__fmul_rn(__uint_as_float(o[jj]), alpha));
+            ob[jj] = __float_as_uint(__fmul_rn(__uint_as_float(ob[jj]), alpha));
+          }
+          tmem_st32(tmem + kColO + lane_off + 32u * par, o);
+          tmem_st32(tmem + kColO + 64u + lane_off + 32u * par, ob);
+          tmem_st_wait();
+          sum = __fmul_rn(sum, alpha);
+        }
+        ++gblk;
+        sum = __fadd_rn(sum, p_chunks(tS, tmem + kColPlo + lane_off, 1u, par, nch, kv, m,
                                       [&](int) {
                                         if (lo_uses > 0 && good)
                                           good = mbar_wait_abort(&bar[kLLoFree + par], (lo_uses - 1) & 1,

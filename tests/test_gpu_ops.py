@@ -204,6 +204,28 @@ def test_attention_isolation_long_sequences(cuda):
     assert np.array_equal(a.cpu().numpy()[:300], b.cpu().numpy()[:300])
 
 
+@pytest.mark.parametrize("late", [1, 3])
+def test_attention_long_late_block_max(cuda, O, late):
+    """The > 256 kernel's reference point starts at the first key block's row
+    max; here key block `late` scores far above block 0 for every query row
+    (keys aligned with the common direction of q), which moves it and
+    rescales O and the row sums mid-sequence.  The result must still match
+    the oracle's max-first softmax."""
+    from esm_b200 import ops
+
+    rng = np.random.default_rng(40 + late)
+    L, H, dh = 600, 2, 64
+    cu = np.array([0, L], np.int32)
+    q = (0.125 * (1.0 + 0.1 * rng.standard_normal((L, H, dh)))).astype(np.float32)
+    k = rng.standard_normal((L, H, dh)).astype(np.float32)
+    v = rng.standard_normal((L, H, dh)).astype(np.float32)
+    # block `late` (keys 128 late ..): scores about 8 * 2 = 16 against about 0 +- 3 elsewhere
+    k[128 * late:128 * late + 40] = np.float32(2.0) + 0.05 * rng.standard_normal((40, H, dh)).astype(np.float32)
+    out = ops.attention_varlen(_t(q, cuda), _t(k, cuda), _t(v, cuda), _t(cu, cuda), H, dh)
+    ops.synchronize()
+    _close(out.cpu().numpy(), O.attention_varlen(q, k, v, cu, H, dh))
+
+
 @pytest.mark.parametrize("L", [64, 600])
 def test_attention_large_scores_finite(cuda, L):
     """Scores of 57600 (q = k = 30): the softmax's row max keeps every
