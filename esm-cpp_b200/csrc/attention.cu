@@ -133,11 +133,11 @@ cudaError_t launch_attention_tma(const float* q, const float* k, const float* v,
 cudaError_t launch_attention_tma_pair(const float* q, const float* k, const float* v,
                                       const int* cu, int B, int H, long T, float* out,
                                       uint32_t* amax, uint32_t* status, int num_sms, bool qk_bf16,
-                                      cudaStream_t s);
+                                      cudaStream_t s, bool wait_late);
 cudaError_t launch_attention_tma_long(const float* q, const float* k, const float* v,
                                       const int* cu, int B, int H, long T, int max_len, float* out,
                                       uint32_t* amax, uint32_t* status, int num_sms, bool qk_bf16,
-                                      cudaStream_t s);
+                                      cudaStream_t s, bool wait_late);
 
 cudaError_t launch_attention_varlen(const float* q, const float* k, const float* v,
                                     const int* cu, int B, int H, int dh, long T, int min_len,
@@ -149,19 +149,25 @@ cudaError_t launch_attention_varlen(const float* q, const float* k, const float*
   // L <= 128, a CTA pair for 129..256, one CTA per (sequence, head, 128-row
   // query tile) above; other head dims: FP32 SIMT.
   if (dh == 64 && status != nullptr) {
+    // A kernel that follows another of these (same inputs, other sequences)
+    // waits for it at its end, not its start (wait_late): it runs in the
+    // earlier kernel's tail and still completes after it.
+    bool after = false;
     if (min_len <= 128) {
       cudaError_t e =
           launch_attention_tma(q, k, v, cu, B, H, T, out, amax, status, num_sms, qk_bf16, s);
       if (e != cudaSuccess) return e;
+      after = true;
     }
     if (max_len > 128 && min_len <= 256) {
-      cudaError_t e =
-          launch_attention_tma_pair(q, k, v, cu, B, H, T, out, amax, status, num_sms, qk_bf16, s);
+      cudaError_t e = launch_attention_tma_pair(q, k, v, cu, B, H, T, out, amax, status, num_sms,
+                                                qk_bf16, s, after);
       if (e != cudaSuccess) return e;
+      after = true;
     }
     if (max_len > 256) {
       cudaError_t e = launch_attention_tma_long(q, k, v, cu, B, H, T, max_len, out, amax, status,
-                                                num_sms, qk_bf16, s);
+                                                num_sms, qk_bf16, s, after);
       if (e != cudaSuccess) return e;
     }
     return cudaSuccess;

@@ -593,7 +593,7 @@ __global__ void __maxnreg__(128)
                               const __grid_constant__ CUtensorMap tmK,
                               const __grid_constant__ CUtensorMap tmV, const int* __restrict__ cu,
                               int H, int n_items, float* __restrict__ out, uint32_t* amax,
-                              uint32_t* status, int qk_bf16) {
+                              uint32_t* status, int qk_bf16, int wait_late) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -601,14 +601,22 @@ __global__ void __maxnreg__(128)
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + kPNumBars);
   volatile uint32_t* abort_flag = tslot + 1;
   uint8_t* vbuf = smem + kPVbuf;
-  pdl_wait();  // cu and the inputs come from earlier work of the stream
+  // wait_late: the previous kernel is another attention kernel of the same
+  // call (disjoint sequences, same inputs), which passed its own wait before
+  // this grid could launch -- q, k, v and cu are complete.  Waiting for it at
+  // the end instead lets these CTAs fill its tail, and this grid still
+  // completes after it, so the next kernel's wait covers both.
+  if (!wait_late) pdl_wait();
   pdl_trigger();
 
   const uint32_t rank = cluster_ctarank();
   const int stride = static_cast<int>(gridDim.x >> 1);
   Item first;
   const int it0 = next_long(static_cast<int>(blockIdx.x >> 1), stride, n_items, H, cu, first);
-  if (it0 >= n_items) return;  // uniform over the pair, before any barrier
+  if (it0 >= n_items) {  // uniform over the pair, before any barrier
+    if (wait_late) pdl_wait();
+    return;
+  }
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const long rs = static_cast<long>(H) * DH;
@@ -928,6 +936,7 @@ __global__ void __maxnreg__(128)
     tc_fence_after();
     tmem_dealloc_pair(tmem, 512);
   }
+  if (wait_late) pdl_wait();
 }
 
 // ============================================================ long sequences
@@ -1027,20 +1036,28 @@ __global__ void __maxnreg__(128)
                               const __grid_constant__ CUtensorMap tmK,
                               const __grid_constant__ CUtensorMap tmV, const int* __restrict__ cu,
                               int H, int qtiles, int n_items, float* __restrict__ out,
-                              uint32_t* amax, uint32_t* status, int qk_bf16) {
+                              uint32_t* amax, uint32_t* status, int qk_bf16, int wait_late) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kLBarOff);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + kLNumBars);
   volatile uint32_t* abort_flag = tslot + 1;
-  pdl_wait();  // cu and the inputs come from earlier work of the stream
+  // wait_late: the previous kernel is another attention kernel of the same
+  // call (disjoint sequences, same inputs), which passed its own wait before
+  // this grid could launch -- q, k, v and cu are complete.  Waiting for it at
+  // the end instead lets these CTAs fill its tail, and this grid still
+  // completes after it, so the next kernel's wait covers both.
+  if (!wait_late) pdl_wait();
   pdl_trigger();
 
   const int stride = gridDim.x;
   QTile first;
   const int it0 = next_qtile(blockIdx.x, stride, n_items, H, qtiles, cu, first);
-  if (it0 >= n_items) return;  // CTA-uniform, before any barrier
+  if (it0 >= n_items) {  // CTA-uniform, before any barrier
+    if (wait_late) pdl_wait();
+    return;
+  }
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const long rs = static_cast<long>(H) * DH;  // token row stride (floats)
@@ -1416,6 +1433,7 @@ __global__ void __maxnreg__(128)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+  if (wait_late) pdl_wait();
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -1482,7 +1500,8 @@ cudaError_t launch_attention_tma(const float* q, const float* k, const float* v,
 cudaError_t launch_attention_tma_pair(const float* q, const float* k, const float* v,
                                       const int* cu, int B, int H, long T, float* out,
                                       uint32_t* amax, uint32_t* status, int num_sms, bool qk_bf16,
-                                      cudaStream_t s) {
+                                      cudaStream_t s,
+                                      bool wait_late) {
   if (B <= 0 || H <= 0 || T <= 0) return cudaSuccess;
   CUtensorMap tmQ, tmK, tmV;
   const long cols = static_cast<long>(H) * DH;
@@ -1517,7 +1536,8 @@ cudaError_t launch_attention_tma_pair(const float* q, const float* k, const floa
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, attention_tma_pair_kernel, tmQ, tmK, tmV, cu, H,
-                            static_cast<int>(n_items), out, amax, status, qk_bf16 ? 1 : 0);
+                            static_cast<int>(n_items), out, amax, status, qk_bf16 ? 1 : 0,
+                            wait_late ? 1 : 0);
 }
 
 // Every sequence of more than 256 tokens: items = (sequence, head, 128-row
@@ -1526,7 +1546,8 @@ cudaError_t launch_attention_tma_pair(const float* q, const float* k, const floa
 cudaError_t launch_attention_tma_long(const float* q, const float* k, const float* v,
                                       const int* cu, int B, int H, long T, int max_len, float* out,
                                       uint32_t* amax, uint32_t* status, int num_sms, bool qk_bf16,
-                                      cudaStream_t s) {
+                                      cudaStream_t s,
+                                      bool wait_late) {
   if (B <= 0 || H <= 0 || T <= 0 || max_len <= LMAX2) return cudaSuccess;
   CUtensorMap tmQ, tmK, tmV;
   const long cols = static_cast<long>(H) * DH;
@@ -1550,7 +1571,7 @@ cudaError_t launch_attention_tma_long(const float* q, const float* k, const floa
   const int grid = static_cast<int>(std::min<long>(n_items, std::max(1, num_sms)));
   return launch_pdl(attention_tma_long_kernel, dim3(grid), dim3(kThreads), kLSmemBytes, s, tmQ, tmK,
                     tmV, cu, H, qtiles, static_cast<int>(n_items), out, amax, status,
-                    qk_bf16 ? 1 : 0);
+                    qk_bf16 ? 1 : 0, wait_late ? 1 : 0);
 }
 
 }  // namespace esmb200
