@@ -97,6 +97,9 @@ struct esmcu_model {
   using EventPair = std::pair<std::string, std::pair<cudaEvent_t, cudaEvent_t>>;
   std::vector<EventPair> pending;  // recorded, not yet read
   std::vector<cudaEvent_t> event_pool;  // reused so timing adds no event creation
+  // One per group of a ForwardScheduled call, recorded behind the group's
+  // logits copy so the host hands each group to the caller as it lands.
+  std::vector<cudaEvent_t> group_done;
   std::vector<std::pair<std::string, float>> prof;
   int launches = 0;
 };
@@ -838,7 +841,13 @@ int run_groups(esmcu_model* m, const std::vector<std::vector<int>>& groups, cons
   cudaStream_t s = m->ctx->stream;
   char* base = m->arena;
   char* hp = m->pinned;
-  for (auto& p : ps) {
+  while (m->group_done.size() < ps.size()) {
+    cudaEvent_t e = nullptr;
+    ESMCU_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    m->group_done.push_back(e);
+  }
+  for (size_t pi = 0; pi < ps.size(); ++pi) {
+    auto& p = ps[pi];
     const size_t n_ids = static_cast<size_t>(p.T) * 4, n_cu = static_cast<size_t>(p.B + 1) * 4;
     std::memcpy(hp + p.off_ids, p.ids.data(), n_ids);
     if (masks_concat) std::memcpy(hp + p.off_masks, p.masks.data(), n_ids);
@@ -861,9 +870,13 @@ int run_groups(esmcu_model* m, const std::vector<std::vector<int>>& groups, cons
     ESMCU_CUDA(cudaMemcpyAsync(hp + p.off_logits, d_logits,
                                static_cast<size_t>(score_rows ? p.B : p.T) * V * 4,
                                cudaMemcpyDeviceToHost, s));
+    ESMCU_CUDA(cudaEventRecord(m->group_done[pi], s));
   }
-  ESMCU_CUDA(cudaStreamSynchronize(s));
-  for (const auto& p : ps) {
+  // Every group is queued; each is copied to the caller's rows as soon as
+  // its logits have landed, while the device runs the later groups.
+  for (size_t pi = 0; pi < ps.size(); ++pi) {
+    const auto& p = ps[pi];
+    ESMCU_CUDA(cudaEventSynchronize(m->group_done[pi]));
     const float* src = reinterpret_cast<const float*>(hp + p.off_logits);
     for (size_t gi = 0; gi < p.group->size(); ++gi) {
       const int idx = (*p.group)[gi];
@@ -932,6 +945,7 @@ int esmcu_model_destroy(esmcu_model* m) {
     cudaEventDestroy(e.second.second);
   }
   for (auto e : m->event_pool) cudaEventDestroy(e);
+  for (auto e : m->group_done) cudaEventDestroy(e);
   if (m->cos_t) cudaFree(m->cos_t);
   if (m->sin_t) cudaFree(m->sin_t);
   if (m->hs_dev) cudaFree(m->hs_dev);
