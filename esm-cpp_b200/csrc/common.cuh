@@ -559,6 +559,26 @@ __device__ __forceinline__ double warp_sum_d(double v) {
 // Non-negative float bit patterns order like the floats, so the absmax of a
 // tensor reduces with an integer atomicMax on the bits (the reference's CAS
 // on float bits, gemm_int8.cpp:464-470, relies on the same fact).
+// Activation quantisation q = clamp(rne(v * inv), -127, 127).  The clamp
+// comes first (the bounds are integers, so clamping before or after rounding
+// gives the same q); adding 1.5 * 2^23 then rounds to the nearest integer,
+// ties to even, in the float adder itself (the ulp there is 1), and the low
+// byte of the sum's bit pattern is q in two's complement (the sum minus the
+// constant's pattern is q itself).  No float-to-int conversion instructions.
+// A NaN clamps to -127, as the reference's AVX-512 conversion (INT_MIN, then
+// the clamp) gives.
+__device__ __forceinline__ uint32_t quant_bits(float v, float inv) {
+  return __float_as_uint(__fadd_rn(fminf(fmaxf(__fmul_rn(v, inv), -127.0f), 127.0f), 12582912.0f));
+}
+__device__ __forceinline__ int quant_int(float v, float inv) {
+  return static_cast<int>(quant_bits(v, inv) - 0x4B400000u);
+}
+// Four columns quantised and packed as int8 (column 0 in the low byte).
+__device__ __forceinline__ uint32_t quant_pack4(float4 y, float inv) {
+  return __byte_perm(__byte_perm(quant_bits(y.x, inv), quant_bits(y.y, inv), 0x0040),
+                     __byte_perm(quant_bits(y.z, inv), quant_bits(y.w, inv), 0x0040), 0x5410);
+}
+
 // amax_publish: block-wide max (all threads call it) -> one atomic into the
 // block's slot.  v >= 0.
 __device__ __forceinline__ void amax_publish(uint32_t* slots, float v) {

@@ -108,16 +108,7 @@ __global__ void __launch_bounds__(kLnThreads)
 #pragma unroll
       for (int i = 0; i < NV4; ++i) {
         const int c = 4 * threadIdx.x + 512 * i;
-        if (c < d) {
-          const int a0 = max(-127, min(127, __float2int_rn(__fmul_rn(v[i].x, inv))));
-          const int a1 = max(-127, min(127, __float2int_rn(__fmul_rn(v[i].y, inv))));
-          const int a2 = max(-127, min(127, __float2int_rn(__fmul_rn(v[i].z, inv))));
-          const int a3 = max(-127, min(127, __float2int_rn(__fmul_rn(v[i].w, inv))));
-          *reinterpret_cast<uint32_t*>(qr + c) = (static_cast<uint32_t>(a0) & 0xffu) |
-                                                 ((static_cast<uint32_t>(a1) & 0xffu) << 8) |
-                                                 ((static_cast<uint32_t>(a2) & 0xffu) << 16) |
-                                                 ((static_cast<uint32_t>(a3) & 0xffu) << 24);
-        }
+        if (c < d) *reinterpret_cast<uint32_t*>(qr + c) = quant_pack4(v[i], inv);
       }
       for (int c = d + threadIdx.x; c < ldq; c += kLnThreads) qr[c] = 0;
     }
@@ -159,11 +150,15 @@ __global__ void layernorm_wide_kernel(const float* __restrict__ x, const float* 
 // The per-tensor W8A8 path only needs LN(x) as int8 with one scale over the
 // whole [rows, d] output, so the fp32 output is never written: phase 1 finds
 // every row's statistics and the absmax of y; after a grid-wide barrier
-// phase 2 recomputes y from x (still in L2) and quantises it.  One warp per
-// row, lane l holding columns 4 l + 128 i (d = 128 NV).
+// phase 2 recomputes y from x (in L2) and quantises it.  One warp per row,
+// lane l holding columns 4 l + 128 i (d = 128 NV).
 
 // Grid-wide barrier for a cooperative launch, used once per launch: `counter`
 // is zero before the launch; the wait is bounded like the mbarrier waits.
+// Each block's thread 0 publishes the block's writes with a fence before its
+// arrival; the acquire load that sees every arrival orders thread 0's later
+// reads after them, and the closing block barrier orders the other threads'
+// reads after thread 0's acquire, so no second fence is needed.
 __device__ __forceinline__ void grid_barrier_once(uint32_t* counter, uint32_t* status) {
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -180,33 +175,28 @@ __device__ __forceinline__ void grid_barrier_once(uint32_t* counter, uint32_t* s
       }
       __nanosleep(64);
     }
-    __threadfence();
   }
   __syncthreads();
 }
 
-// y = fma((x - mean) * inv_std, g, b) on four columns.
-__device__ __forceinline__ float4 ln_y4(float4 v, float meanf, float inv_std, float4 gg, float4 bv) {
-  return make_float4(__fmaf_rn(__fmul_rn(__fsub_rn(v.x, meanf), inv_std), gg.x, bv.x),
-                     __fmaf_rn(__fmul_rn(__fsub_rn(v.y, meanf), inv_std), gg.y, bv.y),
-                     __fmaf_rn(__fmul_rn(__fsub_rn(v.z, meanf), inv_std), gg.z, bv.z),
-                     __fmaf_rn(__fmul_rn(__fsub_rn(v.w, meanf), inv_std), gg.w, bv.w));
+// y = fma((x - mean) * inv_std, g, b) on four columns as two f32x2 pairs
+// (each lane of a packed instruction rounds as the scalar form does).
+__device__ __forceinline__ void ln_y4x2(float4 v, unsigned long long mean2, unsigned long long inv2,
+                                        float4 gg, float4 bv, unsigned long long& y01,
+                                        unsigned long long& y23) {
+  y01 = f2_fma(f2_mul(f2_sub(f2_pack(v.x, v.y), mean2), inv2), f2_pack(gg.x, gg.y), f2_pack(bv.x, bv.y));
+  y23 = f2_fma(f2_mul(f2_sub(f2_pack(v.z, v.w), mean2), inv2), f2_pack(gg.z, gg.w), f2_pack(bv.z, bv.w));
 }
 
-__device__ __forceinline__ uint32_t quant4(float4 y, float inv) {
-  const int a0 = max(-127, min(127, __float2int_rn(__fmul_rn(y.x, inv))));
-  const int a1 = max(-127, min(127, __float2int_rn(__fmul_rn(y.y, inv))));
-  const int a2 = max(-127, min(127, __float2int_rn(__fmul_rn(y.z, inv))));
-  const int a3 = max(-127, min(127, __float2int_rn(__fmul_rn(y.w, inv))));
-  return (static_cast<uint32_t>(a0) & 0xffu) | ((static_cast<uint32_t>(a1) & 0xffu) << 8) |
-         ((static_cast<uint32_t>(a2) & 0xffu) << 16) | ((static_cast<uint32_t>(a3) & 0xffu) << 24);
-}
-
-// 12 warps per block, a row per warp.  Up to d = 2048 (NV <= 16) two blocks
-// share an SM (at most 80 registers: gamma and beta come from shared memory
-// and the statistics take one pass); d = 2560 (ESM-2 3B, NV = 20) holds 80
-// floats of the row per lane and runs one block per SM.
+// 12 warps per block, a row per warp at a time.  Up to d = 2048 (NV <= 16)
+// two blocks share an SM (at most 80 registers); d = 2560 (ESM-2 3B, NV = 20)
+// holds 80 floats of the row per lane and runs one block per SM.  Warp w of
+// block b takes rows w * grid + b, + 12 grid, ...: every block gets a near-
+// equal share of the rows, so the SMs finish each phase together.  Each warp
+// keeps its last row of phase 1 in registers across the grid barrier; phase 2
+// quantises it first and re-reads the others (from L2) most recent first.
 constexpr int kLqThreads = 384;
+constexpr int kLqWarps = kLqThreads / 32;
 
 template <int NV>
 __global__ void __launch_bounds__(kLqThreads, NV <= 16 ? 2 : 1)
@@ -215,8 +205,8 @@ __global__ void __launch_bounds__(kLqThreads, NV <= 16 ? 2 : 1)
                     float2* stats, uint32_t* counter, int8_t* __restrict__ q, long ldq,
                     float* scale_out, uint32_t* status) {
   const int lane = threadIdx.x & 31;
-  const long warp_g = static_cast<long>(blockIdx.x) * (kLqThreads / 32) + (threadIdx.x >> 5);
-  const long nwarps = static_cast<long>(gridDim.x) * (kLqThreads / 32);
+  const long warp_g = static_cast<long>(threadIdx.x >> 5) * gridDim.x + blockIdx.x;
+  const long nwarps = static_cast<long>(gridDim.x) * kLqWarps;
   __shared__ __align__(16) float s_gb[2 * 128 * NV];  // gamma | beta
   for (int i = threadIdx.x; i < d; i += kLqThreads) {
     s_gb[i] = __ldg(g + i);
@@ -238,8 +228,8 @@ __global__ void __launch_bounds__(kLqThreads, NV <= 16 ? 2 : 1)
   // Mean and variance in double in one pass (sum and sum of squares, two
   // partial chains each, one combined warp reduction): var = E[x^2] - mean^2
   // differs from the two-pass double variance by ~1e-12 relative, far below
-  // the float rounding of var that follows.
-  auto stats_row = [&](long r, const float4 (&v)[NV]) {
+  // the float rounding of var that follows.  Returns (mean, inv_std).
+  auto stats_row = [&](const float4 (&v)[NV]) {
     double s0 = 0.0, s1 = 0.0, q0 = 0.0, q1 = 0.0;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
@@ -259,20 +249,27 @@ __global__ void __launch_bounds__(kLqThreads, NV <= 16 ? 2 : 1)
     const double var = fmax(sq / d - mean * mean, 0.0);
     const float inv_std = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(var), eps)));
     const float meanf = static_cast<float>(mean);
+    const unsigned long long mean2 = f2_pack(meanf, meanf), inv2 = f2_pack(inv_std, inv_std);
     float mx = 0.0f;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int c = 4 * lane + 128 * i;
-      const float4 y = ln_y4(v[i], meanf, inv_std, lds128(sg + c * 4u), lds128(sb + c * 4u));
-      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(y.x), fabsf(y.y)), fmaxf(fabsf(y.z), fabsf(y.w))));
+      unsigned long long y01, y23;
+      ln_y4x2(v[i], mean2, inv2, lds128(sg + c * 4u), lds128(sb + c * 4u), y01, y23);
+      float y0, y1, y2, y3;
+      f2_unpack(y01, y0, y1);
+      f2_unpack(y23, y2, y3);
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(y0), fabsf(y1)), fmaxf(fabsf(y2), fabsf(y3))));
     }
-    if (lane == 0) stats[r] = make_float2(meanf, inv_std);
     tmax = fmaxf(tmax, mx);
+    return make_float2(meanf, inv_std);
   };
+  float4 va[NV];  // after the loop: the warp's last row
+  float2 st_last = make_float2(0.0f, 0.0f);
   for (long r = warp_g; r < rows; r += nwarps) {
-    float4 va[NV];
     load_row(r, va);
-    stats_row(r, va);
+    st_last = stats_row(va);
+    if (lane == 0) stats[r] = st_last;
   }
   amax_publish(amax, tmax);
   grid_barrier_once(counter, status);
@@ -291,21 +288,38 @@ __global__ void __launch_bounds__(kLqThreads, NV <= 16 ? 2 : 1)
   }
   __syncthreads();
   const float inv = s_inv;
-  auto quant_row = [&](long r, const float4 (&v)[NV]) {
-    const float2 st = __ldcg(stats + r);
+  // q = rne(y * inv) through the float adder (quant_bits), packed f32x2.
+  // The upper clamp of quant_bits is left out: y is recomputed here exactly
+  // as phase 1 computed it, so |y| <= amax and |y * inv| < 127.5 (the scale
+  // and its reciprocal each round by half an ulp).  The lower clamp stays so
+  // that a NaN still maps to -127.
+  const unsigned long long inv2 = f2_pack(inv, inv), round2 = f2_pack(12582912.0f, 12582912.0f);
+  auto quant_row = [&](long r, float2 st, const float4 (&v)[NV]) {
     int8_t* qr = q + r * ldq;
+    const unsigned long long mean2 = f2_pack(st.x, st.x), is2 = f2_pack(st.y, st.y);
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int c = 4 * lane + 128 * i;
-      const float4 y = ln_y4(v[i], st.x, st.y, lds128(sg + c * 4u), lds128(sb + c * 4u));
-      *reinterpret_cast<uint32_t*>(qr + c) = quant4(y, inv);
+      unsigned long long y01, y23;
+      ln_y4x2(v[i], mean2, is2, lds128(sg + c * 4u), lds128(sb + c * 4u), y01, y23);
+      float t0, t1, t2, t3;
+      f2_unpack(f2_mul(y01, inv2), t0, t1);
+      f2_unpack(f2_mul(y23, inv2), t2, t3);
+      float u0, u1, u2, u3;
+      f2_unpack(f2_add(f2_pack(fmaxf(t0, -127.0f), fmaxf(t1, -127.0f)), round2), u0, u1);
+      f2_unpack(f2_add(f2_pack(fmaxf(t2, -127.0f), fmaxf(t3, -127.0f)), round2), u2, u3);
+      *reinterpret_cast<uint32_t*>(qr + c) =
+          __byte_perm(__byte_perm(__float_as_uint(u0), __float_as_uint(u1), 0x0040),
+                      __byte_perm(__float_as_uint(u2), __float_as_uint(u3), 0x0040), 0x5410);
     }
     for (long c = d + lane; c < ldq; c += 32) qr[c] = 0;
   };
-  for (long r = warp_g; r < rows; r += nwarps) {
-    float4 va[NV];
+  if (warp_g >= rows) return;
+  const long r_last = warp_g + (rows - 1 - warp_g) / nwarps * nwarps;
+  quant_row(r_last, st_last, va);
+  for (long r = r_last - nwarps; r >= warp_g; r -= nwarps) {
     load_row(r, va);
-    quant_row(r, va);
+    quant_row(r, __ldcg(stats + r), va);
   }
 }
 
@@ -326,7 +340,7 @@ cudaError_t launch_lq(const float* x, const float* g, const float* b, float eps,
     if (per_sm <= 0) return cudaErrorNotSupported;
     blocks_per_sm[dev & 63].store(per_sm);
   }
-  const long want = (static_cast<long>(rows) + kLqThreads / 32 - 1) / (kLqThreads / 32);
+  const long want = (static_cast<long>(rows) + kLqWarps - 1) / kLqWarps;
   const int grid = static_cast<int>(std::max(1L, std::min<long>(want, static_cast<long>(per_sm) * sms)));
   // Cooperative (for the grid barrier) and with programmatic dependent
   // launch, so the launch and the gamma / beta loads overlap the previous

@@ -20,10 +20,7 @@ __device__ __forceinline__ float act_scale_from_amax(float amax) {
   return amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
 }
 
-__device__ __forceinline__ int quant1(float x, float inv) {
-  int q = __float2int_rn(__fmul_rn(x, inv));
-  return max(-127, min(127, q));
-}
+__device__ __forceinline__ int quant1(float x, float inv) { return quant_int(x, inv); }
 
 __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
   return (static_cast<uint32_t>(a) & 0xffu) | ((static_cast<uint32_t>(b) & 0xffu) << 8) |
@@ -47,21 +44,22 @@ __global__ void quantize_per_tensor_kernel(const float* __restrict__ x, long ldx
   const float s = act_scale_from_amax(s_amax);
   const float inv = __fdiv_rn(1.0f, s);
   if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = s;
-  const long groups_per_row = ldq / 16;
-  const long total = static_cast<long>(M) * groups_per_row;
+  // 16-byte groups: the launcher keeps M * ldq / 16 below 2^30, so the
+  // row / column split is a 32-bit division.
+  const int groups_per_row = static_cast<int>(ldq / 16);
+  const int total = M * groups_per_row;
   const bool vec = ((ldx & 3) == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
-  for (long g = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; g < total;
-       g += static_cast<long>(gridDim.x) * blockDim.x) {
-    const long m = g / groups_per_row;
-    const int c0 = static_cast<int>(g - m * groups_per_row) * 16;
-    const float* xr = x + m * ldx;
+  for (int g = blockIdx.x * blockDim.x + threadIdx.x; g < total; g += gridDim.x * blockDim.x) {
+    const int m = g / groups_per_row;
+    const int c0 = (g - m * groups_per_row) * 16;
+    const float* xr = x + static_cast<long>(m) * ldx;
     uint32_t w[4];
     if (vec && c0 + 16 <= K) {
+      float4 v[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(xr + c0 + 4 * i));
-        w[i] = pack4(quant1(v.x, inv), quant1(v.y, inv), quant1(v.z, inv), quant1(v.w, inv));
-      }
+      for (int i = 0; i < 4; ++i) v[i] = __ldg(reinterpret_cast<const float4*>(xr + c0 + 4 * i));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) w[i] = quant_pack4(v[i], inv);
     } else {
       int qq[16];
 #pragma unroll
@@ -69,7 +67,7 @@ __global__ void quantize_per_tensor_kernel(const float* __restrict__ x, long ldx
 #pragma unroll
       for (int i = 0; i < 4; ++i) w[i] = pack4(qq[4 * i], qq[4 * i + 1], qq[4 * i + 2], qq[4 * i + 3]);
     }
-    *reinterpret_cast<uint4*>(q + m * ldq + c0) = make_uint4(w[0], w[1], w[2], w[3]);
+    *reinterpret_cast<uint4*>(q + static_cast<long>(m) * ldq + c0) = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 
@@ -160,6 +158,7 @@ cudaError_t launch_quantize_per_tensor(const float* x, long ldx, int M, int K,
   if (M <= 0) return cudaSuccess;
   if ((ldq & 15) || ldq < K || (reinterpret_cast<uintptr_t>(q) & 15)) return cudaErrorInvalidValue;
   const long work = static_cast<long>(M) * (ldq / 16);
+  if (work >= (1l << 30)) return cudaErrorInvalidValue;
   return launch_pdl(quantize_per_tensor_kernel, dim3(grid_for(work, 256)), dim3(256), 0, s, x, ldx,
                     M, K, amax_bits, q, ldq, scale_out);
 }
