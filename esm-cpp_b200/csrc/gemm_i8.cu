@@ -68,12 +68,17 @@ struct Cfg {
   // RoPE epilogue: the tile rows' cos / sin table entries 0..31 (128 rows x
   // 256 bytes), staged once per tile.
   static constexpr int ROPE_BYTES = ROPE ? BM * 256 : 0;
-  // As many stages as the rest of shared memory holds (at most 8).
-  static constexpr int FIT =
-      (kSmemLimit - 1024 - 256 - STAGING_BYTES - COLVEC_BYTES - ROPE_BYTES) / STAGE_BYTES;
+  // As many stages as the rest of shared memory holds (at most 8).  The
+  // tiles start at the first 1024-byte boundary of the dynamic shared memory
+  // (16-byte aligned: up to 1008 bytes of padding); the mbarriers (BAR_BYTES)
+  // sit in that padding when it has room and after the tiles otherwise, so
+  // 1024 bytes cover both.
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int FIT = (kSmemLimit - 1024 - STAGING_BYTES - COLVEC_BYTES - ROPE_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = FIT < 8 ? FIT : 8;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + STAGING_BYTES + COLVEC_BYTES + ROPE_BYTES +
-                              1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int TILE_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + COLVEC_BYTES + ROPE_BYTES;
+  static constexpr int SMEM = TILE_BYTES + 1024;
+  static_assert(2 * STAGES * 8 + 4 * 8 + 4 <= BAR_BYTES, "mbarriers and the TMEM slot fit BAR_BYTES");
 };
 
 struct Params {
@@ -132,8 +137,10 @@ __global__ void __maxnreg__(EW == 16 ? 96 : 168)
   uint8_t* staging = smem + C::STAGES * C::STAGE_BYTES;
   float* colvec = reinterpret_cast<float*>(staging + C::STAGING_BYTES);
   uint8_t* rope_cs = staging + C::STAGING_BYTES + C::COLVEC_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(staging + C::STAGING_BYTES + C::COLVEC_BYTES +
-                                               C::ROPE_BYTES);
+  // The barriers: in the alignment padding when it holds them (the same
+  // place in both CTAs of a pair: same kernel, same shared-memory layout).
+  uint8_t* bar_region = (smem - smem_raw >= C::BAR_BYTES) ? smem_raw : smem + C::TILE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(bar_region);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
