@@ -60,6 +60,45 @@ def test_per_token_quantize_bitexact(cuda, O, M, N, K):
     assert np.array_equal(q.cpu().numpy()[:, :K], q_ref)
 
 
+def _rounding_rows():
+    """Rows whose absmax is 127, so the scale is exactly 1 and q = rne(x):
+    every half-integer tie in [-127.5, 127.5], the bounds, values just off
+    a tie, signed zeros and tiny values."""
+    ties = np.arange(-127, 127, dtype=np.float32) + np.float32(0.5)
+    extra = np.array([127.0, -127.0, 126.6, -126.4, 0.4999999, -0.5000001, 0.0, -0.0, 1e-30, -1e-30,
+                      2.5, -2.5, 3.5, -3.5], np.float32)
+    row = np.concatenate([ties, extra])
+    return np.stack([row, row[::-1].copy(), -row, np.roll(row, 7)]).astype(np.float32)
+
+
+@pytest.mark.parametrize("per_token", [False, True])
+def test_activation_rounding_ties_bounds_and_nan(cuda, O, per_token):
+    """The quantisers round in the float adder (x * inv + 1.5 * 2^23): ties go
+    to even exactly as the reference's conversion, the bounds are kept, and a
+    NaN maps to -127 (the reference's AVX-512 conversion gives INT_MIN, then
+    the clamp)."""
+    from esm_b200 import ACT_PER_TENSOR, ACT_PER_TOKEN, ops
+
+    torch = _torch()
+    A = _rounding_rows()
+    mode = ACT_PER_TOKEN if per_token else ACT_PER_TENSOR
+    q, s = ops.quantize_activations(torch.from_numpy(A).to(cuda), mode)
+    ops.synchronize()
+    q_ref, s_ref = O.quantize_act_per_token(A) if per_token else O.quantize_act_per_tensor(A)
+    assert np.all(s.cpu().numpy() == 1.0) and np.array_equal(s.cpu().numpy(), s_ref)
+    assert np.array_equal(q.cpu().numpy()[:, :A.shape[1]], q_ref)
+    assert np.array_equal(q_ref[0, :254], np.rint(A[0, :254]).astype(np.int8))
+    An = A.copy()
+    An[:, 5] = np.nan
+    qn, sn = ops.quantize_activations(torch.from_numpy(An).to(cuda), mode)
+    ops.synchronize()
+    qn = qn.cpu().numpy()[:, :A.shape[1]]
+    assert np.all(qn[:, 5] == -127)
+    keep = np.arange(A.shape[1]) != 5
+    assert np.array_equal(qn[:, keep], q_ref[:, keep])
+    assert np.all(sn.cpu().numpy() == 1.0)
+
+
 @pytest.mark.parametrize("per_token", [False, True])
 @pytest.mark.parametrize("M,N,K", SHAPES + [(33, 48, 40), (5, 17, 23)])
 def test_linear_int8_matches_oracle(cuda, O, M, N, K, per_token):
